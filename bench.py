@@ -1,0 +1,440 @@
+"""Benchmark of the B200 packed refresh executor (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the north-star target): Llama-3-8B-shaped
+random model in bf16 (32 layers, hidden 4096, 32/8 heads, head_dim 128, MLP
+14336, rope_theta 5e5, vocab 128256, weights N(0, 0.02)), 8192-token context,
+256 tokens deleted at 1024 (edited length N=7936), 64 selected rows in 16
+intervals of 4 at sorted seeded-random, non-adjacent suffix offsets.
+
+A step is one refresh stage through the public API, the reference benchmark's
+scope (benchmarks/benchmark_refresh.py:129-164: output ownership, support
+planning/upload and the layer traversal; prefill, selection and positional
+correction excluded): ``packed_interval_repair(shim, shifted_cache, ids,
+intervals)``. The positional correction (RoPE fix over all 32 layers) is timed
+separately in the same run and reported under ``rope_fix``.
+
+Every step streams 14 GB of weights, far more than the 126 MB L2, so no L2
+flush is needed between steps. Times are CUDA events on the launching stream,
+max over ranks. With N GPUs each rank repairs its own request (different seed,
+no collective on the data path): weak scaling.
+
+``--impl reference`` times the reference algorithm's CPU restatement (oracle/,
+the reference package itself cannot be installed on the GPU box) on all host
+cores on a bounded sample of the same workload, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+CONFIG = dict(name="llama3-8b-shape", layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128,
+              intermediate=14336, vocab=128256, theta=500000.0, context=8192, delete_at=1024, delete=256,
+              intervals=16, rows=64)
+METRIC = "repaired rows/s (packed refresh stage, Llama-3-8B shape, 8192 ctx, 16 intervals, 64 rows)"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            data = json.load(fh)
+        return float(data["hbm_gbs"]), float(data["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def make_intervals(seed: int, suffix_start: int, length: int, count: int, width: int):
+    """Sorted, non-overlapping, non-adjacent intervals at seeded random suffix offsets."""
+    gen = torch.Generator().manual_seed(seed)
+    slots = (length - suffix_start) // (width + 1)
+    picks = sorted(torch.randperm(slots, generator=gen)[:count].tolist())
+    return [(suffix_start + s * (width + 1), suffix_start + s * (width + 1) + width) for s in picks]
+
+
+def build_model(cfg, seed, device):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    config = LlamaConfig(vocab_size=cfg["vocab"], hidden_size=cfg["hidden"], intermediate_size=cfg["intermediate"],
+                         num_hidden_layers=cfg["layers"], num_attention_heads=cfg["heads"],
+                         num_key_value_heads=cfg["kv_heads"], head_dim=cfg["head_dim"], rope_theta=cfg["theta"],
+                         max_position_embeddings=131072, initializer_range=0.02, rms_norm_eps=1e-5)
+    torch.manual_seed(seed)
+    previous = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(device):
+            model = LlamaForCausalLM(config)
+    finally:
+        torch.set_default_dtype(previous)
+    return model.eval()
+
+
+def synthetic_request(cfg, seed, device):
+    """Old ids and a stale old cache (K ~ N(0,1), V ~ N(0,0.5)), edited ids, intervals."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    old_len = cfg["context"]
+    old_ids = torch.randint(0, cfg["vocab"], (1, old_len), device=device, generator=gen)
+    a, b = cfg["delete_at"], cfg["delete_at"] + cfg["delete"]
+    new_ids = torch.cat((old_ids[:, :a], old_ids[:, b:]), dim=1)
+    shape = (1, cfg["kv_heads"], old_len, cfg["head_dim"])
+    pairs = []
+    for _ in range(cfg["layers"]):
+        k = torch.randn(shape, device=device, generator=gen, dtype=torch.float32).to(torch.bfloat16)
+        v = (0.5 * torch.randn(shape, device=device, generator=gen, dtype=torch.float32)).to(torch.bfloat16)
+        pairs.append((k, v))
+    width = cfg["rows"] // cfg["intervals"]
+    intervals = make_intervals(seed, a, new_ids.shape[1], cfg["intervals"], width)
+    return old_ids, new_ids, pairs, intervals
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while a region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._thread = None
+
+    def __enter__(self):
+        def run():
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                         timeout=5).stdout.strip()
+                    if out:
+                        self.samples.append([x.strip() for x in out.split(",")])
+                except (OSError, subprocess.SubprocessError):
+                    return
+                self._stop.wait(0.2)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=6)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        mhz = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": float(self.samples[0][2]) if self.samples[0][2].replace(".", "").isdigit() else None,
+                "samples": len(self.samples), "reasons": reasons}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def rope_fix_bytes(cfg, new_rows, suffix_rows):
+    """Algorithmic bytes: the fused shift kernel reads and writes every kept K
+    and V row; the delta-RoPE part alone is the K suffix read + write."""
+    row = cfg["kv_heads"] * cfg["head_dim"] * 2
+    fused = 2 * 2 * cfg["layers"] * new_rows * row
+    rope = 2 * cfg["layers"] * suffix_rows * row
+    return fused, rope
+
+
+def refresh_bytes(cfg, length):
+    """Per-request algorithmic HBM bytes of the refresh stage: weights once,
+    the ownership copy (read + write of every K/V row), one read of each
+    layer's K/V by attention."""
+    h, i, d = cfg["hidden"], cfg["intermediate"], cfg["head_dim"]
+    q, kv = cfg["heads"] * d, cfg["kv_heads"] * d
+    params = h * q + 2 * h * kv + q * h + 3 * h * i
+    weights = cfg["layers"] * params * 2
+    cache = 2 * cfg["layers"] * cfg["kv_heads"] * length * d * 2
+    return weights + 2 * cache + cache, params
+
+
+def run_cpu_baseline(cfg, sample_layers, threads, seed=0):
+    """Reference algorithm (oracle CPU restatement) on a bounded sample:
+    ``sample_layers`` of the workload's layers, full context and rows; rows/s
+    scaled to the full depth."""
+    from oracle import packed_oracle as oracle
+
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(seed)
+    h, i, d = cfg["hidden"], cfg["intermediate"], cfg["head_dim"]
+    q, kv = cfg["heads"] * d, cfg["kv_heads"] * d
+
+    def w(*shape):
+        return (0.02 * torch.randn(shape, generator=gen)).to(torch.bfloat16)
+
+    layers = [dict(in_norm=torch.ones(h, dtype=torch.bfloat16), q=w(q, h), k=w(kv, h), v=w(kv, h), o=w(h, q),
+                   post_norm=torch.ones(h, dtype=torch.bfloat16), gate=w(i, h), up=w(i, h), down=w(h, i))
+              for _ in range(sample_layers)]
+    model = oracle.OracleModel(embed=w(cfg["vocab"], h), layers=layers, heads=cfg["heads"],
+                               kv_heads=cfg["kv_heads"], head_dim=d, eps=1e-5,
+                               inv_freq=oracle.default_inv_freq(cfg["theta"], d), qk_norm=False)
+    length = cfg["context"] - cfg["delete"]
+    ids = torch.randint(0, cfg["vocab"], (length,), generator=gen)
+    base = [((torch.randn((1, cfg["kv_heads"], length, d), generator=gen)).to(torch.bfloat16),
+             (0.5 * torch.randn((1, cfg["kv_heads"], length, d), generator=gen)).to(torch.bfloat16))
+            for _ in range(sample_layers)]
+    width = cfg["rows"] // cfg["intervals"]
+    intervals = make_intervals(seed, cfg["delete_at"], length, cfg["intervals"], width)
+    positions = [p for a, b in intervals for p in range(a, b)]
+    oracle.packed_refresh(model, base, ids, positions)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.packed_refresh(model, base, ids, positions)
+        reps += 1
+        if time.perf_counter() - t0 > 8.0 or reps >= 5:
+            break
+    per_step = (time.perf_counter() - t0) / reps
+    per_request = per_step * cfg["layers"] / sample_layers
+    return {"value": len(positions) / per_request, "unit": "rows/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_layers} of {cfg['layers']} layers (full context {length}, {len(positions)} rows), "
+                      f"{reps} timed reps, scaled x{cfg['layers'] / sample_layers:g} to full depth",
+            "ms_per_request": per_request * 1e3}
+
+
+def reference_arm(args):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    cfg = dict(CONFIG)
+    base = run_cpu_baseline(cfg, sample_layers=2, threads=threads)
+    line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["ms_per_request"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random weights N(0,0.02), ids, stale cache)",
+            "config": {"workload": "config2: Llama-3-8B shape, 8192 ctx, delete 256@1024, 16x4 rows",
+                       "parallelism": f"dp{world} (rank 0 only)", "l2": "weights 14 GB >> L2"},
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": base["value"], "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def our_arm(args):
+    from budgeted_kv_cache_repair_b200 import OperatorShim, build_halo_cache, packed_interval_repair
+    from budgeted_kv_cache_repair_b200 import _lib, engine
+    from budgeted_kv_cache_repair_b200 import build as native_build
+    from budgeted_kv_cache_repair_b200.validate import cache_layers
+
+    world, rank, local = _dist()
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
+    native_build.build()
+    _lib.load()
+    cfg = dict(CONFIG)
+    seed = 1 + rank
+    model = build_model(cfg, seed, device)
+    shim = OperatorShim(model)
+    old_ids, new_ids, old_pairs, intervals = synthetic_request(cfg, seed, device)
+    from budgeted_kv_cache_repair_b200.cache import make_cache
+
+    old_cache = make_cache(old_pairs)
+    length = new_ids.shape[1]
+    rows = sum(b - a for a, b in intervals)
+    hbm, tflops, peak_src = _peaks()
+    stream = torch.cuda.current_stream()
+
+    # ---- positional correction (RoPE fix, fused shift cache) ----
+    for _ in range(args.warmup):
+        shifted, alignment = build_halo_cache(shim, old_cache, old_ids, new_ids, 0)
+    torch.cuda.synchronize()
+    from budgeted_kv_cache_repair_b200.cache import shift_layers
+
+    rope_ms = []
+    for _ in range(max(args.steps, 5)):
+        begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        begin.record(stream)
+        layers = shift_layers(shim, old_pairs, alignment, alignment["new_suffix_start"], alignment["old_suffix_start"])
+        end.record(stream)
+        end.synchronize()
+        rope_ms.append(begin.elapsed_time(end))
+        del layers
+    fused_bytes, rope_bytes = rope_fix_bytes(cfg, length, alignment["suffix"])
+    rope_t = statistics.median(rope_ms) / 1e3
+
+    # ---- refresh stage through the public API ----
+    ids_dev = new_ids
+    for _ in range(args.warmup):
+        out, receipt = packed_interval_repair(shim, shifted, ids_dev, intervals)
+        del out
+    torch.cuda.synchronize()
+    timer = engine.KernelTimer()
+    step_events = []
+    sampler = ClockSampler(device.index)
+    _barrier(world)
+    torch.cuda.synchronize()
+    launches_before = _lib.load().kvr_kernel_launches()
+    with sampler:
+        region_begin = torch.cuda.Event(enable_timing=True)
+        region_begin.record(stream)
+        engine.set_kernel_timer(timer)
+        for _ in range(args.steps):
+            b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b.record(stream)
+            out, receipt = packed_interval_repair(shim, shifted, ids_dev, intervals)
+            e.record(stream)
+            step_events.append((b, e))
+            del out
+        engine.set_kernel_timer(None)
+        region_end = torch.cuda.Event(enable_timing=True)
+        region_end.record(stream)
+        torch.cuda.synchronize()
+    launches = _lib.load().kvr_kernel_launches() - launches_before
+    _barrier(world)
+    region_ms = region_begin.elapsed_time(region_end)
+    step_ms = [b.elapsed_time(e) for b, e in step_events]
+    region_ms = _max_over_ranks(region_ms, world)
+    ms_per_step = region_ms / args.steps
+    value = world * rows * args.steps / (region_ms / 1e3)
+
+    # ---- e2e: host ids in, refreshed rows of the last layer out ----
+    host_ids = new_ids.cpu().pin_memory()
+    pos_dev = torch.tensor([p for a, b in intervals for p in range(a, b)], device=device)
+    readback = torch.empty((2, cfg["kv_heads"], rows, cfg["head_dim"]), dtype=torch.bfloat16).pin_memory()
+    for _ in range(max(1, args.warmup)):
+        out, _ = packed_interval_repair(shim, shifted, host_ids, intervals)
+    torch.cuda.synchronize()
+    _barrier(world)
+    e_begin = torch.cuda.Event(enable_timing=True)
+    e_begin.record(stream)
+    for _ in range(args.steps):
+        out, _ = packed_interval_repair(shim, shifted, host_ids, intervals)
+        k_last, v_last = cache_layers(out)[-1]
+        sel = torch.stack((k_last[0].index_select(1, pos_dev), v_last[0].index_select(1, pos_dev)))
+        readback.copy_(sel, non_blocking=True)
+        del out
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(e_begin.elapsed_time(e_end), world) / args.steps
+    e2e_value = world * rows / (e2e_ms / 1e3)
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+
+    totals = timer.totals_ms()
+    kernels = {}
+    algo_bytes, params = refresh_bytes(cfg, length)
+    cache_bytes = 2 * cfg["layers"] * cfg["kv_heads"] * length * cfg["head_dim"] * 2
+    if "copy_layers" in totals:
+        n, ms = totals["copy_layers"]
+        gbs = 2 * cache_bytes / (ms / n / 1e3) / 1e9
+        kernels["copy_layers"] = {"launches": n, "avg_us": ms / n * 1e3, "bytes_per_launch": 2 * cache_bytes,
+                                  "achieved_gbs": gbs, "frac_hbm": gbs / hbm, "share_of_step": ms / sum(step_ms)}
+    if "selected_attention" in totals:
+        n, ms = totals["selected_attention"]
+        kv_bytes = 2 * cfg["kv_heads"] * (max(p for a, b in intervals for p in range(a, b)) + 1) * cfg["head_dim"] * 2
+        flops = 4.0 * cfg["heads"] * cfg["head_dim"] * sum(p + 1 for a, b in intervals for p in range(a, b))
+        kernels["selected_attention"] = {
+            "launches": n, "avg_us": ms / n * 1e3, "kv_bytes_per_launch": kv_bytes,
+            "achieved_gbs": kv_bytes / (ms / n / 1e3) / 1e9, "frac_hbm": kv_bytes / (ms / n / 1e3) / 1e9 / hbm,
+            "achieved_tflops": flops / (ms / n / 1e3) / 1e12, "share_of_step": ms / sum(step_ms)}
+    rope_gbs = fused_bytes / rope_t / 1e9
+    clocks = sampler.summary()
+    cpu = run_cpu_baseline(cfg, sample_layers=2, threads=os.cpu_count() or 1) if world == 1 and not args.no_cpu else None
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random weights N(0,0.02), ids, stale cache)",
+        "config": {"workload": "config2: Llama-3-8B shape, 8192 ctx, delete 256@1024 (N=7936), 16 intervals x 4 rows",
+                   "rows": rows, "logical_length": length, "intervals": intervals[:4] + ["..."],
+                   "parallelism": f"dp{world}", "l2": "no flush: 14 GB of weights stream per step (>> 126 MB L2)"},
+        "refresh_ms": {"median": statistics.median(step_ms), "min": min(step_ms), "max": max(step_ms)},
+        "roofline": {"bound": "hbm", "kernel": "kvr_shift_cache_layers (RoPE fix + shift, 32 layers, 1 launch)",
+                     "achieved": rope_gbs, "peak": hbm, "unit": "GB/s", "frac": rope_gbs / hbm,
+                     "traffic": None, "algorithmic_bytes": fused_bytes, "rope_only_bytes": rope_bytes,
+                     "avg_us": rope_t * 1e6, "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"},
+        "step_roofline": {"bound": "hbm", "algorithmic_bytes": algo_bytes,
+                          "achieved_gbs": algo_bytes / (ms_per_step / 1e3) / 1e9,
+                          "frac": algo_bytes / (ms_per_step / 1e3) / 1e9 / hbm,
+                          "floor_ms": algo_bytes / hbm / 1e6},
+        "kernels": kernels,
+        "e2e": {"value": e2e_value, "unit": "rows/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(host_ids.numel() * 8),
+                "d2h_bytes_per_step": int(readback.numel() * 2)},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        our_arm(args)
+
+
+if __name__ == "__main__":
+    main()

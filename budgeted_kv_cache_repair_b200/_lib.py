@@ -1,0 +1,114 @@
+"""ctypes binding of libkvr_b200.so, the C ABI declared in include/kvr_b200.h.
+
+The library is built in-tree (``python -m budgeted_kv_cache_repair_b200.build``)
+and loaded from ``lib/`` next to this file. There is no fallback: every
+product entry point fails loudly when the library is missing.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIBRARY = os.path.join(HERE, "lib", "libkvr_b200.so")
+
+OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT = 0, 1, 2, 3, 4
+DTYPE_BF16, DTYPE_F16 = 0, 1
+MAX_LAYER_TENSORS = 256
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_L = ctypes.c_int64
+_F = ctypes.c_float
+_PP = ctypes.POINTER(ctypes.c_void_p)
+
+# name -> (restype, argtypes); mirrors include/kvr_b200.h one to one.
+SIGNATURES = {
+    "kvr_version": (ctypes.c_char_p, []),
+    "kvr_status_string": (ctypes.c_char_p, [_I]),
+    "kvr_last_cuda_error": (_I, []),
+    "kvr_kernel_launches": (ctypes.c_uint64, []),
+    "kvr_copy_layers": (_I, [_PP, _PP, _I, _I, _L, _I, _L, _L, _L, _L, _I, _P]),
+    "kvr_rope_shift_layers": (_I, [_PP, _PP, _I, _I, _L, _I, _L, _L, _L, _L, _P, _I, _P]),
+    "kvr_shift_cache_layers": (_I, [_PP, _PP, _PP, _PP, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L,
+                                    _P, _I, _I, _P]),
+    "kvr_scatter_rows": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _L, _L, _L, _L, _L, _P, _I, _P]),
+    "kvr_embed_rows": (_I, [_P, _L, _I, _P, _L, _P, _L, _P, _P, _I, _P]),
+    "kvr_add_rmsnorm": (_I, [_P, _P, _P, _P, _L, _I, _L, _L, _L, _F, _I, _P]),
+    "kvr_qkv_rope_scatter": (_I, [_P, _P, _P, _L, _L, _L, _P, _P, _F, _P, _P, _P, _L, _I, _I, _I,
+                                  _P, _P, _P, _L, _L, _L, _P, _I, _P]),
+    "kvr_silu_mul": (_I, [_P, _P, _P, _L, _L, _L, _L, _L, _I, _P]),
+    "kvr_attention_workspace_size": (ctypes.c_size_t, [_L, _I, _I, _I, _L]),
+    "kvr_selected_attention": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _P,
+                                    ctypes.c_size_t, _I, _P]),
+}
+
+_lock = threading.Lock()
+_handle = None
+
+
+class KvrError(RuntimeError):
+    """A native call failed after host-side validation passed."""
+
+
+def library_path() -> str:
+    return LIBRARY
+
+
+def load():
+    """Load the library once; raise if it was not built."""
+    global _handle
+    if _handle is not None:
+        return _handle
+    with _lock:
+        if _handle is None:
+            if not os.path.exists(LIBRARY):
+                raise RuntimeError(
+                    f"{LIBRARY} is missing: build it with `python -m budgeted_kv_cache_repair_b200.build` "
+                    "(the B200 engine has no CPU or eager fallback)")
+            lib = ctypes.CDLL(LIBRARY)
+            for name, (restype, argtypes) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _handle = lib
+    return _handle
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.bfloat16:
+        return DTYPE_BF16
+    if dtype == torch.float16:
+        return DTYPE_F16
+    raise ValueError("the B200 engine computes in bfloat16 or float16")
+
+
+def stream_handle(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr_array(tensors) -> ctypes.Array:
+    arr = (ctypes.c_void_p * len(tensors))()
+    for i, t in enumerate(tensors):
+        arr[i] = t.data_ptr() if isinstance(t, torch.Tensor) else int(t)
+    return arr
+
+
+def check(status: int, what: str) -> None:
+    if status == OK:
+        return
+    lib = load()
+    text = lib.kvr_status_string(status).decode()
+    if status in (ERR_INVALID_ARG, ERR_UNSUPPORTED):
+        raise ValueError(f"{what}: {text}")
+    cuda = lib.kvr_last_cuda_error()
+    raise KvrError(f"{what}: {text} (cudaError {cuda})")
+
+
+def call(name: str, *args) -> None:
+    fn = getattr(load(), name)
+    check(fn(*args), name)

@@ -1,0 +1,425 @@
+// HBM-bound cache kernels: ownership copy, delta-RoPE positional correction,
+// fused shift cache, indexed row scatter and embedding gather.
+//
+// All of them move 16-byte vectors (8 bf16/fp16) with consecutive threads on
+// consecutive addresses. A "segment" is one (tensor, head) plane of rows*D
+// elements; blockIdx.y walks segments and blockIdx.x (grid-stride) walks rows
+// inside a segment, so no per-vector integer division is needed.
+#include <stdio.h>
+
+#include "kvr_common.cuh"
+
+namespace kvr {
+
+namespace {
+thread_local int g_last_cuda_error = 0;
+unsigned long long g_launches = 0;
+}
+
+void set_last_cuda_error(cudaError_t e) { g_last_cuda_error = static_cast<int>(e); }
+void count_launch() { __atomic_add_fetch(&g_launches, 1ull, __ATOMIC_RELAXED); }
+
+// ---------------------------------------------------------------------------
+// Ownership copy (clone_cache, cache.py:31-44).
+// ---------------------------------------------------------------------------
+struct CopyArgs {
+  int heads;
+  int64_t rows;
+  int vecs_per_row;  // head_dim / 8
+  int64_t src_hs, src_rs, dst_hs, dst_rs;  // element strides
+  bool dense;        // rows of both sides are contiguous inside a head
+};
+
+__global__ void __launch_bounds__(256) copy_layers_kernel(LayerPtrs ptrs, CopyArgs a) {
+  const int seg = blockIdx.y;                    // tensor * heads + head
+  const int t = seg / a.heads;
+  const int h = seg - t * a.heads;
+  const uint16_t* src = static_cast<const uint16_t*>(ptrs.src[t]) + h * a.src_hs;
+  uint16_t* dst = static_cast<uint16_t*>(ptrs.dst[t]) + h * a.dst_hs;
+  if (a.dense) {
+    // Whole plane is one contiguous span of rows*D elements on both sides.
+    const int64_t nvec = a.rows * a.vecs_per_row;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; i + 3 * step < nvec; i += 4 * step) {
+      Vec8 v0 = ld_vec8_stream(src + i * 8);
+      Vec8 v1 = ld_vec8_stream(src + (i + step) * 8);
+      Vec8 v2 = ld_vec8_stream(src + (i + 2 * step) * 8);
+      Vec8 v3 = ld_vec8_stream(src + (i + 3 * step) * 8);
+      st_vec8_stream(dst + i * 8, v0);
+      st_vec8_stream(dst + (i + step) * 8, v1);
+      st_vec8_stream(dst + (i + 2 * step) * 8, v2);
+      st_vec8_stream(dst + (i + 3 * step) * 8, v3);
+    }
+    for (; i < nvec; i += step) st_vec8_stream(dst + i * 8, ld_vec8_stream(src + i * 8));
+    return;
+  }
+  const int vpr = a.vecs_per_row;
+  const int64_t nvec = a.rows * vpr;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nvec; i += step) {
+    const int64_t r = i / vpr;
+    const int v = static_cast<int>(i - r * vpr);
+    st_vec8_stream(dst + r * a.dst_rs + v * 8, ld_vec8_stream(src + r * a.src_rs + v * 8));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Delta-RoPE (shifted_suffix_keys, cache.py:47-77). Each thread owns one
+// 8-element vector of the low half of a row and its partner in the high half,
+// so rotate_half needs no data exchange.
+// ---------------------------------------------------------------------------
+struct RopeArgs {
+  int heads;
+  int64_t rows;
+  int64_t src_hs, src_rs, dst_hs, dst_rs;
+};
+
+template <class T, int D>
+__device__ __forceinline__ void rope_pair(const uint16_t* src_row, uint16_t* dst_row, int j,
+                                          const float* cs) {
+  constexpr int H = D / 2;
+  Vec8 lo = ld_vec8_stream(src_row + j * 8);
+  Vec8 hi = ld_vec8_stream(src_row + H + j * 8);
+  Vec8 olo, ohi;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int d = j * 8 + e;
+    const float xl = T::to_f(lo.h[e]);
+    const float xh = T::to_f(hi.h[e]);
+    // d < D/2: rotate_half = -x[d + D/2];  d >= D/2: rotate_half = x[d - D/2].
+    olo.h[e] = rope_elem<T>(xl, -xh, cs[d], cs[D + d]);
+    ohi.h[e] = rope_elem<T>(xh, xl, cs[H + d], cs[D + H + d]);
+  }
+  st_vec8_stream(dst_row + j * 8, olo);
+  st_vec8_stream(dst_row + H + j * 8, ohi);
+}
+
+template <class T, int D>
+__global__ void __launch_bounds__(256) rope_shift_kernel(LayerPtrs ptrs, RopeArgs a,
+                                                         const uint16_t* __restrict__ cos_sin) {
+  __shared__ float cs[2 * D];
+  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) cs[i] = T::to_f(cos_sin[i]);
+  __syncthreads();
+  const int seg = blockIdx.y;
+  const int l = seg / a.heads;
+  const int h = seg - l * a.heads;
+  const uint16_t* src = static_cast<const uint16_t*>(ptrs.src[l]) + h * a.src_hs;
+  uint16_t* dst = static_cast<uint16_t*>(ptrs.dst[l]) + h * a.dst_hs;
+  constexpr int PAIRS = D / 16;  // vector pairs per row
+  const int64_t n = a.rows * PAIRS;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += step) {
+    const int64_t r = i / PAIRS;  // PAIRS is a power of two: shift
+    const int j = static_cast<int>(i & (PAIRS - 1));
+    rope_pair<T, D>(src + r * a.src_rs, dst + r * a.dst_rs, j, cs);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fused shift cache (build_halo_cache, cache.py:103-144, halo 0): prefix rows
+// copied, tail rows moved up by the deleted span with K re-rotated.
+// Segment = (layer, head, component) with component 0 = K, 1 = V.
+// ---------------------------------------------------------------------------
+struct ShiftArgs {
+  int heads;
+  int64_t new_rows, prefix, old_tail, new_tail;
+  int64_t old_hs, old_rs, new_hs, new_rs;
+  int apply_rope;
+};
+
+struct ShiftPtrs {
+  const void* k_old[KVR_MAX_LAYER_TENSORS / 2];
+  const void* v_old[KVR_MAX_LAYER_TENSORS / 2];
+  void* k_new[KVR_MAX_LAYER_TENSORS / 2];
+  void* v_new[KVR_MAX_LAYER_TENSORS / 2];
+};
+
+template <class T, int D>
+__global__ void __launch_bounds__(256) shift_cache_kernel(ShiftPtrs ptrs, ShiftArgs a,
+                                                          const uint16_t* __restrict__ cos_sin) {
+  __shared__ float cs[2 * D];
+  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) cs[i] = T::to_f(cos_sin[i]);
+  __syncthreads();
+  const int seg = blockIdx.y;
+  const int comp = seg & 1;
+  const int lh = seg >> 1;
+  const int l = lh / a.heads;
+  const int h = lh - l * a.heads;
+  const uint16_t* src =
+      static_cast<const uint16_t*>(comp ? ptrs.v_old[l] : ptrs.k_old[l]) + h * a.old_hs;
+  uint16_t* dst = static_cast<uint16_t*>(comp ? ptrs.v_new[l] : ptrs.k_new[l]) + h * a.new_hs;
+  constexpr int PAIRS = D / 16;
+  constexpr int HALF = D / 2;
+  const bool rotate = comp == 0 && a.apply_rope;
+  const int64_t n = a.new_rows * PAIRS;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += step) {
+    const int64_t r = i / PAIRS;
+    const int j = static_cast<int>(i & (PAIRS - 1));
+    int64_t sr;
+    bool tail;
+    if (r < a.prefix) {
+      sr = r;
+      tail = false;
+    } else if (r >= a.new_tail) {
+      sr = r - a.new_tail + a.old_tail;
+      tail = true;
+    } else {
+      continue;  // changed boundary token: recomputed by the caller
+    }
+    const uint16_t* s = src + sr * a.old_rs;
+    uint16_t* d = dst + r * a.new_rs;
+    if (tail && rotate) {
+      rope_pair<T, D>(s, d, j, cs);
+    } else {
+      st_vec8_stream(d + j * 8, ld_vec8_stream(s + j * 8));
+      st_vec8_stream(d + HALF + j * 8, ld_vec8_stream(s + HALF + j * 8));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Bitwise scatter (indexed_kv_scatter_ / index_copy_). One warp-slice of
+// D/8 threads per (head, row); positions read once per row.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) scatter_rows_kernel(
+    const uint16_t* __restrict__ kf, const uint16_t* __restrict__ vf, uint16_t* kc, uint16_t* vc,
+    const int64_t* __restrict__ positions, int64_t rows, int heads, int vpr, int64_t cache_rows,
+    int64_t f_hs, int64_t f_rs, int64_t c_hs, int64_t c_rs, int* error_count) {
+  const int64_t n = static_cast<int64_t>(heads) * rows * vpr;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += step) {
+    const int64_t hr = i / vpr;
+    const int v = static_cast<int>(i - hr * vpr);
+    const int64_t h = hr / rows;
+    const int64_t r = hr - h * rows;
+    const int64_t p = positions[r];
+    if (p < 0 || p >= cache_rows) {
+      if (v == 0 && h == 0 && error_count) atomicAdd(error_count, 1);
+      continue;
+    }
+    const int64_t so = h * f_hs + r * f_rs + v * 8;
+    const int64_t dofs = h * c_hs + p * c_rs + v * 8;
+    st_vec8(kc + dofs, ld_vec8(kf + so));
+    st_vec8(vc + dofs, ld_vec8(vf + so));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Embedding gather of the selected rows.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) embed_rows_kernel(
+    const uint16_t* __restrict__ embed, int64_t vocab, int vpr, const int64_t* __restrict__ ids,
+    int64_t id_count, const int64_t* __restrict__ positions, int64_t rows, uint16_t* out,
+    int* error_count) {
+  const int64_t r = blockIdx.x;
+  if (r >= rows) return;
+  const int64_t p = positions[r];
+  int64_t id = -1;
+  if (p >= 0 && p < id_count) id = ids[p];
+  const bool ok = id >= 0 && id < vocab;
+  if (!ok && threadIdx.x == 0 && error_count) atomicAdd(error_count, 1);
+  uint16_t* o = out + r * static_cast<int64_t>(vpr) * 8;
+  for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
+    Vec8 x;
+    if (ok) {
+      x = ld_vec8(embed + id * static_cast<int64_t>(vpr) * 8 + v * 8);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x.h[e] = 0;
+    }
+    st_vec8(o + v * 8, x);
+  }
+}
+
+}  // namespace kvr
+
+using namespace kvr;
+
+namespace {
+
+bool valid_dtype(int dtype) { return dtype == KVR_DTYPE_BF16 || dtype == KVR_DTYPE_F16; }
+
+int blocks_per_segment(int64_t segment_vecs, int segments, int threads) {
+  // Enough CTAs in total for ~8 resident per SM, never more than the work.
+  int64_t total_target = static_cast<int64_t>(kNumSMs) * 8;
+  int64_t per = (total_target + segments - 1) / segments;
+  int64_t need = (segment_vecs + threads - 1) / threads;
+  if (per > need) per = need;
+  if (per < 1) per = 1;
+  if (per > 65535) per = 65535;
+  return static_cast<int>(per);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* kvr_version(void) { return "kvr_b200 0.1 (sm_100a)"; }
+
+const char* kvr_status_string(int status) {
+  switch (status) {
+    case KVR_OK: return "ok";
+    case KVR_ERR_INVALID_ARG: return "invalid argument";
+    case KVR_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case KVR_ERR_CUDA: return "CUDA error";
+    case KVR_ERR_TIMEOUT: return "bounded device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int kvr_last_cuda_error(void) { return g_last_cuda_error; }
+
+uint64_t kvr_kernel_launches(void) { return __atomic_load_n(&g_launches, __ATOMIC_RELAXED); }
+
+int kvr_copy_layers(const void* const* src, void* const* dst, int num_tensors, int heads,
+                    int64_t rows, int head_dim, int64_t src_head_stride, int64_t src_row_stride,
+                    int64_t dst_head_stride, int64_t dst_row_stride, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return KVR_ERR_UNSUPPORTED;
+  if (!src || !dst || num_tensors < 0 || num_tensors > KVR_MAX_LAYER_TENSORS || heads <= 0 ||
+      rows < 0 || head_dim <= 0 || head_dim % 8)
+    return KVR_ERR_INVALID_ARG;
+  if (src_row_stride % 8 || dst_row_stride % 8 || src_head_stride % 8 || dst_head_stride % 8)
+    return KVR_ERR_INVALID_ARG;
+  if (num_tensors == 0 || rows == 0) return KVR_OK;
+  if (static_cast<int64_t>(num_tensors) * heads > 65535) return KVR_ERR_UNSUPPORTED;
+  LayerPtrs p;
+  for (int t = 0; t < num_tensors; ++t) {
+    if (!src[t] || !dst[t] || !aligned16(src[t]) || !aligned16(dst[t])) return KVR_ERR_INVALID_ARG;
+    p.src[t] = src[t];
+    p.dst[t] = dst[t];
+  }
+  CopyArgs a;
+  a.heads = heads;
+  a.rows = rows;
+  a.vecs_per_row = head_dim / 8;
+  a.src_hs = src_head_stride;
+  a.src_rs = src_row_stride;
+  a.dst_hs = dst_head_stride;
+  a.dst_rs = dst_row_stride;
+  a.dense = src_row_stride == head_dim && dst_row_stride == head_dim;
+  const int segs = num_tensors * heads;
+  dim3 grid(blocks_per_segment(rows * a.vecs_per_row / 4, segs, 256), segs);
+  copy_layers_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p, a);
+  return check_launch();
+}
+
+int kvr_rope_shift_layers(const void* const* src, void* const* dst, int num_layers, int heads,
+                          int64_t rows, int head_dim, int64_t src_head_stride,
+                          int64_t src_row_stride, int64_t dst_head_stride, int64_t dst_row_stride,
+                          const void* cos_sin, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return KVR_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return KVR_ERR_UNSUPPORTED;
+  if (!src || !dst || !cos_sin || num_layers < 0 || num_layers > KVR_MAX_LAYER_TENSORS ||
+      heads <= 0 || rows < 0)
+    return KVR_ERR_INVALID_ARG;
+  if (src_row_stride % 8 || dst_row_stride % 8 || src_head_stride % 8 || dst_head_stride % 8)
+    return KVR_ERR_INVALID_ARG;
+  if (num_layers == 0 || rows == 0) return KVR_OK;
+  if (static_cast<int64_t>(num_layers) * heads > 65535) return KVR_ERR_UNSUPPORTED;
+  LayerPtrs p;
+  for (int l = 0; l < num_layers; ++l) {
+    if (!src[l] || !dst[l] || !aligned16(src[l]) || !aligned16(dst[l])) return KVR_ERR_INVALID_ARG;
+    p.src[l] = src[l];
+    p.dst[l] = dst[l];
+  }
+  RopeArgs a{heads, rows, src_head_stride, src_row_stride, dst_head_stride, dst_row_stride};
+  const int segs = num_layers * heads;
+  const int64_t pairs = rows * (head_dim / 16);
+  dim3 grid(blocks_per_segment(pairs / 2, segs, 256), segs);
+  auto s = static_cast<cudaStream_t>(stream);
+  const uint16_t* cs = static_cast<const uint16_t*>(cos_sin);
+  if (dtype == KVR_DTYPE_BF16) {
+    if (head_dim == 128) rope_shift_kernel<BF16, 128><<<grid, 256, 0, s>>>(p, a, cs);
+    else rope_shift_kernel<BF16, 64><<<grid, 256, 0, s>>>(p, a, cs);
+  } else {
+    if (head_dim == 128) rope_shift_kernel<F16, 128><<<grid, 256, 0, s>>>(p, a, cs);
+    else rope_shift_kernel<F16, 64><<<grid, 256, 0, s>>>(p, a, cs);
+  }
+  return check_launch();
+}
+
+int kvr_shift_cache_layers(const void* const* k_old, const void* const* v_old, void* const* k_new,
+                           void* const* v_new, int num_layers, int heads, int head_dim,
+                           int64_t new_rows, int64_t prefix, int64_t old_tail_start,
+                           int64_t new_tail_start, int64_t old_head_stride, int64_t old_row_stride,
+                           int64_t new_head_stride, int64_t new_row_stride, const void* cos_sin,
+                           int apply_rope, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return KVR_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return KVR_ERR_UNSUPPORTED;
+  if (!k_old || !v_old || !k_new || !v_new || (apply_rope && !cos_sin) || num_layers < 0 ||
+      num_layers > KVR_MAX_LAYER_TENSORS / 2 || heads <= 0 || new_rows < 0 || prefix < 0 ||
+      prefix > new_tail_start || new_tail_start > new_rows || old_tail_start < prefix)
+    return KVR_ERR_INVALID_ARG;
+  if (old_row_stride % 8 || new_row_stride % 8 || old_head_stride % 8 || new_head_stride % 8)
+    return KVR_ERR_INVALID_ARG;
+  if (num_layers == 0 || new_rows == 0) return KVR_OK;
+  if (static_cast<int64_t>(num_layers) * heads * 2 > 65535) return KVR_ERR_UNSUPPORTED;
+  ShiftPtrs p;
+  for (int l = 0; l < num_layers; ++l) {
+    const void* ptrs[4] = {k_old[l], v_old[l], k_new[l], v_new[l]};
+    for (const void* q : ptrs)
+      if (!q || !aligned16(q)) return KVR_ERR_INVALID_ARG;
+    p.k_old[l] = k_old[l];
+    p.v_old[l] = v_old[l];
+    p.k_new[l] = k_new[l];
+    p.v_new[l] = v_new[l];
+  }
+  ShiftArgs a{heads, new_rows, prefix, old_tail_start, new_tail_start,
+              old_head_stride, old_row_stride, new_head_stride, new_row_stride, apply_rope};
+  const int segs = num_layers * heads * 2;
+  const int64_t pairs = new_rows * (head_dim / 16);
+  dim3 grid(blocks_per_segment(pairs / 2, segs, 256), segs);
+  auto s = static_cast<cudaStream_t>(stream);
+  const uint16_t* cs = static_cast<const uint16_t*>(cos_sin);
+  if (dtype == KVR_DTYPE_BF16) {
+    if (head_dim == 128) shift_cache_kernel<BF16, 128><<<grid, 256, 0, s>>>(p, a, cs);
+    else shift_cache_kernel<BF16, 64><<<grid, 256, 0, s>>>(p, a, cs);
+  } else {
+    if (head_dim == 128) shift_cache_kernel<F16, 128><<<grid, 256, 0, s>>>(p, a, cs);
+    else shift_cache_kernel<F16, 64><<<grid, 256, 0, s>>>(p, a, cs);
+  }
+  return check_launch();
+}
+
+int kvr_scatter_rows(const void* k_fresh, const void* v_fresh, void* k_cache, void* v_cache,
+                     const int64_t* positions, int64_t rows, int heads, int head_dim,
+                     int64_t cache_rows, int64_t fresh_head_stride, int64_t fresh_row_stride,
+                     int64_t cache_head_stride, int64_t cache_row_stride, int* error_count,
+                     int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return KVR_ERR_UNSUPPORTED;
+  if (rows < 0 || heads <= 0 || head_dim <= 0 || head_dim % 8 || cache_rows < 0)
+    return KVR_ERR_INVALID_ARG;
+  if (rows == 0) return KVR_OK;
+  if (!k_fresh || !v_fresh || !k_cache || !v_cache || !positions) return KVR_ERR_INVALID_ARG;
+  if (!aligned16(k_fresh) || !aligned16(v_fresh) || !aligned16(k_cache) || !aligned16(v_cache) ||
+      fresh_head_stride % 8 || fresh_row_stride % 8 || cache_head_stride % 8 || cache_row_stride % 8)
+    return KVR_ERR_INVALID_ARG;
+  const int vpr = head_dim / 8;
+  const int64_t n = static_cast<int64_t>(heads) * rows * vpr;
+  scatter_rows_kernel<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(k_fresh), static_cast<const uint16_t*>(v_fresh),
+      static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), positions, rows, heads,
+      vpr, cache_rows, fresh_head_stride, fresh_row_stride, cache_head_stride, cache_row_stride,
+      error_count);
+  return check_launch();
+}
+
+int kvr_embed_rows(const void* embed, int64_t vocab, int hidden, const int64_t* ids,
+                   int64_t id_count, const int64_t* positions, int64_t rows, void* out,
+                   int* error_count, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return KVR_ERR_UNSUPPORTED;
+  if (rows < 0 || hidden <= 0 || hidden % 8 || vocab <= 0 || id_count < 0)
+    return KVR_ERR_INVALID_ARG;
+  if (rows == 0) return KVR_OK;
+  if (!embed || !ids || !positions || !out || !aligned16(embed) || !aligned16(out))
+    return KVR_ERR_INVALID_ARG;
+  if (rows > 0x7fffffff) return KVR_ERR_UNSUPPORTED;
+  embed_rows_kernel<<<static_cast<unsigned>(rows), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(embed), vocab, hidden / 8, ids, id_count, positions, rows,
+      static_cast<uint16_t*>(out), error_count);
+  return check_launch();
+}
+
+}  // extern "C"

@@ -1,0 +1,304 @@
+// Per-layer row kernels of the packed forward: residual add + RMSNorm, the
+// fused K/V epilogue (q/k-norm, RoPE, q packing, K/V scatter into the cache),
+// and the MLP activation. Each reproduces the rounding points of the
+// transformers modules the reference drives (one rounding per torch op).
+#include "kvr_common.cuh"
+
+namespace kvr {
+
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxVecs = 4;  // hidden_size <= 256 * 4 * 8 = 8192
+
+template <class T>
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
+    uint16_t* hidden, const uint16_t* __restrict__ delta, const uint16_t* __restrict__ weight,
+    uint16_t* out, int vpr, int64_t h_stride, int64_t d_stride, int64_t o_stride, float inv_h,
+    float eps) {
+  const int64_t r = blockIdx.x;
+  uint16_t* hrow = hidden + r * h_stride;
+  Vec8 x[kNormMaxVecs];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormMaxVecs; ++k) {
+    const int v = threadIdx.x + k * kNormThreads;
+    if (v < vpr) {
+      x[k] = ld_vec8(hrow + v * 8);
+      if (delta) {
+        // residual + hidden_states, rounded to the element type.
+        Vec8 dv = ld_vec8(delta + r * d_stride + v * 8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[k].h[e] = T::from_f(__fadd_rn(T::to_f(x[k].h[e]), T::to_f(dv.h[e])));
+        st_vec8(hrow + v * 8, x[k]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float f = T::to_f(x[k].h[e]);
+        ss = __fmaf_rn(f, f, ss);
+      }
+    }
+  }
+  // Block reduction of the sum of squares.
+  __shared__ float red[kNormThreads / 32];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < kNormThreads / 32 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(__fadd_rn(red[0] * inv_h, eps));
+#pragma unroll
+  for (int k = 0; k < kNormMaxVecs; ++k) {
+    const int v = threadIdx.x + k * kNormThreads;
+    if (v < vpr) {
+      Vec8 w = ld_vec8(weight + v * 8);
+      Vec8 y;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float normed = rnd<T>(__fmul_rn(T::to_f(x[k].h[e]), inv));
+        y.h[e] = T::from_f(__fmul_rn(T::to_f(w.h[e]), normed));
+      }
+      st_vec8(out + r * o_stride + v * 8, y);
+    }
+  }
+}
+
+// One warp per (row, head slot). Slots [0, q_heads) are query heads (when q_out
+// is given), then kv_heads key heads, then kv_heads value heads. Lane l holds
+// elements [l*E, l*E+E) of the head (E = D/32); its RoPE partner d +- D/2
+// lives in lane l ^ 16.
+struct QkvArgs {
+  const uint16_t* q_in;
+  const uint16_t* k_in;
+  const uint16_t* v_in;
+  int64_t q_rs, k_rs, v_rs;
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
+  float eps;
+  const uint16_t* cos_tab;
+  const uint16_t* sin_tab;
+  const int64_t* positions;
+  int64_t rows;
+  int q_heads, kv_heads;
+  uint16_t* q_out;
+  uint16_t* k_cache;
+  uint16_t* v_cache;
+  int64_t cache_rows, c_hs, c_rs;
+  int* error_count;
+};
+
+template <class T, int D>
+__global__ void __launch_bounds__(256) qkv_rope_scatter_kernel(QkvArgs a) {
+  constexpr int E = D / 32;  // 4 for D=128, 2 for D=64
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int qh = a.q_out ? a.q_heads : 0;
+  const int slots = qh + 2 * a.kv_heads;
+  const int64_t r = warp / slots;
+  if (r >= a.rows) return;
+  const int slot = static_cast<int>(warp - r * slots);
+  const int64_t p = a.positions[r];
+  const bool is_q = slot < qh;
+  const bool is_v = slot >= qh + a.kv_heads;
+  const int head = is_q ? slot : (is_v ? slot - qh - a.kv_heads : slot - qh);
+  if (!is_q && (p < 0 || p >= a.cache_rows)) {
+    if (lane == 0 && head == 0 && !is_v && a.error_count) atomicAdd(a.error_count, 1);
+    return;
+  }
+  const uint16_t* src = is_q ? a.q_in + r * a.q_rs : (is_v ? a.v_in + r * a.v_rs : a.k_in + r * a.k_rs);
+  src += head * D + lane * E;
+  uint16_t* dst = is_q ? a.q_out + (r * a.q_heads + head) * D
+                       : (is_v ? a.v_cache : a.k_cache) + head * a.c_hs + p * a.c_rs;
+  dst += lane * E;
+  uint16_t xb[E];
+  if constexpr (E == 4) {
+    uint2 u = *reinterpret_cast<const uint2*>(src);
+    *reinterpret_cast<uint2*>(xb) = u;
+  } else {
+    uint32_t u = *reinterpret_cast<const uint32_t*>(src);
+    *reinterpret_cast<uint32_t*>(xb) = u;
+  }
+  if (is_v) {  // bitwise copy into the cache row
+    if constexpr (E == 4) *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(xb);
+    else *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(xb);
+    return;
+  }
+  float x[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = T::to_f(xb[e]);
+  const uint16_t* nw = is_q ? a.q_norm : a.k_norm;
+  if (nw) {  // Qwen3 per-head RMSNorm over head_dim
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss = __fmaf_rn(x[e], x[e], ss);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(__fadd_rn(ss * (1.0f / D), a.eps));
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float normed = rnd<T>(__fmul_rn(x[e], inv));
+      x[e] = rnd<T>(__fmul_rn(T::to_f(nw[lane * E + e]), normed));
+    }
+  }
+  // RoPE at the row's absolute position: out = x*cos + rotate_half(x)*sin.
+  const uint16_t* ct = a.cos_tab + r * D + lane * E;
+  const uint16_t* st = a.sin_tab + r * D + lane * E;
+  const bool low = lane < 16;
+  uint16_t ob[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
+    const float rot = low ? -partner : partner;
+    ob[e] = rope_elem<T>(x[e], rot, T::to_f(ct[e]), T::to_f(st[e]));
+  }
+  if constexpr (E == 4) *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(ob);
+  else *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(ob);
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) silu_mul_kernel(const uint16_t* __restrict__ gate,
+                                                       const uint16_t* __restrict__ up,
+                                                       uint16_t* out, int64_t rows, int vpr,
+                                                       int64_t g_rs, int64_t u_rs, int64_t o_rs) {
+  const int64_t n = rows * vpr;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += step) {
+    const int64_t r = i / vpr;
+    const int v = static_cast<int>(i - r * vpr);
+    Vec8 g = ld_vec8(gate + r * g_rs + v * 8);
+    Vec8 u = ld_vec8(up + r * u_rs + v * 8);
+    Vec8 o;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float x = T::to_f(g.h[e]);
+      const float act = rnd<T>(x / (1.0f + expf(-x)));
+      o.h[e] = T::from_f(__fmul_rn(act, T::to_f(u.h[e])));
+    }
+    st_vec8(out + r * o_rs + v * 8, o);
+  }
+}
+
+}  // namespace kvr
+
+using namespace kvr;
+
+extern "C" {
+
+int kvr_add_rmsnorm(void* hidden, const void* delta, const void* weight, void* out, int64_t rows,
+                    int hidden_size, int64_t hidden_stride, int64_t delta_stride,
+                    int64_t out_stride, float eps, int dtype, void* stream) {
+  if (dtype != KVR_DTYPE_BF16 && dtype != KVR_DTYPE_F16) return KVR_ERR_UNSUPPORTED;
+  if (rows < 0 || hidden_size <= 0 || hidden_size % 8) return KVR_ERR_INVALID_ARG;
+  if (hidden_size > kNormThreads * kNormMaxVecs * 8) return KVR_ERR_UNSUPPORTED;
+  if (rows == 0) return KVR_OK;
+  if (rows > 0x7fffffff) return KVR_ERR_UNSUPPORTED;
+  if (!hidden || !weight || !out || !aligned16(hidden) || !aligned16(weight) || !aligned16(out) ||
+      (delta && !aligned16(delta)) || hidden_stride % 8 || out_stride % 8 ||
+      (delta && delta_stride % 8))
+    return KVR_ERR_INVALID_ARG;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int vpr = hidden_size / 8;
+  const float inv_h = 1.0f / static_cast<float>(hidden_size);
+  if (dtype == KVR_DTYPE_BF16)
+    add_rmsnorm_kernel<BF16><<<static_cast<unsigned>(rows), kNormThreads, 0, s>>>(
+        static_cast<uint16_t*>(hidden), static_cast<const uint16_t*>(delta),
+        static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), vpr, hidden_stride,
+        delta_stride, out_stride, inv_h, eps);
+  else
+    add_rmsnorm_kernel<F16><<<static_cast<unsigned>(rows), kNormThreads, 0, s>>>(
+        static_cast<uint16_t*>(hidden), static_cast<const uint16_t*>(delta),
+        static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), vpr, hidden_stride,
+        delta_stride, out_stride, inv_h, eps);
+  return check_launch();
+}
+
+int kvr_qkv_rope_scatter(const void* q_in, const void* k_in, const void* v_in,
+                         int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride,
+                         const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_tab,
+                         const void* sin_tab, const int64_t* positions, int64_t rows, int q_heads,
+                         int kv_heads, int head_dim, void* q_out, void* k_cache, void* v_cache,
+                         int64_t cache_rows, int64_t cache_head_stride, int64_t cache_row_stride,
+                         int* error_count, int dtype, void* stream) {
+  if (dtype != KVR_DTYPE_BF16 && dtype != KVR_DTYPE_F16) return KVR_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return KVR_ERR_UNSUPPORTED;
+  if (rows < 0 || q_heads <= 0 || kv_heads <= 0 || cache_rows < 0) return KVR_ERR_INVALID_ARG;
+  if (rows == 0) return KVR_OK;
+  if (!k_in || !v_in || !cos_tab || !sin_tab || !positions || !k_cache || !v_cache ||
+      (q_out && !q_in))
+    return KVR_ERR_INVALID_ARG;
+  // Lanes move 4/8-byte slices of a head: require 8-byte alignment of every base/stride.
+  const void* ptrs[] = {q_in, k_in, v_in, q_out, k_cache, v_cache, cos_tab, sin_tab};
+  for (const void* p : ptrs)
+    if (p && (reinterpret_cast<uintptr_t>(p) & 7u)) return KVR_ERR_INVALID_ARG;
+  if (q_row_stride % 4 || k_row_stride % 4 || v_row_stride % 4 || cache_head_stride % 4 ||
+      cache_row_stride % 4)
+    return KVR_ERR_INVALID_ARG;
+  QkvArgs a;
+  a.q_in = static_cast<const uint16_t*>(q_in);
+  a.k_in = static_cast<const uint16_t*>(k_in);
+  a.v_in = static_cast<const uint16_t*>(v_in);
+  a.q_rs = q_row_stride;
+  a.k_rs = k_row_stride;
+  a.v_rs = v_row_stride;
+  a.q_norm = static_cast<const uint16_t*>(q_norm_w);
+  a.k_norm = static_cast<const uint16_t*>(k_norm_w);
+  a.eps = eps;
+  a.cos_tab = static_cast<const uint16_t*>(cos_tab);
+  a.sin_tab = static_cast<const uint16_t*>(sin_tab);
+  a.positions = positions;
+  a.rows = rows;
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  a.q_out = static_cast<uint16_t*>(q_out);
+  a.k_cache = static_cast<uint16_t*>(k_cache);
+  a.v_cache = static_cast<uint16_t*>(v_cache);
+  a.cache_rows = cache_rows;
+  a.c_hs = cache_head_stride;
+  a.c_rs = cache_row_stride;
+  a.error_count = error_count;
+  const int slots = (q_out ? q_heads : 0) + 2 * kv_heads;
+  const int64_t warps = rows * slots;
+  const int64_t blocks = (warps + 7) / 8;
+  if (blocks > 0x7fffffff) return KVR_ERR_UNSUPPORTED;
+  auto s = static_cast<cudaStream_t>(stream);
+  if (dtype == KVR_DTYPE_BF16) {
+    if (head_dim == 128) qkv_rope_scatter_kernel<BF16, 128><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+    else qkv_rope_scatter_kernel<BF16, 64><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+  } else {
+    if (head_dim == 128) qkv_rope_scatter_kernel<F16, 128><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+    else qkv_rope_scatter_kernel<F16, 64><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+  }
+  return check_launch();
+}
+
+int kvr_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int64_t width,
+                 int64_t gate_stride, int64_t up_stride, int64_t out_stride, int dtype,
+                 void* stream) {
+  if (dtype != KVR_DTYPE_BF16 && dtype != KVR_DTYPE_F16) return KVR_ERR_UNSUPPORTED;
+  if (rows < 0 || width <= 0 || width % 8) return KVR_ERR_INVALID_ARG;
+  if (rows == 0) return KVR_OK;
+  if (!gate || !up || !out || !aligned16(gate) || !aligned16(up) || !aligned16(out) ||
+      gate_stride % 8 || up_stride % 8 || out_stride % 8)
+    return KVR_ERR_INVALID_ARG;
+  if (width / 8 > 0x7fffffff) return KVR_ERR_UNSUPPORTED;
+  const int vpr = static_cast<int>(width / 8);
+  auto s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(rows * vpr, 256);
+  if (dtype == KVR_DTYPE_BF16)
+    silu_mul_kernel<BF16><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(gate),
+                                                static_cast<const uint16_t*>(up),
+                                                static_cast<uint16_t*>(out), rows, vpr, gate_stride,
+                                                up_stride, out_stride);
+  else
+    silu_mul_kernel<F16><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(gate),
+                                               static_cast<const uint16_t*>(up),
+                                               static_cast<uint16_t*>(out), rows, vpr, gate_stride,
+                                               up_stride, out_stride);
+  return check_launch();
+}
+
+}  // extern "C"

@@ -1,0 +1,146 @@
+"""Packed selected-row refresh on the B200 (drop-in for the reference's
+``packed_interval_repair``, kernels/packed_cache.py:225-298).
+
+Same signature, validation order, error types, receipt keys and ownership
+contract; the native decoder forward with per-layer ``index_copy_`` and masked
+SDPA is replaced by ``engine.refresh_rows`` over an owned copy made by one
+multi-layer copy kernel.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Sequence
+
+import torch
+
+from . import _lib
+from .cache import copy_layers, make_cache
+from .engine import model_view, refresh_rows
+from .plan import IndexedPlan
+from .validate import qualify_model, validate_cache, validate_intervals
+
+# The reference's default backend names select this engine's kernels, so a
+# call with default arguments (api.py:235) lands here. The reference's
+# experimental Triton and Flex paths are not built: one attention path, no
+# multi-backend dispatch.
+ATTENTION_BACKENDS = ("sdpa", "sm100a")
+WRITEBACK_BACKENDS = ("torch", "sm100a")
+ENGINE = "kvr_b200/sm_100a"
+
+
+def make_receipt(intervals, length: int, layer_count: int, attention_backend: str = "sdpa",
+                 writeback_backend: str = "torch") -> dict[str, Any]:
+    """The reference's receipt keys (kernels/packed_cache.py:259-273) plus ``engine``."""
+    selected = [p for start, end in intervals for p in range(start, end)]
+    return {
+        "executor": "packed_interval_repair",
+        "schedule": "packed_selected_rows_layer_major",
+        "attention_backend": attention_backend,
+        "writeback_backend": writeback_backend,
+        "interval_count": len(intervals),
+        "recomputed_tokens": len(selected),
+        "logical_length": length,
+        "layer_count": layer_count,
+        "base_cache_ownership": "borrowed_immutable",
+        "output_cache_ownership": "independent" if selected else "borrowed_base",
+        "selected_absolute_positions": selected,
+        "native_model_mutated": False,
+        "numerical_contract": "separate_schedule_qualification_required",
+        "engine": ENGINE,
+    }
+
+
+def _check_ids(edited_ids_t) -> int:
+    if not isinstance(edited_ids_t, torch.Tensor) or edited_ids_t.ndim != 2 or edited_ids_t.shape[0] != 1:
+        raise ValueError("edited_ids_t must be a single-batch rank-two tensor")
+    if edited_ids_t.dtype not in (torch.int32, torch.int64):
+        raise ValueError("edited_ids_t must contain int32 or int64 IDs")
+    return int(edited_ids_t.shape[1])
+
+
+def _device_ids(edited_ids_t: torch.Tensor, device: torch.device) -> torch.Tensor:
+    ids = edited_ids_t[0]
+    if ids.device != device:
+        if ids.device.type == "cpu" and not ids.is_pinned():
+            ids = ids.pin_memory()
+        ids = ids.to(device, non_blocking=True)
+    if ids.dtype != torch.int64:
+        ids = ids.to(torch.int64)
+    return ids.contiguous()
+
+
+def _base_and_dtype(shim, layers, device):
+    model = shim.generator
+    base = shim._base_transformer(model)
+    dtype = layers[0][0].dtype
+    if dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("the B200 packed executor computes in bfloat16 or float16")
+    qualify_model(model, base, len(layers), device, dtype)
+    return base
+
+
+def refresh_owned_layers(shim: Any, layers, edited_ids_t: torch.Tensor, intervals, plan: IndexedPlan | None = None):
+    """Refresh ``intervals`` in place in caller-owned layer tensors (no copy, no receipt)."""
+    length = _check_ids(edited_ids_t)
+    intervals = validate_intervals(intervals, length)
+    selected = tuple(p for start, end in intervals for p in range(start, end))
+    if not selected:
+        return
+    device = layers[0][0].device
+    if device.type != "cuda":
+        raise ValueError("the B200 packed executor requires CUDA tensors")
+    base = _base_and_dtype(shim, layers, device)
+    host_plan = plan if plan is not None else IndexedPlan(selected, length)
+    device_plan = host_plan.to(device)
+    with torch.cuda.device(device):
+        ids = _device_ids(edited_ids_t, device)
+        refresh_rows(model_view(base), layers, ids, device_plan.positions, host_plan.max_position, length)
+
+
+@torch.no_grad()
+def packed_interval_repair(
+    shim: Any, base_cache: Any, edited_ids_t: torch.Tensor,
+    intervals: Sequence[tuple[int, int]], *,
+    attention_backend: str = "sdpa", writeback_backend: str = "torch",
+    plan: Any = None,
+) -> tuple[Any, dict[str, Any]]:
+    """Recompute sorted selected rows in one layer-major pass on the B200.
+
+    ``plan`` optionally supplies a reusable host ``IndexedPlan`` for exactly
+    these intervals and this logical length. Returns ``(cache, receipt)``:
+    a new ``DynamicCache`` owning its storage, bit-identical to ``base_cache``
+    outside the selected rows, or ``base_cache`` itself for an empty support.
+    ``base_cache`` is never modified, including on failure.
+    """
+    if attention_backend not in ATTENTION_BACKENDS:
+        raise ValueError("attention_backend must be 'sdpa' (default) or 'sm100a'; "
+                         "the Triton/Flex prototypes are not part of the B200 engine")
+    if writeback_backend not in WRITEBACK_BACKENDS:
+        raise ValueError("writeback_backend must be 'torch' (default) or 'sm100a'")
+    length = _check_ids(edited_ids_t)
+    layers = validate_cache(base_cache, length)
+    intervals = validate_intervals(intervals, length)
+    selected = tuple(p for start, end in intervals for p in range(start, end))
+    if plan is not None:
+        if not isinstance(plan, IndexedPlan) or tuple(plan.positions) != selected or plan.logical_length != length:
+            raise ValueError("supplied IndexedPlan must match exact selected positions and cache length")
+    receipt = make_receipt(intervals, length, len(layers), attention_backend, writeback_backend)
+    if not selected:
+        return base_cache, receipt
+    device = layers[0][0].device
+    if device.type != "cuda" or edited_ids_t.device.type not in ("cpu", "cuda"):
+        raise ValueError("the B200 packed executor requires a CUDA cache (there is no CPU path)")
+    if any(k.device != device or v.device != device for k, v in layers):
+        raise ValueError("packed executor requires all cache layers on the request device")
+    base = _base_and_dtype(shim, layers, device)
+    view = model_view(base)
+    if layers[0][0].shape[1] != view.kv_heads or layers[0][0].shape[3] != view.head_dim:
+        raise ValueError("cache head geometry does not match the model")
+    _lib.load()
+    host_plan = plan if plan is not None else IndexedPlan(selected, length)
+    with torch.cuda.device(device):
+        device_plan = host_plan.to(device)
+        ids = _device_ids(edited_ids_t, device)
+        owned = copy_layers(layers)                      # kernels/packed_cache.py:287
+        refresh_rows(view, owned, ids, device_plan.positions, host_plan.max_position, length)
+    return make_cache(owned), receipt

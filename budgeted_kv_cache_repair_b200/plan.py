@@ -1,0 +1,143 @@
+"""Host and device plans for the selected rows of one request.
+
+Mirrors ``IndexedPlan`` / ``DeviceIndexedPlan`` of the reference
+(kernels/indexed_attention.py:42-158): the same constructor, fields, tile
+metadata (BLOCK_M=16 query rows, BLOCK_N=64 keys: ``full_prefix_tiles`` key
+tiles visible to every row of a query tile, ``total_tiles`` tiles reaching its
+last row), validation messages and sealing against mutation. The sm_100a
+attention kernel tiles differently (64 packed (row, head) entries per CTA) and
+derives its own bounds on the device from ``positions``; the tile fields stay
+for callers that read them.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from numbers import Integral
+from typing import Sequence
+
+import torch
+
+BLOCK_M = 16
+BLOCK_N = 64
+
+
+@dataclass(frozen=True)
+class IndexedPlan:
+    """Sorted absolute positions, validated entirely on the CPU.
+
+    Tensor positions are rejected: creating a plan never hides a device-to-host
+    synchronisation (kernels/indexed_attention.py:44-49).
+    """
+
+    positions: Sequence[int]
+    logical_length: int
+    full_prefix_tiles: tuple[int, ...] = field(init=False)
+    total_tiles: tuple[int, ...] = field(init=False)
+
+    def __post_init__(self):
+        if isinstance(self.logical_length, bool) or not isinstance(self.logical_length, Integral):
+            raise ValueError("logical_length must be a host integer")
+        length = int(self.logical_length)
+        if length < 0 or length > (1 << 63) - 1:
+            raise ValueError("logical_length must fit nonnegative signed int64")
+        if isinstance(self.positions, torch.Tensor):
+            raise ValueError("positions must be host integers, not a tensor")
+        try:
+            original = tuple(self.positions)
+        except TypeError as error:
+            raise ValueError("positions must be a sequence of host integers") from error
+        if any(isinstance(p, bool) or not isinstance(p, Integral) for p in original):
+            raise ValueError("positions must contain host integers")
+        positions = tuple(int(p) for p in original)
+        if any(p < 0 or p >= length for p in positions):
+            raise ValueError("positions must lie within logical_length")
+        if any(a >= b for a, b in zip(positions, positions[1:])):
+            raise ValueError("positions must be strictly increasing and unique")
+        full, total = [], []
+        for row in range(0, len(positions), BLOCK_M):
+            tile = positions[row:row + BLOCK_M]
+            full.append((tile[0] + 1) // BLOCK_N)
+            total.append((tile[-1] + BLOCK_N) // BLOCK_N)
+        object.__setattr__(self, "positions", positions)
+        object.__setattr__(self, "logical_length", length)
+        object.__setattr__(self, "full_prefix_tiles", tuple(full))
+        object.__setattr__(self, "total_tiles", tuple(total))
+
+    @property
+    def selected_count(self) -> int:
+        return len(self.positions)
+
+    @property
+    def max_position(self) -> int:
+        return self.positions[-1] if self.positions else -1
+
+    def to(self, device) -> "DeviceIndexedPlan":
+        """Upload O(B) metadata on the caller's current stream for this device."""
+        if isinstance(device, int):
+            device = torch.device("cuda", device)
+        else:
+            device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("device plan requires a CUDA device")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        with torch.cuda.device(device), torch.inference_mode(False):
+            host = torch.tensor(
+                [*self.positions, *self.full_prefix_tiles, *self.total_tiles], dtype=torch.int64
+            ).pin_memory()
+            packed = host.to(device, non_blocking=True)
+            count, tiles = len(self.positions), len(self.full_prefix_tiles)
+            positions = packed[:count]
+            full = packed[count:count + tiles]
+            total = packed[count + tiles:]
+        tensors = (positions, full, total)
+        seal = (id(self), tuple(id(t) for t in tensors), tuple(t._version for t in tensors))
+        # Keep the pinned staging buffer alive until the copy has run.
+        return DeviceIndexedPlan(self, positions, full, total, seal, host)
+
+
+@dataclass(frozen=True)
+class DeviceIndexedPlan:
+    """Device metadata from IndexedPlan.to; tensors are immutable by contract
+    (kernels/indexed_attention.py:113-139)."""
+
+    host_plan: IndexedPlan
+    positions: torch.Tensor
+    full_prefix_tiles: torch.Tensor
+    total_tiles: torch.Tensor
+    _seal: tuple | None = field(default=None, repr=False, compare=False)
+    _staging: torch.Tensor | None = field(default=None, repr=False, compare=False)
+
+    @property
+    def logical_length(self) -> int:
+        return self.host_plan.logical_length
+
+    @property
+    def selected_count(self) -> int:
+        return self.host_plan.selected_count
+
+    @property
+    def device(self) -> torch.device:
+        return self.positions.device
+
+
+def validate_device_plan(plan, device: torch.device) -> None:
+    """Reject plans that were replaced, mutated or not factory-made
+    (kernels/indexed_attention.py:142-158)."""
+    if not isinstance(plan, DeviceIndexedPlan) or not isinstance(plan.host_plan, IndexedPlan):
+        raise ValueError("device_plan must be produced by IndexedPlan.to")
+    tiles = (plan.selected_count + BLOCK_M - 1) // BLOCK_M
+    for tensor, count in ((plan.positions, plan.selected_count),
+                          (plan.full_prefix_tiles, tiles), (plan.total_tiles, tiles)):
+        if (not isinstance(tensor, torch.Tensor) or tensor.device != device
+                or not tensor.is_cuda or tensor.dtype != torch.int64
+                or tensor.shape != (count,) or not tensor.is_contiguous()):
+            raise ValueError("device plan has incompatible metadata shape, dtype, or device")
+    tensors = (plan.positions, plan.full_prefix_tiles, plan.total_tiles)
+    try:
+        seal = (id(plan.host_plan), tuple(id(t) for t in tensors), tuple(t._version for t in tensors))
+    except RuntimeError as error:
+        raise ValueError("device plan must be produced by IndexedPlan.to") from error
+    if plan._seal != seal:
+        raise ValueError("device plan metadata was replaced, mutated, or not factory-created")

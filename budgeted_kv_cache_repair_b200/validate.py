@@ -1,0 +1,154 @@
+"""Contract checks shared by the packed executor and the cache operators.
+
+Each check raises ``ValueError`` before any device work, with the reference's
+rules (kernels/executor.py:19-70, kernels/packed_cache.py:123-163,
+api.py:135-166, kernels/writeback.py:6-15).
+"""
+
+from __future__ import annotations
+
+from numbers import Integral
+from typing import Any, Sequence
+
+import torch
+
+
+def cache_layers(cache: Any) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """``(K, V)`` of every layer of a transformers Cache (4.57 or 5.x) or a
+    sequence of pairs, without copying."""
+    layers = getattr(cache, "layers", None)
+    if layers is not None and all(hasattr(layer, "keys") and hasattr(layer, "values") for layer in layers):
+        return [(layer.keys, layer.values) for layer in layers]
+    try:
+        count = len(cache)
+    except TypeError as exc:
+        raise ValueError("base_cache must expose indexed K/V layers") from exc
+    out = []
+    for index in range(count):
+        try:
+            key, value = cache[index][:2]
+        except (TypeError, ValueError, IndexError) as exc:
+            raise ValueError(f"cache layer {index} must contain one K/V pair") from exc
+        out.append((key, value))
+    return out
+
+
+def validate_cache(cache: Any, logical_length: int) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """Rank-4 ``[1, Hkv, N, D]`` floating K/V, identical geometry on every layer
+    (kernels/executor.py:19-47). Returns the layer pairs."""
+    layers = cache_layers(cache)
+    if not layers:
+        raise ValueError("base_cache must contain at least one K/V layer")
+    expected_shape = expected_dtype = None
+    for index, (key, value) in enumerate(layers):
+        if not isinstance(key, torch.Tensor) or not isinstance(value, torch.Tensor):
+            raise ValueError(f"cache layer {index} K/V must be tensors")
+        if key.ndim != 4 or value.ndim != 4:
+            raise ValueError(f"cache layer {index} K/V must have rank four")
+        if key.shape != value.shape or key.dtype != value.dtype or key.device != value.device:
+            raise ValueError(f"cache layer {index} K/V geometry, dtype, and device must agree")
+        if key.shape[0] != 1 or key.shape[2] != logical_length:
+            raise ValueError(f"cache layer {index} must match the single-batch edited token length")
+        if key.shape[1] <= 0 or key.shape[3] <= 0 or not key.is_floating_point():
+            raise ValueError(f"cache layer {index} requires nonempty floating-point KV heads")
+        if expected_shape is None:
+            expected_shape, expected_dtype = key.shape, key.dtype
+        elif key.shape != expected_shape or key.dtype != expected_dtype:
+            raise ValueError("cache layers must have regular shapes and matching dtypes")
+    return layers
+
+
+def validate_intervals(intervals: Sequence[tuple[int, int]], logical_length: int) -> tuple[tuple[int, int], ...]:
+    """Sorted, disjoint, maximal (non-adjacent) half-open ranges (kernels/executor.py:50-70)."""
+    if not isinstance(intervals, (list, tuple)):
+        raise ValueError("intervals must be a list or tuple of maximal half-open ranges")
+    result = []
+    previous_end = -1
+    for interval in intervals:
+        if not isinstance(interval, (tuple, list)) or len(interval) != 2:
+            raise ValueError("each interval must contain exactly a start and end")
+        if any(isinstance(v, bool) or not isinstance(v, Integral) for v in interval):
+            raise ValueError("interval bounds must be integers, not booleans")
+        start, end = int(interval[0]), int(interval[1])
+        if not 0 <= start < end <= logical_length:
+            raise ValueError("interval bounds must satisfy 0 <= start < end <= token length")
+        if start <= previous_end:
+            raise ValueError("intervals must be sorted, disjoint, and maximal (no adjacent ranges)")
+        result.append((start, end))
+        previous_end = end
+    return tuple(result)
+
+
+def nonoverlapping_layout(tensor: torch.Tensor) -> bool:
+    """Sufficient proof that no two elements share storage (kernels/writeback.py:6-15)."""
+    extent = 1
+    for stride, size in sorted(zip(tensor.stride(), tensor.shape)):
+        if size > 1:
+            if stride < extent:
+                return False
+            extent += (size - 1) * stride
+    return True
+
+
+def kv_strides(tensor: torch.Tensor) -> tuple[int, int]:
+    """(head_stride, row_stride) of a ``[1, H, N, D]`` tensor with unit D stride."""
+    if tensor.stride(3) != 1 and tensor.shape[3] > 1:
+        raise ValueError("cache tensors need a unit stride along head_dim")
+    return tensor.stride(1), tensor.stride(2)
+
+
+def require_cuda_tensors(tensors, what: str) -> torch.device:
+    device = None
+    for t in tensors:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError(f"{what} requires CUDA tensors (the B200 engine has no CPU path)")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise ValueError(f"{what}: all tensors must share one CUDA device")
+    return device
+
+
+def qualify_model(model: Any, base: Any, layer_count: int, device: torch.device, dtype: torch.dtype) -> None:
+    """Model contract of the packed path (kernels/packed_cache.py:123-163, api.py:135-166).
+
+    Exact native dense Llama/Qwen3 classes, eval mode, default RoPE, full
+    attention, every parameter on the request device, no offload hooks or
+    per-instance forwards, and the arithmetic the kernels implement.
+    """
+    from transformers.models.llama.modeling_llama import LlamaForCausalLM, LlamaModel
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3ForCausalLM, Qwen3Model
+
+    pairs = {(LlamaForCausalLM, LlamaModel), (Qwen3ForCausalLM, Qwen3Model)}
+    if (type(model), type(base)) not in pairs and type(model) not in (LlamaModel, Qwen3Model):
+        raise ValueError("packed executor requires exact native dense Llama or Qwen3 classes")
+    if model.training or base.training or any(module.training for module in base.modules()):
+        raise ValueError("packed executor requires eval mode on all decoder modules")
+    config = model.config
+    if config.num_hidden_layers != layer_count or len(base.layers) != layer_count:
+        raise ValueError("model and cache layer counts must agree")
+    rope = getattr(config, "rope_parameters", None)
+    rope_type = rope.get("rope_type", "default") if isinstance(rope, dict) else None
+    if rope is None:
+        scaling = getattr(config, "rope_scaling", None)
+        rope_type = "default" if scaling is None else scaling.get("rope_type", scaling.get("type"))
+    if rope_type != "default" or getattr(base.rotary_emb, "rope_type", "default") != "default":
+        raise ValueError("packed executor supports default fixed RoPE only")
+    if getattr(config, "use_sliding_window", False) or getattr(base, "has_sliding_layers", False):
+        raise ValueError("packed executor requires full attention")
+    if any(kind != "full_attention" for kind in getattr(config, "layer_types", []) or []):
+        raise ValueError("packed executor rejects sliding/hybrid attention")
+    if any(parameter.device != device for parameter in model.parameters()):
+        raise ValueError("packed executor requires all model parameters on the request device")
+    if any(getattr(module, "_hf_hook", None) is not None for module in model.modules()):
+        raise ValueError("packed executor does not support dispatch/offload hooks")
+    if any("forward" in module.__dict__ for module in base.modules()):
+        raise ValueError("packed executor does not support per-instance decoder forward overrides")
+    if getattr(model, "is_quantized", False):
+        raise ValueError("packed executor does not support quantized models")
+    if getattr(config, "hidden_act", "silu") != "silu":
+        raise ValueError("packed executor implements the SiLU-gated MLP only")
+    if getattr(config, "attention_bias", False) or getattr(config, "mlp_bias", False):
+        raise ValueError("packed executor implements bias-free projections only")
+    if any(parameter.dtype != dtype for parameter in base.parameters()):
+        raise ValueError("model parameters and cache must share one bfloat16/float16 dtype")

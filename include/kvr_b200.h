@@ -1,0 +1,193 @@
+/*
+ * kvr_b200.h - C ABI of the B200 packed refresh engine (libkvr_b200.so).
+ *
+ * Plain pointers, sizes and strides only. Every entry point:
+ *   - returns an int status (KVR_OK or one of the KVR_ERR_* codes below),
+ *   - validates its arguments on the host before launching anything,
+ *   - launches on the caller's stream (`stream` is a cudaStream_t; NULL is the
+ *     legacy default stream), never synchronises and never reads device memory
+ *     back to the host,
+ *   - lets no C++ exception cross the ABI.
+ * Device pointers must belong to the current device. Element type codes are
+ * KVR_DTYPE_BF16 and KVR_DTYPE_F16. Strides are in elements.
+ *
+ * Cache tensors use the reference layout [1, Hkv, N, D] per layer (transformers
+ * DynamicCache), addressed here as (head_stride, row_stride) with unit stride
+ * along D. Reference paths below are relative to yh0903/budgeted-kv-cache-repair.
+ */
+#ifndef KVR_B200_H
+#define KVR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KVR_API __attribute__((visibility("default")))
+#else
+#define KVR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVR_OK 0
+#define KVR_ERR_INVALID_ARG 1   /* bad pointer, size, stride or alignment */
+#define KVR_ERR_UNSUPPORTED 2   /* shape/dtype outside the built kernels */
+#define KVR_ERR_CUDA 3          /* a CUDA runtime call failed; see kvr_last_cuda_error */
+#define KVR_ERR_TIMEOUT 4       /* a bounded device wait gave up */
+
+#define KVR_DTYPE_BF16 0
+#define KVR_DTYPE_F16 1
+
+/* Largest number of per-layer tensors one multi-layer launch takes (K and V of
+ * 128 layers). */
+#define KVR_MAX_LAYER_TENSORS 256
+
+/* Library identification and diagnostics. */
+KVR_API const char* kvr_version(void);
+KVR_API const char* kvr_status_string(int status);
+/* cudaError_t of the last failing CUDA call in this thread (0 if none). */
+KVR_API int kvr_last_cuda_error(void);
+/* Kernels this library has launched in this process (all threads, all
+ * devices); a diagnostic counter for benchmarks and tests. */
+KVR_API uint64_t kvr_kernel_launches(void);
+
+/*
+ * Output ownership copy of every layer: dst[t][h, n, :] = src[t][h, n, :] for
+ * t < num_tensors (K and V of each layer, any order), h < heads, n < rows.
+ * Replaces clone_cache (cache.py:31-44) as used by packed_interval_repair
+ * (kernels/packed_cache.py:287). One launch for all layers.
+ */
+KVR_API int kvr_copy_layers(const void* const* src, void* const* dst, int num_tensors,
+                    int heads, int64_t rows, int head_dim,
+                    int64_t src_head_stride, int64_t src_row_stride,
+                    int64_t dst_head_stride, int64_t dst_row_stride,
+                    int dtype, void* stream);
+
+/*
+ * Delta-RoPE of retained suffix keys for every layer at once:
+ *   dst[l][h, r, :] = src[l][h, r, :] * cos + rotate_half(src[l][h, r, :]) * sin
+ * with cos/sin = cos_sin[0:D], cos_sin[D:2D] (one angle set: every row moves
+ * by the same shift), each product and the sum rounded to the element type the
+ * way torch's bf16/fp16 elementwise ops round them. src == dst is allowed.
+ * Replaces shifted_suffix_keys (cache.py:47-77) called per layer by
+ * build_halo_cache (cache.py:129-139).
+ */
+KVR_API int kvr_rope_shift_layers(const void* const* src, void* const* dst, int num_layers,
+                          int heads, int64_t rows, int head_dim,
+                          int64_t src_head_stride, int64_t src_row_stride,
+                          int64_t dst_head_stride, int64_t dst_row_stride,
+                          const void* cos_sin, int dtype, void* stream);
+
+/*
+ * Whole shift cache for every layer in one launch (build_halo_cache with
+ * halo 0, cache.py:103-144): for each layer, head and new row n < new_rows
+ *   n <  prefix          : K, V copied from old row n
+ *   n >= new_tail_start  : K rotated (as above; copied when apply_rope == 0)
+ *                          and V copied from old row n - new_tail_start + old_tail_start
+ * Rows in [prefix, new_tail_start) are left untouched (changed boundary tokens,
+ * recomputed afterwards). k_old/v_old/k_new/v_new each hold num_layers pointers.
+ */
+KVR_API int kvr_shift_cache_layers(const void* const* k_old, const void* const* v_old,
+                           void* const* k_new, void* const* v_new, int num_layers,
+                           int heads, int head_dim, int64_t new_rows, int64_t prefix,
+                           int64_t old_tail_start, int64_t new_tail_start,
+                           int64_t old_head_stride, int64_t old_row_stride,
+                           int64_t new_head_stride, int64_t new_row_stride,
+                           const void* cos_sin, int apply_rope, int dtype, void* stream);
+
+/*
+ * Bitwise row scatter of fresh K/V into one layer's cache:
+ *   k_cache[h, positions[r], :] = k_fresh[h, r, :] (same for V).
+ * Positions outside [0, cache_rows) are skipped and counted in *error_count
+ * (device int, may be NULL). Replaces indexed_kv_scatter_
+ * (kernels/indexed_attention.py:179-204) and _PackedLayer.update's index_copy_
+ * (kernels/packed_cache.py:189-191).
+ */
+KVR_API int kvr_scatter_rows(const void* k_fresh, const void* v_fresh, void* k_cache, void* v_cache,
+                     const int64_t* positions, int64_t rows, int heads, int head_dim,
+                     int64_t cache_rows,
+                     int64_t fresh_head_stride, int64_t fresh_row_stride,
+                     int64_t cache_head_stride, int64_t cache_row_stride,
+                     int* error_count, int dtype, void* stream);
+
+/*
+ * Embedding gather of the selected rows (the native forward's embed_tokens on
+ * edited_ids.index_select(1, positions), kernels/packed_cache.py:291):
+ *   out[r, :] = embed[ids[positions[r]], :]
+ * Out-of-range positions or ids write a zero row and increment *error_count.
+ */
+KVR_API int kvr_embed_rows(const void* embed, int64_t vocab, int hidden,
+                   const int64_t* ids, int64_t id_count, const int64_t* positions, int64_t rows,
+                   void* out, int* error_count, int dtype, void* stream);
+
+/*
+ * Residual add fused with RMSNorm (transformers LlamaRMSNorm / Qwen3RMSNorm and
+ * the decoder layer's `residual + hidden_states`):
+ *   if delta != NULL: hidden = round(hidden + delta)   (written back in place)
+ *   out = round(weight * round(hidden * rsqrt(mean(hidden^2) + eps)))
+ * mean in fp32. Row-major [rows, hidden_size] with row strides.
+ */
+KVR_API int kvr_add_rmsnorm(void* hidden, const void* delta, const void* weight, void* out,
+                    int64_t rows, int hidden_size, int64_t hidden_stride, int64_t delta_stride,
+                    int64_t out_stride, float eps, int dtype, void* stream);
+
+/*
+ * Per-layer K/V epilogue of the packed forward, fused (kernels/packed_cache.py:
+ * 290-295 through the native attention module and _PackedLayer.update):
+ *   q  = RoPE(q_norm(q))       -> q_out[r, head, :]       (q_norm only if q_norm_w)
+ *   k  = RoPE(k_norm(k))       -> k_cache[h, positions[r], :]
+ *   v                          -> v_cache[h, positions[r], :]   (bitwise)
+ * q_in/k_in/v_in: GEMM outputs [rows, heads*D] with row strides. cos/sin:
+ * [rows, D] tables of the element type (rotary_emb at the selected positions).
+ * q_out: [rows, q_heads, D] contiguous; may be NULL (K/V only, e.g. the last
+ * layer). Out-of-range positions are skipped and counted in *error_count.
+ */
+KVR_API int kvr_qkv_rope_scatter(const void* q_in, const void* k_in, const void* v_in,
+                         int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride,
+                         const void* q_norm_w, const void* k_norm_w, float eps,
+                         const void* cos_tab, const void* sin_tab, const int64_t* positions,
+                         int64_t rows, int q_heads, int kv_heads, int head_dim,
+                         void* q_out, void* k_cache, void* v_cache, int64_t cache_rows,
+                         int64_t cache_head_stride, int64_t cache_row_stride,
+                         int* error_count, int dtype, void* stream);
+
+/*
+ * MLP activation: out = round(round(silu(gate)) * up), elementwise over
+ * [rows, width] (transformers LlamaMLP.forward: act_fn(gate_proj(x)) * up_proj(x)).
+ */
+KVR_API int kvr_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int64_t width,
+                 int64_t gate_stride, int64_t up_stride, int64_t out_stride,
+                 int dtype, void* stream);
+
+/*
+ * Selected-query absolute-causal attention with GQA, on sm_100a tensor cores.
+ * q [rows, q_heads, D] contiguous; K/V [kv_heads, cache_rows, D] with strides;
+ * out [rows, q_heads, D] contiguous. Row r attends keys 0..positions[r]
+ * (inclusive); positions must be strictly increasing (as IndexedPlan
+ * guarantees). Query head j reads KV head j / (q_heads / kv_heads).
+ * softmax(scale * q.k) in fp32, one rounding on output.
+ * Replaces _packed_attention's SDPA call with its dense [1,1,B,N] mask and
+ * repeat_kv (kernels/packed_cache.py:47-67, 203-207) and the experimental
+ * indexed_causal_attention (kernels/indexed_attention.py:207-241).
+ *
+ * The key range is split across CTAs when rows are few; partial results go
+ * to `workspace` (device memory of at least kvr_attention_workspace_size()
+ * bytes, any contents) and a second launch combines them. Both launches are
+ * on `stream`; the workspace must not be shared by overlapping calls.
+ */
+KVR_API size_t kvr_attention_workspace_size(int64_t rows, int q_heads, int kv_heads, int head_dim,
+                                    int64_t cache_rows);
+KVR_API int kvr_selected_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                           const int64_t* positions, int64_t rows, int q_heads, int kv_heads,
+                           int head_dim, int64_t cache_rows,
+                           int64_t cache_head_stride, int64_t cache_row_stride,
+                           int64_t max_position, float scale,
+                           void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVR_B200_H */

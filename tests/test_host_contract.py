@@ -1,0 +1,239 @@
+"""Host-side contract of the B200 engine (no GPU needed): C-ABI exports, plan
+and interval rules against the reference's golden verdicts, fail-closed errors."""
+
+import ctypes
+import os
+import re
+from dataclasses import FrozenInstanceError
+
+import pytest
+import torch
+
+from conftest import ROOT, load_golden
+
+
+@pytest.fixture(scope="module")
+def built():
+    from budgeted_kv_cache_repair_b200 import build
+
+    return build.build()
+
+
+def _header_symbols():
+    text = open(os.path.join(ROOT, "include", "kvr_b200.h")).read()
+    return sorted(set(re.findall(r"^KVR_API [^(]*?\b(kvr_\w+)\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol(built):
+    from budgeted_kv_cache_repair_b200 import _lib
+
+    lib = ctypes.CDLL(built)
+    names = _header_symbols()
+    assert len(names) >= 14
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures must mirror the header"
+    assert _lib.load().kvr_version().decode().startswith("kvr_b200")
+    assert _lib.load().kvr_status_string(2).decode() == "unsupported shape or dtype"
+
+
+def test_native_argument_checks_run_without_a_gpu(built):
+    """Bad arguments are rejected on the host before any launch."""
+    from budgeted_kv_cache_repair_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.kvr_copy_layers(None, None, 1, 1, 1, 8, 8, 8, 8, 8, 0, None) == _lib.ERR_INVALID_ARG
+    assert lib.kvr_rope_shift_layers(None, None, 1, 1, 1, 96, 96, 96, 96, 96, None, 0, None) == _lib.ERR_UNSUPPORTED
+    assert lib.kvr_selected_attention(None, None, None, None, None, 4, 3, 2, 128, 10, 1280, 128, 3, 1.0, None, 0, 0,
+                                      None) == _lib.ERR_INVALID_ARG
+    assert lib.kvr_silu_mul(None, None, None, 0, 16, 16, 16, 16, 7, None) == _lib.ERR_UNSUPPORTED
+    # Empty work is a no-op success.
+    assert lib.kvr_scatter_rows(None, None, None, None, None, 0, 1, 64, 9, 0, 0, 0, 0, None, 0, None) == _lib.OK
+    assert lib.kvr_attention_workspace_size(64, 32, 8, 128, 7936) > 0
+    assert lib.kvr_attention_workspace_size(5000, 32, 8, 128, 7936) == 0  # enough tiles: no split
+
+
+def test_alignment_matches_reference():
+    from budgeted_kv_cache_repair_b200 import token_alignment
+
+    for case in load_golden("alignment.pt"):
+        assert token_alignment(case["old"], case["new"]) == case["expected"]
+
+
+def test_plan_tiles_and_interval_rules_match_reference():
+    from budgeted_kv_cache_repair_b200 import IndexedPlan, positions_to_intervals
+    from budgeted_kv_cache_repair_b200.validate import validate_intervals
+
+    golden = load_golden("plans.pt")
+    for plan in golden["plans"]:
+        ours = IndexedPlan(plan["positions"], plan["length"])
+        assert ours.full_prefix_tiles == tuple(plan["full"]) and ours.total_tiles == tuple(plan["total"])
+        assert positions_to_intervals(plan["positions"]) == [tuple(x) for x in plan["intervals"]]
+    for verdict in golden["interval_verdicts"]:
+        if verdict["ok"]:
+            assert [list(x) for x in validate_intervals(verdict["intervals"], verdict["length"])] == \
+                   [list(x) for x in verdict["result"]]
+        else:
+            with pytest.raises(ValueError):
+                validate_intervals(verdict["intervals"], verdict["length"])
+
+
+def test_host_plan_owns_immutable_sorted_metadata():
+    from budgeted_kv_cache_repair_b200 import IndexedPlan
+
+    positions = [3, 4, 8, 9]
+    plan = IndexedPlan(positions, 10)
+    positions[0] = 0
+    assert plan.positions == (3, 4, 8, 9) and plan.max_position == 9
+    with pytest.raises(FrozenInstanceError):
+        plan.logical_length = 12
+
+
+@pytest.mark.parametrize("positions,length", [
+    ([2, 1], 4), ([1, 1], 4), ([-1], 4), ([4], 4), ([True], 4), ([1.0], 4), (torch.tensor([1]), 4),
+    ([0], -1), ([], True), ([], 4.0), ([], 1 << 63), (None, 4),
+])
+def test_invalid_host_plans_fail_before_any_device_operation(positions, length):
+    from budgeted_kv_cache_repair_b200 import IndexedPlan
+
+    with pytest.raises(ValueError):
+        IndexedPlan(positions, length)
+
+
+def test_host_plan_upload_rejects_cpu():
+    from budgeted_kv_cache_repair_b200 import IndexedPlan
+
+    with pytest.raises(ValueError, match="CUDA"):
+        IndexedPlan([0], 1).to("cpu")
+
+
+def test_operators_reject_cpu_without_fallback():
+    from budgeted_kv_cache_repair_b200 import IndexedPlan, indexed_causal_attention, indexed_kv_scatter_
+    from budgeted_kv_cache_repair_b200.cache import copy_layers
+
+    q = torch.zeros((1, 1, 1, 64), dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA"):
+        indexed_causal_attention(q, q, q, IndexedPlan([0], 1))
+    with pytest.raises(ValueError, match="CUDA"):
+        indexed_kv_scatter_(q, q, q, q, IndexedPlan([0], 1))
+    with pytest.raises(ValueError, match="CUDA"):
+        copy_layers([(q, q)])
+
+
+def _tiny_model(family="llama"):
+    from transformers import LlamaConfig, LlamaForCausalLM, Qwen3Config, Qwen3ForCausalLM
+
+    options = dict(vocab_size=97, hidden_size=32, intermediate_size=64, num_hidden_layers=2,
+                   num_attention_heads=4, num_key_value_heads=2, head_dim=8, max_position_embeddings=64)
+    torch.manual_seed(71)
+    if family == "llama":
+        return LlamaForCausalLM(LlamaConfig(**options)).eval()
+    return Qwen3ForCausalLM(Qwen3Config(**options, layer_types=["full_attention"] * 2)).eval()
+
+
+def _request(model, length=12):
+    from budgeted_kv_cache_repair_b200 import OperatorShim
+
+    ids = (torch.arange(length) % 60 + 4).unsqueeze(0)
+    with torch.no_grad():
+        base = model(input_ids=ids, use_cache=True).past_key_values
+    return OperatorShim(model), ids, base
+
+
+def test_empty_support_returns_base_and_does_no_work(monkeypatch):
+    import budgeted_kv_cache_repair_b200.packed as packed
+    from budgeted_kv_cache_repair_b200 import IndexedPlan, packed_interval_repair
+    from budgeted_kv_cache_repair_b200.cache import make_cache
+
+    def forbidden(*args, **kwargs):
+        raise AssertionError("empty support must not prepare or execute work")
+
+    monkeypatch.setattr(packed, "qualify_model", forbidden)
+    monkeypatch.setattr(packed, "refresh_rows", forbidden)
+    monkeypatch.setattr(packed, "copy_layers", forbidden)
+    monkeypatch.setattr(IndexedPlan, "to", forbidden)
+    base = make_cache([(torch.zeros(1, 2, 0, 8), torch.zeros(1, 2, 0, 8)) for _ in range(2)])
+    actual, receipt = packed_interval_repair(object(), base, torch.empty((1, 0), dtype=torch.long), [])
+    assert actual is base
+    assert receipt["output_cache_ownership"] == "borrowed_base"
+    assert receipt["recomputed_tokens"] == 0
+
+
+def test_receipt_keys_match_reference():
+    from budgeted_kv_cache_repair_b200.packed import make_receipt
+
+    golden = load_golden("case_cfg0_llama_fp32.pt")["receipt"]
+    ours = make_receipt([(50, 54)], golden["logical_length"], golden["layer_count"])
+    for key, value in golden.items():
+        assert ours[key] == value, key
+    assert ours["engine"].startswith("kvr_b200")
+
+
+@pytest.mark.parametrize("fault", ["attention_backend", "writeback_backend", "interval", "ids_rank", "ids_dtype",
+                                   "cache_length", "plan", "cpu_cache"])
+def test_fail_closed_contract_before_device_work(fault):
+    from budgeted_kv_cache_repair_b200 import IndexedPlan, packed_interval_repair
+
+    model = _tiny_model()
+    shim, ids, base = _request(model)
+    kwargs, intervals = {}, [(3, 5)]
+    if fault == "attention_backend":
+        kwargs["attention_backend"] = "triton"
+    elif fault == "writeback_backend":
+        kwargs["writeback_backend"] = "triton"
+    elif fault == "interval":
+        intervals = [(3, 5), (5, 6)]
+    elif fault == "ids_rank":
+        ids = ids[0]
+    elif fault == "ids_dtype":
+        ids = ids.float()
+    elif fault == "cache_length":
+        ids = ids[:, :-1]
+    elif fault == "plan":
+        kwargs["plan"] = IndexedPlan((3,), 12)
+    with pytest.raises(ValueError):
+        packed_interval_repair(shim, base, ids, intervals, **kwargs)
+
+
+def test_api_validates_before_work():
+    from budgeted_kv_cache_repair_b200 import repair_after_deletion, select_support
+    from budgeted_kv_cache_repair_b200.api import budget_tokens
+
+    model = _tiny_model()
+    for bad in (True, -1, 101, float("nan")):
+        with pytest.raises(ValueError):
+            repair_after_deletion(model, None, None, "abc", delete_span=(0, 1), query="", budget_percent=bad)
+    with pytest.raises(ValueError):
+        repair_after_deletion(model, None, None, "abc", delete_span=(2, 1), query="")
+    with pytest.raises(ValueError):
+        repair_after_deletion(model, None, None, "abc", delete_span=(0, 1), query="", executor="other")
+    with pytest.raises(ValueError, match="CUDA"):
+        repair_after_deletion(model, None, None, "abc", delete_span=(0, 1), query="")
+    assert budget_tokens(3, 5) == 1 and budget_tokens(100, 2) == 2 and budget_tokens(72, 5) == 4
+    assert budget_tokens(0, 50) == 0 and budget_tokens(10, 100) == 10
+
+
+def test_shift_cache_host_path_rejects_cpu_caches():
+    from budgeted_kv_cache_repair_b200 import build_halo_cache
+
+    model = _tiny_model()
+    shim, ids, base = _request(model)
+    with pytest.raises(ValueError, match="CUDA"):
+        build_halo_cache(shim, base, ids, ids[:, 2:], 0)
+
+
+def test_rotate_half_uses_split_half_convention():
+    from budgeted_kv_cache_repair_b200 import rotate_half
+
+    assert rotate_half(torch.tensor([1.0, 2.0, 3.0, 4.0])).tolist() == [-3.0, -4.0, 1.0, 2.0]
+
+
+def test_dynamic_cache_construction_keeps_storage():
+    from budgeted_kv_cache_repair_b200.cache import make_cache
+    from budgeted_kv_cache_repair_b200.validate import cache_layers
+
+    pairs = [(torch.randn(1, 2, 5, 8), torch.randn(1, 2, 5, 8)) for _ in range(3)]
+    cache = make_cache(pairs)
+    assert cache.get_seq_length() == 5 and len(cache_layers(cache)) == 3
+    for (k, v), (k2, v2) in zip(pairs, cache_layers(cache)):
+        assert k is k2 and v is v2
