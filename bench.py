@@ -292,17 +292,18 @@ def our_arm(args):
     torch.cuda.synchronize()
     from budgeted_kv_cache_repair_b200.cache import shift_layers
 
-    rope_ms = []
+    rope_timer = engine.KernelTimer()
+    torch.cuda.nvtx.range_push("rope_fix")
+    engine.set_kernel_timer(rope_timer)
     for _ in range(max(args.steps, 5)):
-        begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        begin.record(stream)
         layers = shift_layers(shim, old_pairs, alignment, alignment["new_suffix_start"], alignment["old_suffix_start"])
-        end.record(stream)
-        end.synchronize()
-        rope_ms.append(begin.elapsed_time(end))
         del layers
+    engine.set_kernel_timer(None)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    n_rope, rope_total = rope_timer.totals_ms()["shift_cache_layers"]
     fused_bytes, rope_bytes = rope_fix_bytes(cfg, length, alignment["suffix"])
-    rope_t = statistics.median(rope_ms) / 1e3
+    rope_t = rope_total / n_rope / 1e3
 
     # ---- refresh stage through the public API ----
     ids_dev = new_ids
@@ -316,6 +317,7 @@ def our_arm(args):
     _barrier(world)
     torch.cuda.synchronize()
     launches_before = _lib.load().kvr_kernel_launches()
+    torch.cuda.nvtx.range_push("refresh")
     with sampler:
         region_begin = torch.cuda.Event(enable_timing=True)
         region_begin.record(stream)
@@ -331,6 +333,7 @@ def our_arm(args):
         region_end = torch.cuda.Event(enable_timing=True)
         region_end.record(stream)
         torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     launches = _lib.load().kvr_kernel_launches() - launches_before
     _barrier(world)
     region_ms = region_begin.elapsed_time(region_end)

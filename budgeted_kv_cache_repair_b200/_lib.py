@@ -18,6 +18,7 @@ LIBRARY = os.path.join(HERE, "lib", "libkvr_b200.so")
 
 OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT = 0, 1, 2, 3, 4
 DTYPE_BF16, DTYPE_F16 = 0, 1
+ATTN_P_SPLIT, ATTN_P_ROUNDED = 0, 1
 MAX_LAYER_TENSORS = 256
 
 _P = ctypes.c_void_p
@@ -43,7 +44,7 @@ SIGNATURES = {
                                   _P, _P, _P, _L, _L, _L, _P, _I, _P]),
     "kvr_silu_mul": (_I, [_P, _P, _P, _L, _L, _L, _L, _L, _I, _P]),
     "kvr_attention_workspace_size": (ctypes.c_size_t, [_L, _I, _I, _I, _L]),
-    "kvr_selected_attention": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _P,
+    "kvr_selected_attention": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _I, _P,
                                     ctypes.c_size_t, _I, _P]),
 }
 

@@ -168,6 +168,10 @@ def shift_layers(model: Any, pairs, alignment: dict, recompute_end: int, old_tai
     v_new = [torch.empty((1, heads, new_rows, dim), dtype=key.dtype, device=device) for _ in pairs]
     if new_rows:
         table = _shift_table(model, key, shift) if shift and old_rows > old_tail_start else None
+        from .engine import kernel_timer
+
+        timer = kernel_timer()
+        token = timer.start("shift_cache_layers") if timer else None
         lib = _lib.load()
         _lib.check(lib.kvr_shift_cache_layers(
             _lib.ptr_array([k for k, _ in pairs]), _lib.ptr_array([v for _, v in pairs]),
@@ -175,6 +179,8 @@ def shift_layers(model: Any, pairs, alignment: dict, recompute_end: int, old_tai
             alignment["prefix"], old_tail_start, recompute_end, hs, rs, new_rows * dim, dim,
             table.data_ptr() if table is not None else None, 1 if table is not None else 0,
             _lib.dtype_code(key.dtype), _lib.stream_handle(device)), "shift_cache_layers")
+        if token:
+            timer.stop(token)
     return list(zip(k_new, v_new))
 
 

@@ -1,414 +1,598 @@
-// Selected-query absolute-causal attention with GQA packing and split-KV.
+// Selected-query absolute-causal attention on sm_100a tensor cores (tcgen05 +
+// TMEM + TMA), GQA-packed and split over the key range.
 //
-// Work unit (CTA): one KV head h, one tile of BM=64 "m-entries", one key chunk.
-// An m-entry is a (selected row r, query head of group g) pair, m = r*G + g, so
-// the G query heads that share KV head h ride in the same MMA rows and every
-// K/V tile read from HBM serves all of them (no repeat_kv). Rows are sorted by
-// absolute position, so a tile's causal span is [0, pos(last row)] and keys
-// below pos(first row) need no mask.
+// Work unit (CTA): one KV head h, one tile of 128 "m-entries" and one key
+// chunk. An m-entry is a (selected row r, query head g of the group) pair,
+// m = r*G + g: the G query heads that share KV head h occupy MMA rows of the
+// same tile, so each K/V tile brought on chip serves all of them (no
+// repeat_kv). Rows are sorted by absolute position; a tile's causal span is
+// [0, pos(last row)].
 //
-// Inside a CTA, 4 warps each own 16 m-entries. K/V blocks of 64 keys stream
-// through a cp.async double buffer in XOR-swizzled shared memory; S = Q K^T and
-// O += P V run on the tensor cores (m16n8k16, fp32 accumulate). The online
-// softmax is fp32. P is split as P = P_hi + P_lo (both in the element type)
-// and both halves multiply V, so probabilities keep ~16 mantissa bits, close
-// to the reference's fp32-probability P@V (kernels/_indexed_triton.py:58).
+// One CTA per SM, 6 warps:
+//   warp 4  TMA producer: K and V blocks of 128 keys, 128B-swizzled, into a
+//           ring of NS stages (bounded-wait mbarriers, no multicast)
+//   warp 5  MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S
+//           buffers, then O += P_j V_j into the TMEM O accumulator
+//   warps 0-3  softmax: thread t owns TMEM lane t = m-entry t. It loads its S
+//           row, applies the causal/chunk mask, keeps a running max, writes
+//           P = 2^(s - m) to shared memory as the A operand of the PV MMA, and
+//           rescales its O row in TMEM only when the max grew by more than
+//           2^8 (exact: the final normalisation uses the same stale max).
+// QK^T of block j+1 overlaps the softmax of block j.
 //
-// When the (head, tile) grid is too small for 148 SMs the key range is cut
-// into chunks; each chunk CTA writes unnormalised partials (O, running max,
-// running sum) to the workspace and attn_combine_kernel merges them.
+// Precision: QK^T and PV run on bf16/fp16 operands with fp32 accumulation.
+// With SPLIT, P is issued as P_hi + P_lo (two element-type halves, two PV
+// MMAs), keeping ~16 mantissa bits of the probabilities as the reference's
+// fp32-probability P@V does (kernels/_indexed_triton.py:58); without SPLIT, P
+// is rounded once, as in fused SDPA kernels.
+//
+// Partial results of a split key range go to the workspace as (O, max, sum)
+// and attn_combine_kernel merges them. Every wait is bounded: on timeout the
+// kernel records an error code in the workspace status word, stops issuing,
+// drains its own in-flight TMA and MMA work, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <math.h>
 
+#include <type_traits>
+
 #include "kvr_common.cuh"
+#include "kvr_sm100.cuh"
 
 namespace kvr {
-
 namespace attn {
 
-constexpr int BM = 64;        // m-entries per CTA
-constexpr int BN = 64;        // keys per block
-constexpr int THREADS = 128;  // 4 warps x 16 m-entries
+constexpr int BM = 128;  // m-entries per CTA (MMA M, TMEM lanes)
+constexpr int BN = 128;  // keys per block (MMA N of QK^T, K of PV)
+constexpr int kSoftmaxThreads = 256;  // warps 0-7: two threads per m-entry row
+constexpr int kTmaWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int THREADS = 320;
+constexpr int SUB = BM * 128;  // one [128 rows x 128 B] swizzled sub-tile
+constexpr int STATUS_BYTES = 256;
+constexpr long long WAIT_LIMIT = 4000000000LL;  // SM clocks (~2 s)
+
+enum Err : int { ERR_KV_EMPTY = 1, ERR_Q_FULL, ERR_KV_FULL, ERR_S_FREE, ERR_P_FULL, ERR_S_FULL,
+                 ERR_PV_DONE, ERR_DRAIN, ERR_RED, ERR_SMEM_ALIGN };
 
 struct Args {
   const uint16_t* q;
-  const uint16_t* k;
-  const uint16_t* v;
   uint16_t* out;
   const int64_t* positions;
   int64_t rows;
   int hq, hkv, group;
-  int64_t cache_rows, c_hs, c_rs;
   float scale_log2;
   int tiles, nchunks;
   int64_t chunk;  // keys per chunk (multiple of BN)
-  float* ws_o;    // [hkv][tiles][nchunks][BM][D]
-  float* ws_ml;   // [hkv][tiles][nchunks][BM][2]
+  int* status;    // workspace status word (error code, 0 = ok)
+  float* ws_o;    // [hkv][tiles][nchunks][BM][D] unnormalised O
+  float* ws_ml;   // [hkv][tiles][nchunks][BM][2] (running max, sum)
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
+template <int D, bool SPLIT>
+struct Layout {
+  static constexpr int DS = D / 64;  // 64-element (128 B) sub-tiles across head_dim
+  static constexpr int NS = (D == 128 || SPLIT) ? 2 : 3;  // K/V ring stages
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + DS * SUB;
+  static constexpr int V_OFF = K_OFF + NS * DS * SUB;
+  // P buffers (A operand of P.V, [128 rows x 128 keys]): double-buffered so the
+  // softmax of block j overlaps the P.V MMA of block j-1, except for split P at
+  // head_dim 128, where two halves of two buffers do not fit next to K/V.
+  static constexpr int NP = (SPLIT && D == 128) ? 1 : 2;
+  static constexpr int P_BYTES = (SPLIT ? 4 : 2) * SUB;  // hi (+ lo) halves, 2 sub-tiles each
+  static constexpr int P_OFF = V_OFF + NS * DS * SUB;
+  static constexpr int BAR_OFF = P_OFF + NP * P_BYTES;
+  // q_full, kv_full[NS], kv_empty[NS], s_full[2], s_free[2], p_full[NP], pv_done[NP], drain, red_bar[3]
+  static constexpr int NBAR = 1 + 2 * NS + 4 + 2 * NP + 1 + 3;
+  static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;
+  static constexpr int RED_OFF = MISC_OFF + 16;  // float [2 parities][2 halves][128 rows] max/sum exchange
+  static constexpr int USED = RED_OFF + 2 * 2 * BM * 4;
+  // Swizzled tiles need a 1 KB-aligned base; the allocation carries what slack
+  // fits under the per-CTA limit and the kernel checks it at run time.
+  static constexpr int BYTES = USED + 1024 <= 232448 ? USED + 1024 : 232448;
+  static constexpr uint32_t STAGE_TX = 2u * DS * SUB;
+  static_assert(USED <= 232448, "dynamic shared memory above the 227 KB per-CTA limit");
+};
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  const int n = valid ? 16 : 0;  // src-size 0 zero-fills the 16 bytes
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(n));
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(n) : "memory");
 }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-template <class T>
-__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1);
-
-template <>
-__device__ __forceinline__ void mma16816<BF16>(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-template <>
-__device__ __forceinline__ void mma16816<F16>(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Two floats -> packed pair of 16-bit elements (low half = first).
 template <class T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return static_cast<uint32_t>(T::from_f(lo)) | (static_cast<uint32_t>(T::from_f(hi)) << 16);
 }
 
-// Byte offset of 16-byte chunk c of row r in a swizzled [rows][D] tile.
-template <int D>
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-  return static_cast<uint32_t>(r * (D * 2) + ((c ^ (r & 7)) << 4));
+// Two floats -> packed pair with the hardware round-to-nearest conversion
+// (cvt.rn.bf16x2.f32 / cvt.rn.f16x2.f32); used for probabilities, which are
+// finite and non-negative, so NaN payload conventions do not arise.
+template <class T>
+__device__ __forceinline__ uint32_t pack2_hw(float lo, float hi) {
+  if constexpr (std::is_same<T, BF16>::value) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+template <class T>
+__device__ __forceinline__ float lo_half(uint32_t v) {
+  return T::to_f(static_cast<uint16_t>(v & 0xffffu));
+}
+template <class T>
+__device__ __forceinline__ float hi_half(uint32_t v) {
+  return T::to_f(static_cast<uint16_t>(v >> 16));
 }
 
-template <class T, int D>
-__global__ void __launch_bounds__(THREADS) attn_kernel(Args a) {
-  constexpr int CPR = D / 8;              // 16-byte chunks per row
-  constexpr int TILE_BYTES = BN * D * 2;  // one K or V block
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* sq = smem;                        // [BM][D]
-  uint8_t* skv = smem + BM * D * 2;          // 2 stages x (K, V)
+// 2^x with the MUFU approximation (relative error ~2^-22; inputs here are <= 8).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
-  const int gq = lane >> 2, tq = lane & 3;
+// Byte offset of 16-byte chunk c (0..7) of row r in a 128B-swizzled sub-tile.
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+template <class T, int D, bool SPLIT>
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                   Args a) {
+  using L = Layout<D, SPLIT>;
+  constexpr int DS = L::DS, NS = L::NS, NP = L::NP;
+  constexpr int HD = D / 2;  // O columns per softmax thread
+  constexpr bool kBF16 = std::is_same<T, BF16>::value;
+  extern __shared__ uint8_t smem_raw[];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.y;
-  const int tile = blockIdx.x / a.nchunks;
-  const int chunk = blockIdx.x - tile * a.nchunks;
+  const int tile = blockIdx.x % a.tiles;  // tiles of one chunk launch together (shared K/V in L2)
+  const int chunk = blockIdx.x / a.tiles;
   const int G = a.group;
   const int64_t total_m = a.rows * G;
   const int64_t m0 = static_cast<int64_t>(tile) * BM;
-  const int64_t r_first = m0 / G;
   int64_t r_last = (m0 + BM - 1) / G;
   if (r_last > a.rows - 1) r_last = a.rows - 1;
-  const int64_t pmin = a.positions[r_first];
   const int64_t pmax = a.positions[r_last];
-  const int64_t k_begin = chunk * a.chunk;
-  if (k_begin > pmax) return;  // this chunk lies past every row of the tile
+  const int64_t k_begin = static_cast<int64_t>(chunk) * a.chunk;
+  if (k_begin > pmax) return;  // chunk lies past every row of the tile (uniform exit)
   int64_t k_end = k_begin + a.chunk;
   if (k_end > pmax + 1) k_end = pmax + 1;
+  const int nblk = static_cast<int>((k_end - k_begin + BN - 1) / BN);
 
-  // Absolute positions of this thread's two MMA rows (padding entries see key 0).
-  int64_t pos_ab[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int64_t m = m0 + warp * 16 + gq + i * 8;
-    pos_ab[i] = m < total_m ? a.positions[m / G] : 0;
-  }
-
-  // Q tile -> shared (cp.async group 0 together with the first K/V block).
-  for (int idx = tid; idx < BM * CPR; idx += THREADS) {
-    const int row = idx / CPR, c = idx - row * CPR;
-    const int64_t m = m0 + row;
-    const bool ok = m < total_m;
-    const int64_t r = ok ? m / G : 0;
-    const int g = ok ? static_cast<int>(m - r * G) : 0;
-    const uint16_t* src = a.q + ((r * a.hq + static_cast<int64_t>(h) * G + g) * D + c * 8);
-    cp_async16(smem_u32(sq + swz<D>(row, c)), ok ? src : a.q, ok);
-  }
-  const uint16_t* kbase = a.k + static_cast<int64_t>(h) * a.c_hs;
-  const uint16_t* vbase = a.v + static_cast<int64_t>(h) * a.c_hs;
-  auto load_kv = [&](int stage, int64_t key0) {
-    uint8_t* sk = skv + stage * 2 * TILE_BYTES;
-    uint8_t* sv = sk + TILE_BYTES;
-    for (int idx = tid; idx < BN * CPR; idx += THREADS) {
-      const int row = idx / CPR, c = idx - row * CPR;
-      const int64_t key = key0 + row;
-      const bool ok = key < k_end;
-      const int64_t off = ok ? key * a.c_rs + c * 8 : 0;
-      cp_async16(smem_u32(sk + swz<D>(row, c)), kbase + off, ok);
-      cp_async16(smem_u32(sv + swz<D>(row, c)), vbase + off, ok);
-    }
-  };
-  load_kv(0, k_begin);
-  cp_commit();
-
-  float o[D / 8][4];
-#pragma unroll
-  for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float mrow[2] = {-INFINITY, -INFINITY};
-  float lrow[2] = {0.f, 0.f};
-  uint32_t qf[D / 16][4];
-  bool have_q = false;
-
-  int stage = 0;
-  for (int64_t blk = k_begin; blk < k_end; blk += BN, stage ^= 1) {
-    const bool has_next = blk + BN < k_end;
-    if (has_next) {
-      load_kv(stage ^ 1, blk + BN);
-      cp_commit();
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
-    __syncthreads();
-    if (!have_q) {
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const int i = lane >> 3;
-        const int row = warp * 16 + (i & 1) * 8 + (lane & 7);
-        ldsm_x4(smem_u32(sq + swz<D>(row, kk * 2 + (i >> 1))), qf[kk][0], qf[kk][1], qf[kk][2],
-                qf[kk][3]);
-      }
-      have_q = true;
-    }
-    const uint8_t* sk = skv + stage * 2 * TILE_BYTES;
-    const uint8_t* sv = sk + TILE_BYTES;
-
-    // S = Q K^T for 64 keys: 8 n-tiles of 8 keys.
-    float s[BN / 8][4];
-#pragma unroll
-    for (int j = 0; j < BN / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-#pragma unroll
-      for (int jp = 0; jp < BN / 16; ++jp) {
-        const int i = lane >> 3;
-        const int key = (jp * 2 + (i >> 1)) * 8 + (lane & 7);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(smem_u32(sk + swz<D>(key, kk * 2 + (i & 1))), b0, b1, b2, b3);
-        mma16816<T>(s[jp * 2], qf[kk], b0, b1);
-        mma16816<T>(s[jp * 2 + 1], qf[kk], b2, b3);
-      }
-    }
-
-    // Scale, causal/chunk mask, online softmax (fp32, base-2).
-    const bool need_mask = blk + BN - 1 > pmin || blk + BN > k_end;
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int j = 0; j < BN / 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float x = s[j][e] * a.scale_log2;
-        if (need_mask) {
-          const int64_t key = blk + j * 8 + tq * 2 + (e & 1);
-          if (key > pos_ab[e >> 1] || key >= k_end) x = -INFINITY;
-        }
-        s[j][e] = x;
-        mx[e >> 1] = fmaxf(mx[e >> 1], x);
-      }
-    }
-    float alpha[2], base[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
-      const float mnew = fmaxf(mrow[i], mx[i]);
-      base[i] = mnew == -INFINITY ? 0.f : mnew;
-      alpha[i] = exp2f(mrow[i] - base[i]);
-      mrow[i] = mnew;
-      lrow[i] *= alpha[i];
-    }
-#pragma unroll
-    for (int n = 0; n < D / 8; ++n) {
-      o[n][0] *= alpha[0];
-      o[n][1] *= alpha[0];
-      o[n][2] *= alpha[1];
-      o[n][3] *= alpha[1];
-    }
-#pragma unroll
-    for (int j = 0; j < BN / 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float p = exp2f(s[j][e] - base[e >> 1]);
-        s[j][e] = p;
-        lrow[e >> 1] += p;
-      }
-    }
-
-    // O += P V with P = P_hi + P_lo.
-#pragma unroll
-    for (int kk = 0; kk < BN / 16; ++kk) {
-      uint32_t ph[4], pl[4];
-      const float* s0 = s[kk * 2];
-      const float* s1 = s[kk * 2 + 1];
-      const float src[8] = {s0[0], s0[1], s0[2], s0[3], s1[0], s1[1], s1[2], s1[3]};
-      float hi[8], lo[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        hi[e] = rnd<T>(src[e]);
-        lo[e] = src[e] - hi[e];
-      }
-      ph[0] = pack2<T>(hi[0], hi[1]);
-      ph[1] = pack2<T>(hi[2], hi[3]);
-      ph[2] = pack2<T>(hi[4], hi[5]);
-      ph[3] = pack2<T>(hi[6], hi[7]);
-      pl[0] = pack2<T>(lo[0], lo[1]);
-      pl[1] = pack2<T>(lo[2], lo[3]);
-      pl[2] = pack2<T>(lo[4], lo[5]);
-      pl[3] = pack2<T>(lo[6], lo[7]);
-#pragma unroll
-      for (int np = 0; np < D / 16; ++np) {
-        const int i = lane >> 3;
-        const int key = kk * 16 + (i & 1) * 8 + (lane & 7);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(smem_u32(sv + swz<D>(key, np * 2 + (i >> 1))), b0, b1, b2, b3);
-        mma16816<T>(o[np * 2], ph, b0, b1);
-        mma16816<T>(o[np * 2], pl, b0, b1);
-        mma16816<T>(o[np * 2 + 1], ph, b2, b3);
-        mma16816<T>(o[np * 2 + 1], pl, b2, b3);
-      }
-    }
-    __syncthreads();  // stage is refilled by the next iteration's prefetch
-  }
-
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 1);
-    lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 2);
-  }
-  if (a.nchunks == 1) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int64_t m = m0 + warp * 16 + gq + i * 8;
-      if (m >= total_m) continue;
-      const int64_t r = m / G;
-      const int g = static_cast<int>(m - r * G);
-      uint16_t* dst = a.out + (r * a.hq + static_cast<int64_t>(h) * G + g) * D;
-      const float inv = 1.0f / lrow[i];
-#pragma unroll
-      for (int n = 0; n < D / 8; ++n) {
-        const uint32_t pr = pack2<T>(o[n][i * 2] * inv, o[n][i * 2 + 1] * inv);
-        *reinterpret_cast<uint32_t*>(dst + n * 8 + tq * 2) = pr;
-      }
-    }
+  const uint32_t raw = sm100::smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  if (base - raw + L::USED > static_cast<uint32_t>(L::BYTES)) {  // uniform: every thread sees the same
+    if (tid == 0) atomicCAS(a.status, 0, ERR_SMEM_ALIGN);
     return;
   }
-  const int64_t w = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks + chunk;
-  float* wo = a.ws_o + w * BM * D;
-  float* wml = a.ws_ml + w * BM * 2;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + L::BAR_OFF;
+  const uint32_t q_full = bar0;
+  auto kv_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto kv_empty = [&](int s) { return bar0 + 8u * (1 + NS + s); };
+  auto s_full = [&](int b) { return bar0 + 8u * (1 + 2 * NS + b); };
+  auto s_free = [&](int b) { return bar0 + 8u * (3 + 2 * NS + b); };
+  auto p_full = [&](int pb) { return bar0 + 8u * (5 + 2 * NS + pb); };
+  auto pv_done = [&](int pb) { return bar0 + 8u * (5 + 2 * NS + NP + pb); };
+  const uint32_t drain = bar0 + 8u * (5 + 2 * NS + 2 * NP);
+  auto red_bar = [&](int b) { return bar0 + 8u * (6 + 2 * NS + 2 * NP + b); };  // b = 2: final sums
+  volatile int* abort = reinterpret_cast<volatile int*>(gbase + L::MISC_OFF);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L::MISC_OFF + 4);
+  float* red = reinterpret_cast<float*>(gbase + L::RED_OFF);  // [2 parities][2 halves][128 rows]
+  int* err = a.status;
+
+  if (tid == 0) {
+    *abort = 0;
+    sm100::mbar_init(q_full, kSoftmaxThreads);
+    for (int s = 0; s < NS; ++s) {
+      sm100::mbar_init(kv_full(s), 1);
+      sm100::mbar_init(kv_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(s_full(b), 1);
+      sm100::mbar_init(s_free(b), kSoftmaxThreads);
+    }
+    for (int pb = 0; pb < NP; ++pb) {
+      sm100::mbar_init(p_full(pb), kSoftmaxThreads);
+      sm100::mbar_init(pv_done(pb), 1);
+    }
+    sm100::mbar_init(drain, 1);
+    for (int b = 0; b < 3; ++b) sm100::mbar_init(red_bar(b), kSoftmaxThreads);
+    sm100::fence_barrier_init();
+  }
+  if (warp == kMmaWarp) {
+    sm100::tmem_alloc(sm100::smem_u32(tmem_slot), 512);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  constexpr uint32_t TM_O = 256;  // O accumulator columns; S buffers at 0 and 128
+
+  if (warp == kTmaWarp) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      sm100::prefetch_tmap(&tmap_k);
+      sm100::prefetch_tmap(&tmap_v);
+      int issued = 0;
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % NS;
+        if (j >= NS && !sm100::mbar_wait(kv_empty(s), ((j / NS) - 1) & 1, abort, err, ERR_KV_EMPTY, WAIT_LIMIT))
+          break;
+        sm100::mbar_arrive_expect_tx(kv_full(s), L::STAGE_TX);
+        const int key0 = static_cast<int>(k_begin + static_cast<int64_t>(j) * BN);
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int ml = warp * 16 + gq + i * 8;
+        for (int ds = 0; ds < DS; ++ds) {
+          sm100::tma_load_3d(base + L::K_OFF + (s * DS + ds) * SUB, &tmap_k, kv_full(s), ds * 64, key0, h);
+          sm100::tma_load_3d(base + L::V_OFF + (s * DS + ds) * SUB, &tmap_v, kv_full(s), ds * 64, key0, h);
+        }
+        issued = j + 1;
+      }
+      // Never leave the CTA while one of our copies may still land in shared memory.
+      if (*abort) {
+        volatile int keep_waiting = 0;
+        for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+          sm100::mbar_wait(kv_full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t IQK = sm100::idesc_f16(kBF16, BM, BN, false);
+      constexpr uint32_t IPV = sm100::idesc_f16(kBF16, BM, D, true);
+      bool ok = sm100::mbar_wait(q_full, 0, abort, err, ERR_Q_FULL, WAIT_LIMIT);
+      auto issue_qk = [&](int j) -> bool {
+        const int s = j % NS, b = j & 1;
+        if (!sm100::mbar_wait(kv_full(s), (j / NS) & 1, abort, err, ERR_KV_FULL, WAIT_LIMIT)) return false;
+        if (j >= 2 && !sm100::mbar_wait(s_free(b), ((j >> 1) - 1) & 1, abort, err, ERR_S_FREE, WAIT_LIMIT))
+          return false;
+        sm100::tc_fence_after();
 #pragma unroll
-    for (int n = 0; n < D / 8; ++n)
-      *reinterpret_cast<float2*>(wo + ml * D + n * 8 + tq * 2) = make_float2(o[n][i * 2], o[n][i * 2 + 1]);
-    if (tq == 0) *reinterpret_cast<float2*>(wml + ml * 2) = make_float2(mrow[i], lrow[i]);
+        for (int k = 0; k < D / 16; ++k) {
+          const int ds = k >> 2, kk = k & 3;
+          const uint64_t da = sm100::desc_sw128(base + L::Q_OFF + ds * SUB + kk * 32, 16, 1024);
+          const uint64_t db = sm100::desc_sw128(base + L::K_OFF + (s * DS + ds) * SUB + kk * 32, 16, 1024);
+          sm100::mma_f16_ss(tmem + b * BN, da, db, IQK, k > 0);
+        }
+        sm100::mma_commit(s_full(b));
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      for (int j = 0; ok && j < nblk; ++j) {
+        if (j + 1 < nblk && !issue_qk(j + 1)) break;
+        const int pb = j % NP;
+        if (!sm100::mbar_wait(p_full(pb), (j / NP) & 1, abort, err, ERR_P_FULL, WAIT_LIMIT)) break;
+        sm100::tc_fence_after();
+        const int s = j % NS;
+        const uint32_t pbase = base + L::P_OFF + pb * L::P_BYTES;
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k) {
+          const int ps = k >> 2, kk = k & 3;
+          // V block: MN-major (head_dim contiguous); 16 keys = two 8-row groups.
+          const uint64_t db = sm100::desc_sw128(base + L::V_OFF + s * DS * SUB + k * 2048, SUB, 1024);
+          const uint64_t da = sm100::desc_sw128(pbase + ps * SUB + kk * 32, 16, 1024);
+          sm100::mma_f16_ss(tmem + TM_O, da, db, IPV, (j > 0 || k > 0) ? 1u : 0u);
+          if constexpr (SPLIT) {
+            const uint64_t dl = sm100::desc_sw128(pbase + 2 * SUB + ps * SUB + kk * 32, 16, 1024);
+            sm100::mma_f16_ss(tmem + TM_O, dl, db, IPV, 1u);
+          }
+        }
+        sm100::mma_commit(pv_done(pb));
+        sm100::mma_commit(kv_empty(s));
+      }
+      // Nothing of ours may still be writing TMEM when it is freed.
+      sm100::mma_commit(drain);
+      volatile int keep_waiting = 0;
+      sm100::mbar_wait(drain, 0, &keep_waiting, err, ERR_DRAIN, WAIT_LIMIT);
+    }
+  } else {
+    // ------- softmax warps: thread (half, row) owns TMEM lane `row`, S/P columns
+    // [64*half, 64*half+64) and O columns [HD*half, HD*half+HD) -------
+    const int row = tid & (BM - 1);
+    const int half = tid >> 7;
+    const int64_t m_abs = m0 + row;
+    const bool valid = m_abs < total_m;
+    const int64_t r = valid ? m_abs / G : 0;
+    const int g = valid ? static_cast<int>(m_abs - r * G) : 0;
+    const int64_t pos = valid ? a.positions[r] : 0;  // padding rows see key 0 only
+    const uint16_t* qsrc = a.q + ((r * a.hq + static_cast<int64_t>(h) * G + g) * D);
+#pragma unroll
+    for (int c = half * (D / 16); c < (half + 1) * (D / 16); ++c)
+      cp_async16(base + L::Q_OFF + (c >> 3) * SUB + swz(row, c & 7), valid ? qsrc + c * 8 : a.q, valid);
+    asm volatile("cp.async.commit_group;\ncp.async.wait_all;\n" ::: "memory");
+    sm100::fence_proxy_async_smem();
+    sm100::mbar_arrive(q_full);
+
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t scol = static_cast<uint32_t>(half * 64);
+    const float sl2 = a.scale_log2;
+    float m_used = -INFINITY, lsum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int b = j & 1;
+      // Warp-uniform decisions: tcgen05.ld/st are .sync.aligned.
+      if (!__all_sync(0xffffffffu, sm100::mbar_wait(s_full(b), (j >> 1) & 1, abort, err, ERR_S_FULL, WAIT_LIMIT))) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      uint32_t sv[2][32];
+      sm100::tmem_ld32(tmem + lane_base + b * BN + scol, sv[0]);
+      sm100::tmem_ld32(tmem + lane_base + b * BN + scol + 32, sv[1]);
+      sm100::tmem_wait_ld();
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(s_free(b));
+
+      const int64_t key0 = k_begin + static_cast<int64_t>(j) * BN + half * 64;
+      // Visible columns of this half-block for this row: [0, lim).
+      const int64_t lim64 = (pos + 1 < k_end ? pos + 1 : k_end) - key0;
+      const int lim = lim64 < 0 ? 0 : (lim64 > 64 ? 64 : static_cast<int>(lim64));
+      float mx = -INFINITY;
+      if (lim == 64) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) mx = fmaxf(mx, __uint_as_float(sv[e >> 5][e & 31]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+          const float x = e < lim ? __uint_as_float(sv[e >> 5][e & 31]) : -INFINITY;
+          sv[e >> 5][e & 31] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      }
+      // Row max across the two halves (bounded mbarrier exchange, double-buffered).
+      red[(b * 2 + half) * BM + row] = mx;
+      sm100::mbar_arrive(red_bar(b));
+      if (!__all_sync(0xffffffffu, sm100::mbar_wait(red_bar(b), (j >> 1) & 1, abort, err, ERR_RED, WAIT_LIMIT))) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, red[(b * 2 + (half ^ 1)) * BM + row]);
+      const float m_new = fmaxf(m_used, mx * sl2);  // scale > 0: max commutes with scaling
+      const int pb = j % NP;
+      const bool rescale = m_used != -INFINITY && m_new > m_used + 8.0f;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O must be final up to block j-1 before it is rescaled in TMEM.
+        if (j > 0 && !__all_sync(0xffffffffu, sm100::mbar_wait(pv_done((j - 1) % NP), ((j - 1) / NP) & 1, abort,
+                                                                err, ERR_PV_DONE, WAIT_LIMIT))) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const float f = rescale ? ex2_approx(m_used - m_new) : 1.0f;
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t ov[32];
+          sm100::tmem_ld32(tmem + lane_base + TM_O + half * HD + c * 32, ov);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * f);
+          sm100::tmem_st32(tmem + lane_base + TM_O + half * HD + c * 32, ov);
+        }
+        sm100::tmem_wait_st();
+        if (rescale) {
+          lsum *= f;
+          m_used = m_new;
+        }
+      }
+      if (m_used == -INFINITY) m_used = m_new;  // first visible keys: this O row is still zero
+      const float neg_mb = m_used == -INFINITY ? 0.f : -m_used;
+      // P buffer pb is free once the P.V that last read it (block j - NP) is done.
+      if (j >= NP && !__all_sync(0xffffffffu, sm100::mbar_wait(pv_done(pb), ((j / NP) - 1) & 1, abort, err,
+                                                                ERR_PV_DONE, WAIT_LIMIT))) {
+        ok = false;
+        break;
+      }
+      uint8_t* pdst = gbase + L::P_OFF + pb * L::P_BYTES + half * SUB;  // this half's keys = sub-tile `half`
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 hi, lw;
+        if (c * 8 >= lim) {  // fully masked group: P = 0 without exp
+          hi = make_uint4(0, 0, 0, 0);
+          lw = hi;
+        } else {
+          float p[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            // 2^(s*scale*log2e - m); masked columns hold -inf and give 0.
+            p[e] = ex2_approx(fmaf(__uint_as_float(sv[c >> 2][(c & 3) * 8 + e]), sl2, neg_mb));
+            lsum += p[e];
+          }
+          hi.x = pack2_hw<T>(p[0], p[1]);
+          hi.y = pack2_hw<T>(p[2], p[3]);
+          hi.z = pack2_hw<T>(p[4], p[5]);
+          hi.w = pack2_hw<T>(p[6], p[7]);
+          if constexpr (SPLIT) {
+            lw.x = pack2_hw<T>(p[0] - lo_half<T>(hi.x), p[1] - hi_half<T>(hi.x));
+            lw.y = pack2_hw<T>(p[2] - lo_half<T>(hi.y), p[3] - hi_half<T>(hi.y));
+            lw.z = pack2_hw<T>(p[4] - lo_half<T>(hi.z), p[5] - hi_half<T>(hi.z));
+            lw.w = pack2_hw<T>(p[6] - lo_half<T>(hi.w), p[7] - hi_half<T>(hi.w));
+          }
+        }
+        const uint32_t off = swz(row, c);
+        *reinterpret_cast<uint4*>(pdst + off) = hi;
+        if constexpr (SPLIT) *reinterpret_cast<uint4*>(pdst + 2 * SUB + off) = lw;
+      }
+      sm100::fence_proxy_async_smem();
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(p_full(pb));
+    }
+    // Row sum across the halves, then the epilogue on this thread's O columns.
+    if (ok) {
+      // Parity nblk&1 was last read in block nblk-2; the partner has finished
+      // that read, since it has since arrived on the block nblk-1 exchange.
+      const int fb = nblk & 1;
+      red[(fb * 2 + half) * BM + row] = lsum;
+      sm100::mbar_arrive(red_bar(2));
+      ok = __all_sync(0xffffffffu, sm100::mbar_wait(red_bar(2), 0, abort, err, ERR_RED, WAIT_LIMIT));
+      if (ok) lsum += red[(fb * 2 + (half ^ 1)) * BM + row];
+    }
+    if (ok && __all_sync(0xffffffffu, sm100::mbar_wait(pv_done((nblk - 1) % NP), ((nblk - 1) / NP) & 1, abort,
+                                                       err, ERR_PV_DONE, WAIT_LIMIT))) {
+      sm100::tc_fence_after();
+      if (a.nchunks == 1) {
+        const float inv = 1.0f / lsum;
+        uint16_t* dst = a.out + (r * a.hq + static_cast<int64_t>(h) * G + g) * D + half * HD;
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t ov[32];
+          sm100::tmem_ld32(tmem + lane_base + TM_O + half * HD + c * 32, ov);
+          sm100::tmem_wait_ld();
+          if (valid) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack2<T>(__uint_as_float(ov[v * 8 + 0]) * inv, __uint_as_float(ov[v * 8 + 1]) * inv);
+              w.y = pack2<T>(__uint_as_float(ov[v * 8 + 2]) * inv, __uint_as_float(ov[v * 8 + 3]) * inv);
+              w.z = pack2<T>(__uint_as_float(ov[v * 8 + 4]) * inv, __uint_as_float(ov[v * 8 + 5]) * inv);
+              w.w = pack2<T>(__uint_as_float(ov[v * 8 + 6]) * inv, __uint_as_float(ov[v * 8 + 7]) * inv);
+              *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
+            }
+          }
+        }
+      } else {
+        const int64_t wu = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks + chunk;
+        float* wo = a.ws_o + (wu * BM + row) * D + half * HD;
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t ov[32];
+          sm100::tmem_ld32(tmem + lane_base + TM_O + half * HD + c * 32, ov);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            *reinterpret_cast<uint4*>(wo + c * 32 + v * 4) =
+                make_uint4(ov[v * 4], ov[v * 4 + 1], ov[v * 4 + 2], ov[v * 4 + 3]);
+        }
+        if (half == 0) *reinterpret_cast<float2*>(a.ws_ml + (wu * BM + row) * 2) = make_float2(m_used, lsum);
+      }
+    }
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
   }
 }
 
-// Merge the chunk partials of one (head, tile): O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
+// One warp per m-entry: O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
 template <class T, int D>
 __global__ void __launch_bounds__(256) attn_combine_kernel(Args a) {
+  constexpr int PER = D / 32;  // values per lane
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
-  const int tile = blockIdx.x;
+  const int64_t m_abs = static_cast<int64_t>(blockIdx.x) * 8 + warp;
   const int G = a.group;
   const int64_t total_m = a.rows * G;
-  const int64_t m0 = static_cast<int64_t>(tile) * BM;
-  int64_t r_last = (m0 + BM - 1) / G;
+  if (m_abs >= total_m) return;
+  const int tile = static_cast<int>(m_abs / BM);
+  const int row = static_cast<int>(m_abs - static_cast<int64_t>(tile) * BM);
+  int64_t r_last = (static_cast<int64_t>(tile) * BM + BM - 1) / G;
   if (r_last > a.rows - 1) r_last = a.rows - 1;
   const int64_t pmax = a.positions[r_last];
   int nv = static_cast<int>(pmax / a.chunk) + 1;
   if (nv > a.nchunks) nv = a.nchunks;
   const int64_t w0 = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks;
-  constexpr int VPR = D / 8;
-  for (int idx = threadIdx.x; idx < BM * VPR; idx += blockDim.x) {
-    const int ml = idx / VPR, v = idx - ml * VPR;
-    const int64_t m = m0 + ml;
-    if (m >= total_m) continue;
-    float M = -INFINITY;
-    for (int c = 0; c < nv; ++c) M = fmaxf(M, a.ws_ml[(w0 + c) * BM * 2 + ml * 2]);
-    float L = 0.f;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < nv; ++c) {
-      const float2 ml2 = *reinterpret_cast<const float2*>(a.ws_ml + (w0 + c) * BM * 2 + ml * 2);
-      const float wgt = exp2f(ml2.x - M);  // 0 for rows fully masked in chunk c
-      if (wgt == 0.f) continue;
-      L += wgt * ml2.y;
-      const float4* src = reinterpret_cast<const float4*>(a.ws_o + ((w0 + c) * BM + ml) * D + v * 8);
-      const float4 x0 = src[0], x1 = src[1];
-      acc[0] += wgt * x0.x; acc[1] += wgt * x0.y; acc[2] += wgt * x0.z; acc[3] += wgt * x0.w;
-      acc[4] += wgt * x1.x; acc[5] += wgt * x1.y; acc[6] += wgt * x1.z; acc[7] += wgt * x1.w;
-    }
-    const float inv = 1.0f / L;
-    const int64_t r = m / G;
-    const int g = static_cast<int>(m - r * G);
-    Vec8 out;
+  float M = -INFINITY;
+  for (int c = 0; c < nv; ++c) M = fmaxf(M, a.ws_ml[((w0 + c) * BM + row) * 2]);
+  float Lsum = 0.f, acc[PER];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) out.h[e] = T::from_f(acc[e] * inv);
-    st_vec8(a.out + (r * a.hq + static_cast<int64_t>(h) * G + g) * D + v * 8, out);
+  for (int e = 0; e < PER; ++e) acc[e] = 0.f;
+  for (int c = 0; c < nv; ++c) {
+    const float2 ml = *reinterpret_cast<const float2*>(a.ws_ml + ((w0 + c) * BM + row) * 2);
+    const float wgt = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+    if (wgt == 0.f) continue;
+    Lsum += wgt * ml.y;
+    const float* src = a.ws_o + ((w0 + c) * BM + row) * D + lane * PER;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) acc[e] += wgt * src[e];
   }
+  const float inv = 1.0f / Lsum;
+  const int64_t r = m_abs / G;
+  const int g = static_cast<int>(m_abs - r * G);
+  uint16_t* dst = a.out + (r * a.hq + static_cast<int64_t>(h) * G + g) * D + lane * PER;
+#pragma unroll
+  for (int e = 0; e < PER; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack2<T>(acc[e] * inv, acc[e + 1] * inv);
 }
 
 struct Plan {
   int tiles, nchunks;
   int64_t chunk;
+  int64_t max_chunks;  // upper bound on nchunks for any max_position up to this one
 };
 
 inline Plan make_plan(int64_t rows, int hq, int hkv, int64_t max_position) {
   Plan p;
-  const int group = hq / hkv;
-  const int64_t total_m = rows * group;
+  const int64_t total_m = rows * (hq / hkv);
   p.tiles = static_cast<int>((total_m + BM - 1) / BM);
   const int64_t keys = max_position + 1;
   const int64_t blocks = (keys + BN - 1) / BN;
   const int64_t base = static_cast<int64_t>(p.tiles) * hkv;
-  // Aim for >= 3 CTAs per SM (2 resident + tail) but keep >= 4 key blocks per chunk.
-  const int64_t target = static_cast<int64_t>(kNumSMs) * 3;
+  // One CTA per SM: ~1.5 waves of chunks, >= 4 key blocks each so the
+  // per-CTA prologue (TMEM, barriers, Q tile) is amortised.
+  const int64_t target = static_cast<int64_t>(kNumSMs) * 3 / 2;
   int64_t n = (target + base - 1) / base;
-  int64_t max_n = (blocks + 3) / 4;
+  const int64_t max_n = (blocks + 3) / 4;
   if (n > max_n) n = max_n;
   if (n < 1) n = 1;
-  const int64_t chunk_blocks = (blocks + n - 1) / n;
-  p.chunk = chunk_blocks * BN;
-  p.nchunks = static_cast<int>((keys + p.chunk - 1) / p.chunk);
+  p.chunk = ((blocks + n - 1) / n) * BN;
+  p.nchunks = static_cast<int>((keys + p.chunk - 1) / p.chunk);  // <= n
+  p.max_chunks = n;  // n only grows with max_position, so it bounds every smaller plan
   return p;
 }
 
-inline size_t workspace_bytes(const Plan& p, int hkv, int head_dim) {
-  if (p.nchunks <= 1) return 0;
-  const size_t units = static_cast<size_t>(hkv) * p.tiles * p.nchunks;
-  return units * BM * (head_dim + 2) * sizeof(float) + 256;
+// Partials are laid out with `stride_chunks` chunk slots per (head, tile).
+inline size_t workspace_bytes(int tiles, int64_t chunks, int hkv, int head_dim) {
+  size_t bytes = STATUS_BYTES;
+  if (chunks > 1) {
+    const size_t units = static_cast<size_t>(hkv) * tiles * chunks;
+    bytes += units * BM * (head_dim + 2) * sizeof(float);
+  }
+  return bytes;
 }
 
-template <class T, int D>
-int launch(const Args& a, cudaStream_t s) {
-  const int smem = BM * D * 2 + 2 * 2 * BN * D * 2;
-  // The shared-memory opt-in is a per-device function attribute: set it once
-  // per device (one process drives one GPU, but a process may see several).
+// ------------------------------------------------------------------ host side
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+inline EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  }
+  return fn;
+}
+
+// [kv_heads][cache_rows][D] with element strides (head, row); box 64 x 128 x 1.
+inline bool make_kv_map(CUtensorMap* map, const void* ptr, bool bf16, int head_dim, int64_t rows,
+                        int kv_heads, int64_t hs, int64_t rs) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(kv_heads)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(rs) * 2, static_cast<cuuint64_t>(hs) * 2};
+  cuuint32_t box[3] = {64, BN, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <class T, int D, bool SPLIT>
+int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Args& a, cudaStream_t s) {
+  constexpr int smem = Layout<D, SPLIT>::BYTES;
   static int configured[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -417,18 +601,24 @@ int launch(const Args& a, cudaStream_t s) {
     return KVR_ERR_CUDA;
   }
   if (dev < 0 || dev >= 64 || !__atomic_load_n(&configured[dev], __ATOMIC_ACQUIRE)) {
-    e = cudaFuncSetAttribute(attn_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = cudaFuncSetAttribute(attn_tc_kernel<T, D, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
       set_last_cuda_error(e);
       return KVR_ERR_CUDA;
     }
     if (dev >= 0 && dev < 64) __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
   }
+  e = cudaMemsetAsync(a.status, 0, sizeof(int), s);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return KVR_ERR_CUDA;
+  }
   dim3 grid(a.tiles * a.nchunks, a.hkv);
-  attn_kernel<T, D><<<grid, THREADS, smem, s>>>(a);
+  attn_tc_kernel<T, D, SPLIT><<<grid, THREADS, smem, s>>>(mk, mv, a);
   int st = check_launch();
   if (st != KVR_OK || a.nchunks == 1) return st;
-  attn_combine_kernel<T, D><<<dim3(a.tiles, a.hkv), 256, 0, s>>>(a);
+  const int64_t total_m = a.rows * a.group;
+  attn_combine_kernel<T, D><<<dim3(static_cast<unsigned>((total_m + 7) / 8), a.hkv), 256, 0, s>>>(a);
   return check_launch();
 }
 
@@ -442,18 +632,20 @@ extern "C" {
 size_t kvr_attention_workspace_size(int64_t rows, int q_heads, int kv_heads, int head_dim,
                                     int64_t cache_rows) {
   if (rows <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads || cache_rows <= 0)
-    return 0;
+    return attn::STATUS_BYTES;
   attn::Plan p = attn::make_plan(rows, q_heads, kv_heads, cache_rows - 1);
-  return attn::workspace_bytes(p, kv_heads, head_dim);
+  return attn::workspace_bytes(p.tiles, p.max_chunks, kv_heads, head_dim);
 }
 
 int kvr_selected_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
                            const int64_t* positions, int64_t rows, int q_heads, int kv_heads,
                            int head_dim, int64_t cache_rows, int64_t cache_head_stride,
                            int64_t cache_row_stride, int64_t max_position, float scale,
-                           void* workspace, size_t workspace_bytes, int dtype, void* stream) {
+                           int precision, void* workspace, size_t workspace_bytes, int dtype,
+                           void* stream) {
   if (dtype != KVR_DTYPE_BF16 && dtype != KVR_DTYPE_F16) return KVR_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return KVR_ERR_UNSUPPORTED;
+  if (precision != KVR_ATTN_P_SPLIT && precision != KVR_ATTN_P_ROUNDED) return KVR_ERR_INVALID_ARG;
   if (rows < 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads || cache_rows < 0)
     return KVR_ERR_INVALID_ARG;
   if (rows == 0) return KVR_OK;
@@ -461,36 +653,44 @@ int kvr_selected_attention(const void* q, const void* k_cache, const void* v_cac
       !aligned16(v_cache) || !aligned16(out) || cache_head_stride % 8 || cache_row_stride % 8)
     return KVR_ERR_INVALID_ARG;
   if (max_position < 0 || max_position >= cache_rows || !(scale == scale)) return KVR_ERR_INVALID_ARG;
+  if (cache_rows > 0x7fffffffLL || kv_heads > 65535) return KVR_ERR_UNSUPPORTED;
   attn::Plan p = attn::make_plan(rows, q_heads, kv_heads, max_position);
-  if (static_cast<int64_t>(p.tiles) * p.nchunks > 0x7fffffff || kv_heads > 65535)
+  if (static_cast<int64_t>(p.tiles) * p.nchunks > 0x7fffffff) return KVR_ERR_UNSUPPORTED;
+  const size_t need = attn::workspace_bytes(p.tiles, p.nchunks, kv_heads, head_dim);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace)) return KVR_ERR_INVALID_ARG;
+  const bool bf16 = dtype == KVR_DTYPE_BF16;
+  CUtensorMap mk, mv;
+  if (!attn::make_kv_map(&mk, k_cache, bf16, head_dim, cache_rows, kv_heads, cache_head_stride,
+                         cache_row_stride) ||
+      !attn::make_kv_map(&mv, v_cache, bf16, head_dim, cache_rows, kv_heads, cache_head_stride,
+                         cache_row_stride))
     return KVR_ERR_UNSUPPORTED;
-  const size_t need = attn::workspace_bytes(p, kv_heads, head_dim);
-  if (need && (!workspace || workspace_bytes < need || !aligned16(workspace)))
-    return KVR_ERR_INVALID_ARG;
   attn::Args a;
   a.q = static_cast<const uint16_t*>(q);
-  a.k = static_cast<const uint16_t*>(k_cache);
-  a.v = static_cast<const uint16_t*>(v_cache);
   a.out = static_cast<uint16_t*>(out);
   a.positions = positions;
   a.rows = rows;
   a.hq = q_heads;
   a.hkv = kv_heads;
   a.group = q_heads / kv_heads;
-  a.cache_rows = cache_rows;
-  a.c_hs = cache_head_stride;
-  a.c_rs = cache_row_stride;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.tiles = p.tiles;
   a.nchunks = p.nchunks;
   a.chunk = p.chunk;
+  a.status = static_cast<int*>(workspace);
+  a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + attn::STATUS_BYTES);
   const size_t units = static_cast<size_t>(kv_heads) * p.tiles * p.nchunks;
-  a.ws_o = static_cast<float*>(workspace);
-  a.ws_ml = need ? a.ws_o + units * attn::BM * head_dim : nullptr;
+  a.ws_ml = a.ws_o + units * attn::BM * head_dim;
   auto s = static_cast<cudaStream_t>(stream);
-  if (dtype == KVR_DTYPE_BF16)
-    return head_dim == 128 ? attn::launch<BF16, 128>(a, s) : attn::launch<BF16, 64>(a, s);
-  return head_dim == 128 ? attn::launch<F16, 128>(a, s) : attn::launch<F16, 64>(a, s);
+  const bool split = precision == KVR_ATTN_P_SPLIT;
+  if (bf16) {
+    if (head_dim == 128)
+      return split ? attn::launch<BF16, 128, true>(mk, mv, a, s) : attn::launch<BF16, 128, false>(mk, mv, a, s);
+    return split ? attn::launch<BF16, 64, true>(mk, mv, a, s) : attn::launch<BF16, 64, false>(mk, mv, a, s);
+  }
+  if (head_dim == 128)
+    return split ? attn::launch<F16, 128, true>(mk, mv, a, s) : attn::launch<F16, 128, false>(mk, mv, a, s);
+  return split ? attn::launch<F16, 64, true>(mk, mv, a, s) : attn::launch<F16, 64, false>(mk, mv, a, s);
 }
 
 }  // extern "C"

@@ -139,7 +139,9 @@ template <class T, int D>
 __global__ void __launch_bounds__(256) shift_cache_kernel(ShiftPtrs ptrs, ShiftArgs a,
                                                           const uint16_t* __restrict__ cos_sin) {
   __shared__ float cs[2 * D];
-  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) cs[i] = T::to_f(cos_sin[i]);
+  // The table is only passed (non-null) when the tail is rotated.
+  if (a.apply_rope)
+    for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) cs[i] = T::to_f(cos_sin[i]);
   __syncthreads();
   const int seg = blockIdx.y;
   const int comp = seg & 1;

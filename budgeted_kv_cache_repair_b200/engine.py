@@ -95,6 +95,10 @@ class ModelView:
 
 _views: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
 
+# Probabilities enter P.V as P_hi + P_lo (close to fp32 P, as the reference's
+# own indexed kernel keeps them); ATTN_P_ROUNDED rounds P once like fused SDPA.
+ATTENTION_PRECISION = _lib.ATTN_P_SPLIT
+
 
 class KernelTimer:
     """Optional CUDA-event brackets around named launches on the current stream.
@@ -212,7 +216,7 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
         token = _timer.start("selected_attention") if _timer else None
         _lib.check(lib.kvr_selected_attention(
             ws.q_rot.data_ptr(), key.data_ptr(), value.data_ptr(), ws.attn.data_ptr(), pos_ptr, rows,
-            view.heads, view.kv_heads, D, cache_rows, c_hs, c_rs, max_position, scale,
+            view.heads, view.kv_heads, D, cache_rows, c_hs, c_rs, max_position, scale, ATTENTION_PRECISION,
             ws.attn_ws.data_ptr(), ws.attn_ws.numel(), dt, stream), "selected_attention")
         if token:
             _timer.stop(token)

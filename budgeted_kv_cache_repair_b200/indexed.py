@@ -117,7 +117,7 @@ def indexed_causal_attention(q, k, v, device_plan, scale=None):
         _lib.check(lib.kvr_selected_attention(
             packed_q.data_ptr(), kk.data_ptr(), vv.data_ptr(), packed_out.data_ptr(),
             device_plan.positions.data_ptr(), rows, heads, kv_heads, dim, length, kk.stride(1), kk.stride(2),
-            device_plan.host_plan.max_position, float(scale), workspace.data_ptr(), workspace.numel(),
+            device_plan.host_plan.max_position, float(scale), _lib.ATTN_P_SPLIT, workspace.data_ptr(), workspace.numel(),
             _lib.dtype_code(q.dtype), _lib.stream_handle(q.device)), "selected_attention")
         output.copy_(packed_out.transpose(0, 1).unsqueeze(0))
     return output

@@ -162,29 +162,37 @@ KVR_API int kvr_silu_mul(const void* gate, const void* up, void* out, int64_t ro
                  int dtype, void* stream);
 
 /*
- * Selected-query absolute-causal attention with GQA, on sm_100a tensor cores.
+ * Selected-query absolute-causal attention with GQA on sm_100a tensor cores
+ * (tcgen05 MMA with TMEM accumulators, TMA-fed K/V).
  * q [rows, q_heads, D] contiguous; K/V [kv_heads, cache_rows, D] with strides;
  * out [rows, q_heads, D] contiguous. Row r attends keys 0..positions[r]
  * (inclusive); positions must be strictly increasing (as IndexedPlan
- * guarantees). Query head j reads KV head j / (q_heads / kv_heads).
- * softmax(scale * q.k) in fp32, one rounding on output.
+ * guarantees) and max_position must equal positions[rows-1]. Query head j
+ * reads KV head j / (q_heads / kv_heads). softmax(scale * q.k) in fp32, one
+ * rounding on output. `precision` selects how probabilities enter the P.V
+ * product: KVR_ATTN_P_SPLIT (P = P_hi + P_lo in the element type, ~16
+ * mantissa bits) or KVR_ATTN_P_ROUNDED (one rounding, as fused SDPA kernels do).
  * Replaces _packed_attention's SDPA call with its dense [1,1,B,N] mask and
  * repeat_kv (kernels/packed_cache.py:47-67, 203-207) and the experimental
  * indexed_causal_attention (kernels/indexed_attention.py:207-241).
  *
- * The key range is split across CTAs when rows are few; partial results go
- * to `workspace` (device memory of at least kvr_attention_workspace_size()
- * bytes, any contents) and a second launch combines them. Both launches are
- * on `stream`; the workspace must not be shared by overlapping calls.
+ * `workspace` is device memory of at least kvr_attention_workspace_size()
+ * bytes (any contents). Its first 4 bytes receive a status word: 0, or the
+ * code of a bounded device-side wait that gave up (then the output is not
+ * valid). When rows are few the key range is split across CTAs and partial
+ * results go to the rest of the workspace, merged by a second launch on the
+ * same stream. Calls that overlap on the GPU must not share a workspace.
  */
+#define KVR_ATTN_P_SPLIT 0
+#define KVR_ATTN_P_ROUNDED 1
 KVR_API size_t kvr_attention_workspace_size(int64_t rows, int q_heads, int kv_heads, int head_dim,
-                                    int64_t cache_rows);
+                                            int64_t cache_rows);
 KVR_API int kvr_selected_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
-                           const int64_t* positions, int64_t rows, int q_heads, int kv_heads,
-                           int head_dim, int64_t cache_rows,
-                           int64_t cache_head_stride, int64_t cache_row_stride,
-                           int64_t max_position, float scale,
-                           void* workspace, size_t workspace_bytes, int dtype, void* stream);
+                                   const int64_t* positions, int64_t rows, int q_heads, int kv_heads,
+                                   int head_dim, int64_t cache_rows,
+                                   int64_t cache_head_stride, int64_t cache_row_stride,
+                                   int64_t max_position, float scale, int precision,
+                                   void* workspace, size_t workspace_bytes, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -289,3 +289,28 @@ def test_row_kernels_match_torch_rounding(lib):
     ref = torch.nn.functional.silu(gate) * up
     assert (act.float() - ref.float()).abs().max() <= 2 ** -7 * ref.float().abs().max()
     assert (act == ref).float().mean() > 0.99
+
+
+@pytest.mark.parametrize("precision", [0, 1])
+@pytest.mark.parametrize("dim,heads,kv_heads,count,length", [(128, 32, 8, 64, 7936), (64, 8, 2, 300, 2000),
+                                                              (128, 8, 8, 5, 130), (128, 64, 8, 129, 3001)])
+def test_attention_c_abi_status_word_and_precision_modes(lib, precision, dim, heads, kv_heads, count, length):
+    """Direct C-ABI call: the workspace status word stays 0 and both P modes meet the fp64 oracle."""
+    L = lib.load()
+    torch.manual_seed(count + dim)
+    positions = sorted(torch.randperm(length)[:count].tolist())
+    pos = torch.tensor(positions, device=DEV)
+    q = (torch.randn(count, heads, dim, device=DEV) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(1, kv_heads, length, dim, device=DEV) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(1, kv_heads, length, dim, device=DEV) * 0.5).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    ws_bytes = L.kvr_attention_workspace_size(count, heads, kv_heads, dim, length)
+    ws = torch.full((ws_bytes,), 0xFF, dtype=torch.uint8, device=DEV)
+    lib.check(L.kvr_selected_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), pos.data_ptr(),
+                                       count, heads, kv_heads, dim, length, length * dim, dim, positions[-1],
+                                       dim ** -0.5, precision, ws.data_ptr(), ws_bytes, 0, lib.stream_handle()),
+              "attention")
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32).item()) == 0
+    expected = oracle.selected_attention_fp64(q.permute(1, 0, 2)[None].cpu(), k.cpu(), v.cpu(), positions)
+    _assert_attention_close(out.permute(1, 0, 2)[None], expected)

@@ -44,13 +44,15 @@ def test_native_argument_checks_run_without_a_gpu(built):
     lib = _lib.load()
     assert lib.kvr_copy_layers(None, None, 1, 1, 1, 8, 8, 8, 8, 8, 0, None) == _lib.ERR_INVALID_ARG
     assert lib.kvr_rope_shift_layers(None, None, 1, 1, 1, 96, 96, 96, 96, 96, None, 0, None) == _lib.ERR_UNSUPPORTED
-    assert lib.kvr_selected_attention(None, None, None, None, None, 4, 3, 2, 128, 10, 1280, 128, 3, 1.0, None, 0, 0,
-                                      None) == _lib.ERR_INVALID_ARG
+    assert lib.kvr_selected_attention(None, None, None, None, None, 4, 3, 2, 128, 10, 1280, 128, 3, 1.0, 0, None, 0,
+                                      0, None) == _lib.ERR_INVALID_ARG
+    assert lib.kvr_selected_attention(None, None, None, None, None, 4, 4, 2, 128, 10, 1280, 128, 3, 1.0, 7, None, 0,
+                                      0, None) == _lib.ERR_INVALID_ARG
     assert lib.kvr_silu_mul(None, None, None, 0, 16, 16, 16, 16, 7, None) == _lib.ERR_UNSUPPORTED
     # Empty work is a no-op success.
     assert lib.kvr_scatter_rows(None, None, None, None, None, 0, 1, 64, 9, 0, 0, 0, 0, None, 0, None) == _lib.OK
     assert lib.kvr_attention_workspace_size(64, 32, 8, 128, 7936) > 0
-    assert lib.kvr_attention_workspace_size(5000, 32, 8, 128, 7936) == 0  # enough tiles: no split
+    assert lib.kvr_attention_workspace_size(20000, 32, 8, 128, 7936) == 256  # enough tiles: status word only
 
 
 def test_alignment_matches_reference():
