@@ -65,6 +65,7 @@ struct Args {
   int tiles, nchunks;
   int64_t chunk;  // keys per chunk (multiple of BN)
   int* status;    // workspace status word (error code, 0 = ok)
+  int q_by_tma;   // Q tile fetched by TMA (128 % group == 0) or by cp.async
   float* ws_o;    // [hkv][tiles][nchunks][BM][D] unnormalised O
   float* ws_ml;   // [hkv][tiles][nchunks][BM][2] (running max, sum)
 };
@@ -83,11 +84,11 @@ struct Layout {
   static constexpr int P_BYTES = (SPLIT ? 4 : 2) * SUB;  // hi (+ lo) halves, 2 sub-tiles each
   static constexpr int P_OFF = V_OFF + NS * DS * SUB;
   static constexpr int BAR_OFF = P_OFF + NP * P_BYTES;
-  // q_full, kv_full[NS], kv_empty[NS], s_full[2], s_free[2], p_full[NP], pv_done[NP], drain, red_bar[3]
-  static constexpr int NBAR = 1 + 2 * NS + 4 + 2 * NP + 1 + 3;
+  // q_full, kv_full[NS], kv_empty[NS], s_full[2], s_free[2], p_full[NP], pv_done[NP], drain, red_bar
+  static constexpr int NBAR = 1 + 2 * NS + 4 + 2 * NP + 1 + 1;
   static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;
-  static constexpr int RED_OFF = MISC_OFF + 16;  // float [2 parities][2 halves][128 rows] max/sum exchange
-  static constexpr int USED = RED_OFF + 2 * 2 * BM * 4;
+  static constexpr int RED_OFF = MISC_OFF + 16;  // float [2 halves][128 rows][max, sum]
+  static constexpr int USED = RED_OFF + 2 * BM * 2 * 4;
   // Swizzled tiles need a 1 KB-aligned base; the allocation carries what slack
   // fits under the per-CTA limit and the kernel checks it at run time.
   static constexpr int BYTES = USED + 1024 <= 232448 ? USED + 1024 : 232448;
@@ -142,10 +143,10 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
 template <class T, int D, bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                   Args a) {
+                   const __grid_constant__ CUtensorMap tmap_q, Args a) {
   using L = Layout<D, SPLIT>;
   constexpr int DS = L::DS, NS = L::NS, NP = L::NP;
-  constexpr int HD = D / 2;  // O columns per softmax thread
+  constexpr int HD = D / 2;  // output columns per softmax thread in the epilogue
   constexpr bool kBF16 = std::is_same<T, BF16>::value;
   extern __shared__ uint8_t smem_raw[];
 
@@ -181,15 +182,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto p_full = [&](int pb) { return bar0 + 8u * (5 + 2 * NS + pb); };
   auto pv_done = [&](int pb) { return bar0 + 8u * (5 + 2 * NS + NP + pb); };
   const uint32_t drain = bar0 + 8u * (5 + 2 * NS + 2 * NP);
-  auto red_bar = [&](int b) { return bar0 + 8u * (6 + 2 * NS + 2 * NP + b); };  // b = 2: final sums
+  const uint32_t red_bar = bar0 + 8u * (6 + 2 * NS + 2 * NP);
   volatile int* abort = reinterpret_cast<volatile int*>(gbase + L::MISC_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L::MISC_OFF + 4);
-  float* red = reinterpret_cast<float*>(gbase + L::RED_OFF);  // [2 parities][2 halves][128 rows]
+  float* red = reinterpret_cast<float*>(gbase + L::RED_OFF);  // [2 halves][128 rows][max, sum]
   int* err = a.status;
 
   if (tid == 0) {
     *abort = 0;
-    sm100::mbar_init(q_full, kSoftmaxThreads);
+    sm100::mbar_init(q_full, a.q_by_tma ? 1 : kSoftmaxThreads);
     for (int s = 0; s < NS; ++s) {
       sm100::mbar_init(kv_full(s), 1);
       sm100::mbar_init(kv_empty(s), 1);
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       sm100::mbar_init(pv_done(pb), 1);
     }
     sm100::mbar_init(drain, 1);
-    for (int b = 0; b < 3; ++b) sm100::mbar_init(red_bar(b), kSoftmaxThreads);
+    sm100::mbar_init(red_bar, kSoftmaxThreads);
     sm100::fence_barrier_init();
   }
   if (warp == kMmaWarp) {
@@ -214,13 +215,24 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
-  constexpr uint32_t TM_O = 256;  // O accumulator columns; S buffers at 0 and 128
+  // TMEM columns: S buffers [0,128) and [128,256); one O accumulator per key
+  // half, [256, 256+D) and [256+D, 256+2D).
+  constexpr uint32_t TM_O = 256;
 
   if (warp == kTmaWarp) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       sm100::prefetch_tmap(&tmap_k);
       sm100::prefetch_tmap(&tmap_v);
+      if (a.q_by_tma) {
+        // The tile's 128 m-entries are 128/G consecutive rows x the G heads of
+        // KV head h: one box per 64-column half of head_dim.
+        sm100::mbar_arrive_expect_tx(q_full, DS * SUB);
+#pragma unroll
+        for (int ds = 0; ds < DS; ++ds)
+          sm100::tma_load_3d(base + L::Q_OFF + ds * SUB, &tmap_q, q_full, ds * 64, h * G,
+                             static_cast<int>(m0 / G));
+      }
       int issued = 0;
       for (int j = 0; j < nblk; ++j) {
         const int s = j % NS;
@@ -238,6 +250,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Never leave the CTA while one of our copies may still land in shared memory.
       if (*abort) {
         volatile int keep_waiting = 0;
+        if (a.q_by_tma) sm100::mbar_wait(q_full, 0, &keep_waiting, nullptr, 0, WAIT_LIMIT);
         for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
           sm100::mbar_wait(kv_full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
       }
@@ -273,15 +286,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int s = j % NS;
         const uint32_t pbase = base + L::P_OFF + pb * L::P_BYTES;
 #pragma unroll
-        for (int k = 0; k < BN / 16; ++k) {
-          const int ps = k >> 2, kk = k & 3;
-          // V block: MN-major (head_dim contiguous); 16 keys = two 8-row groups.
-          const uint64_t db = sm100::desc_sw128(base + L::V_OFF + s * DS * SUB + k * 2048, SUB, 1024);
-          const uint64_t da = sm100::desc_sw128(pbase + ps * SUB + kk * 32, 16, 1024);
-          sm100::mma_f16_ss(tmem + TM_O, da, db, IPV, (j > 0 || k > 0) ? 1u : 0u);
-          if constexpr (SPLIT) {
-            const uint64_t dl = sm100::desc_sw128(pbase + 2 * SUB + ps * SUB + kk * 32, 16, 1024);
-            sm100::mma_f16_ss(tmem + TM_O, dl, db, IPV, 1u);
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {  // 16 keys per MMA, 64 keys per half
+            // V block: MN-major (head_dim contiguous); 16 keys = two 8-row groups.
+            const uint64_t db =
+                sm100::desc_sw128(base + L::V_OFF + s * DS * SUB + (half * 4 + k) * 2048, SUB, 1024);
+            const uint64_t da = sm100::desc_sw128(pbase + half * SUB + k * 32, 16, 1024);
+            const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+            sm100::mma_f16_ss(tmem + TM_O + half * D, da, db, IPV, acc);
+            if constexpr (SPLIT) {
+              const uint64_t dl = sm100::desc_sw128(pbase + 2 * SUB + half * SUB + k * 32, 16, 1024);
+              sm100::mma_f16_ss(tmem + TM_O + half * D, dl, db, IPV, 1u);
+            }
           }
         }
         sm100::mma_commit(pv_done(pb));
@@ -293,8 +310,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       sm100::mbar_wait(drain, 0, &keep_waiting, err, ERR_DRAIN, WAIT_LIMIT);
     }
   } else {
-    // ------- softmax warps: thread (half, row) owns TMEM lane `row`, S/P columns
-    // [64*half, 64*half+64) and O columns [HD*half, HD*half+HD) -------
+    // ------- softmax warps: thread (half, row) owns TMEM lane `row` and the keys
+    // [64*half, 64*half+64) of every block, with its own running max, sum and O
+    // accumulator (merged with the other half once, in the epilogue) -------
     const int row = tid & (BM - 1);
     const int half = tid >> 7;
     const int64_t m_abs = m0 + row;
@@ -302,16 +320,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int64_t r = valid ? m_abs / G : 0;
     const int g = valid ? static_cast<int>(m_abs - r * G) : 0;
     const int64_t pos = valid ? a.positions[r] : 0;  // padding rows see key 0 only
-    const uint16_t* qsrc = a.q + ((r * a.hq + static_cast<int64_t>(h) * G + g) * D);
+    if (!a.q_by_tma) {
+      const uint16_t* qsrc = a.q + ((r * a.hq + static_cast<int64_t>(h) * G + g) * D);
 #pragma unroll
-    for (int c = half * (D / 16); c < (half + 1) * (D / 16); ++c)
-      cp_async16(base + L::Q_OFF + (c >> 3) * SUB + swz(row, c & 7), valid ? qsrc + c * 8 : a.q, valid);
-    asm volatile("cp.async.commit_group;\ncp.async.wait_all;\n" ::: "memory");
-    sm100::fence_proxy_async_smem();
-    sm100::mbar_arrive(q_full);
+      for (int c = half * (D / 16); c < (half + 1) * (D / 16); ++c)
+        cp_async16(base + L::Q_OFF + (c >> 3) * SUB + swz(row, c & 7), valid ? qsrc + c * 8 : a.q, valid);
+      asm volatile("cp.async.commit_group;\ncp.async.wait_all;\n" ::: "memory");
+      sm100::fence_proxy_async_smem();
+      sm100::mbar_arrive(q_full);
+    }
 
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t scol = static_cast<uint32_t>(half * 64);
+    const uint32_t ocol = TM_O + static_cast<uint32_t>(half * D);
     const float sl2 = a.scale_log2;
     float m_used = -INFINITY, lsum = 0.f;
     bool ok = true;
@@ -334,31 +355,28 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Visible columns of this half-block for this row: [0, lim).
       const int64_t lim64 = (pos + 1 < k_end ? pos + 1 : k_end) - key0;
       const int lim = lim64 < 0 ? 0 : (lim64 > 64 ? 64 : static_cast<int>(lim64));
-      float mx = -INFINITY;
+      // Eight independent max chains (no 64-deep dependency).
+      float mx8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
       if (lim == 64) {
 #pragma unroll
-        for (int e = 0; e < 64; ++e) mx = fmaxf(mx, __uint_as_float(sv[e >> 5][e & 31]));
+        for (int e = 0; e < 64; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sv[e >> 5][e & 31]));
       } else {
 #pragma unroll
         for (int e = 0; e < 64; ++e) {
           const float x = e < lim ? __uint_as_float(sv[e >> 5][e & 31]) : -INFINITY;
           sv[e >> 5][e & 31] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+          mx8[e & 7] = fmaxf(mx8[e & 7], x);
         }
       }
-      // Row max across the two halves (bounded mbarrier exchange, double-buffered).
-      red[(b * 2 + half) * BM + row] = mx;
-      sm100::mbar_arrive(red_bar(b));
-      if (!__all_sync(0xffffffffu, sm100::mbar_wait(red_bar(b), (j >> 1) & 1, abort, err, ERR_RED, WAIT_LIMIT))) {
-        ok = false;
-        break;
-      }
-      mx = fmaxf(mx, red[(b * 2 + (half ^ 1)) * BM + row]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_new = fmaxf(m_used, mx * sl2);  // scale > 0: max commutes with scaling
       const int pb = j % NP;
       const bool rescale = m_used != -INFINITY && m_new > m_used + 8.0f;
       if (__any_sync(0xffffffffu, rescale)) {
-        // O must be final up to block j-1 before it is rescaled in TMEM.
+        // This half's O must be final up to block j-1 before it is rescaled in TMEM.
         if (j > 0 && !__all_sync(0xffffffffu, sm100::mbar_wait(pv_done((j - 1) % NP), ((j - 1) / NP) & 1, abort,
                                                                 err, ERR_PV_DONE, WAIT_LIMIT))) {
           ok = false;
@@ -367,13 +385,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         sm100::tc_fence_after();
         const float f = rescale ? ex2_approx(m_used - m_new) : 1.0f;
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
+        for (int c = 0; c < D / 32; ++c) {
           uint32_t ov[32];
-          sm100::tmem_ld32(tmem + lane_base + TM_O + half * HD + c * 32, ov);
+          sm100::tmem_ld32(tmem + lane_base + ocol + c * 32, ov);
           sm100::tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * f);
-          sm100::tmem_st32(tmem + lane_base + TM_O + half * HD + c * 32, ov);
+          sm100::tmem_st32(tmem + lane_base + ocol + c * 32, ov);
         }
         sm100::tmem_wait_st();
         if (rescale) {
@@ -390,6 +408,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       uint8_t* pdst = gbase + L::P_OFF + pb * L::P_BYTES + half * SUB;  // this half's keys = sub-tile `half`
+      float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent sum chains
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint4 hi, lw;
@@ -402,7 +421,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int e = 0; e < 8; ++e) {
             // 2^(s*scale*log2e - m); masked columns hold -inf and give 0.
             p[e] = ex2_approx(fmaf(__uint_as_float(sv[c >> 2][(c & 3) * 8 + e]), sl2, neg_mb));
-            lsum += p[e];
+            ls8[e] += p[e];
           }
           hi.x = pack2_hw<T>(p[0], p[1]);
           hi.y = pack2_hw<T>(p[2], p[3]);
@@ -419,58 +438,69 @@ __global__ void __launch_bounds__(THREADS, 1)
         *reinterpret_cast<uint4*>(pdst + off) = hi;
         if constexpr (SPLIT) *reinterpret_cast<uint4*>(pdst + 2 * SUB + off) = lw;
       }
+      lsum += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
       sm100::fence_proxy_async_smem();
       sm100::tc_fence_before();
       sm100::mbar_arrive(p_full(pb));
     }
-    // Row sum across the halves, then the epilogue on this thread's O columns.
+    // Merge the two halves of each row: both threads of a row read (max, sum)
+    // of both halves, then each produces HD output columns from both O halves.
+    float w_self = 0.f, w_other = 0.f, lrow = 0.f, mrow = -INFINITY;
     if (ok) {
-      // Parity nblk&1 was last read in block nblk-2; the partner has finished
-      // that read, since it has since arrived on the block nblk-1 exchange.
-      const int fb = nblk & 1;
-      red[(fb * 2 + half) * BM + row] = lsum;
-      sm100::mbar_arrive(red_bar(2));
-      ok = __all_sync(0xffffffffu, sm100::mbar_wait(red_bar(2), 0, abort, err, ERR_RED, WAIT_LIMIT));
-      if (ok) lsum += red[(fb * 2 + (half ^ 1)) * BM + row];
+      red[(half * BM + row) * 2 + 0] = m_used;
+      red[(half * BM + row) * 2 + 1] = lsum;
+      sm100::mbar_arrive(red_bar);
+      ok = __all_sync(0xffffffffu, sm100::mbar_wait(red_bar, 0, abort, err, ERR_RED, WAIT_LIMIT));
+      if (ok) {
+        const float m_o = red[((half ^ 1) * BM + row) * 2 + 0];
+        const float l_o = red[((half ^ 1) * BM + row) * 2 + 1];
+        mrow = fmaxf(m_used, m_o);
+        w_self = m_used == -INFINITY ? 0.f : ex2_approx(m_used - mrow);
+        w_other = m_o == -INFINITY ? 0.f : ex2_approx(m_o - mrow);
+        lrow = w_self * lsum + w_other * l_o;
+      }
     }
     if (ok && __all_sync(0xffffffffu, sm100::mbar_wait(pv_done((nblk - 1) % NP), ((nblk - 1) / NP) & 1, abort,
                                                        err, ERR_PV_DONE, WAIT_LIMIT))) {
       sm100::tc_fence_after();
-      if (a.nchunks == 1) {
-        const float inv = 1.0f / lsum;
-        uint16_t* dst = a.out + (r * a.hq + static_cast<int64_t>(h) * G + g) * D + half * HD;
+      // O columns [half*HD, half*HD+HD) of this row = w_self*O_self + w_other*O_other.
+      const float w0 = half == 0 ? w_self : w_other;
+      const float w1 = half == 0 ? w_other : w_self;
+      const bool final_out = a.nchunks == 1;
+      const float inv = final_out ? 1.0f / lrow : 1.0f;
+      const int64_t wu = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks + chunk;
+      uint16_t* dst = a.out + (r * a.hq + static_cast<int64_t>(h) * G + g) * D + half * HD;
+      float* wo = a.ws_o + (wu * BM + row) * D + half * HD;
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t ov[32];
-          sm100::tmem_ld32(tmem + lane_base + TM_O + half * HD + c * 32, ov);
-          sm100::tmem_wait_ld();
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o0[32], o1[32];
+        sm100::tmem_ld32(tmem + lane_base + TM_O + half * HD + c * 32, o0);
+        sm100::tmem_ld32(tmem + lane_base + TM_O + D + half * HD + c * 32, o1);
+        sm100::tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = (w0 * __uint_as_float(o0[e]) + w1 * __uint_as_float(o1[e])) * inv;
+        if (final_out) {
           if (valid) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
+            for (int q = 0; q < 4; ++q) {
               uint4 w;
-              w.x = pack2<T>(__uint_as_float(ov[v * 8 + 0]) * inv, __uint_as_float(ov[v * 8 + 1]) * inv);
-              w.y = pack2<T>(__uint_as_float(ov[v * 8 + 2]) * inv, __uint_as_float(ov[v * 8 + 3]) * inv);
-              w.z = pack2<T>(__uint_as_float(ov[v * 8 + 4]) * inv, __uint_as_float(ov[v * 8 + 5]) * inv);
-              w.w = pack2<T>(__uint_as_float(ov[v * 8 + 6]) * inv, __uint_as_float(ov[v * 8 + 7]) * inv);
-              *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
+              w.x = pack2<T>(v[q * 8 + 0], v[q * 8 + 1]);
+              w.y = pack2<T>(v[q * 8 + 2], v[q * 8 + 3]);
+              w.z = pack2<T>(v[q * 8 + 4], v[q * 8 + 5]);
+              w.w = pack2<T>(v[q * 8 + 6], v[q * 8 + 7]);
+              *reinterpret_cast<uint4*>(dst + c * 32 + q * 8) = w;
             }
           }
-        }
-      } else {
-        const int64_t wu = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks + chunk;
-        float* wo = a.ws_o + (wu * BM + row) * D + half * HD;
+        } else {
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t ov[32];
-          sm100::tmem_ld32(tmem + lane_base + TM_O + half * HD + c * 32, ov);
-          sm100::tmem_wait_ld();
-#pragma unroll
-          for (int v = 0; v < 8; ++v)
-            *reinterpret_cast<uint4*>(wo + c * 32 + v * 4) =
-                make_uint4(ov[v * 4], ov[v * 4 + 1], ov[v * 4 + 2], ov[v * 4 + 3]);
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(wo + c * 32 + q * 4) = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2],
+                                                                          v[q * 4 + 3]);
         }
-        if (half == 0) *reinterpret_cast<float2*>(a.ws_ml + (wu * BM + row) * 2) = make_float2(m_used, lsum);
       }
+      if (!final_out && half == 0)
+        *reinterpret_cast<float2*>(a.ws_ml + (wu * BM + row) * 2) = make_float2(mrow, lrow);
     }
   }
 
@@ -535,16 +565,24 @@ inline Plan make_plan(int64_t rows, int hq, int hkv, int64_t max_position) {
   const int64_t keys = max_position + 1;
   const int64_t blocks = (keys + BN - 1) / BN;
   const int64_t base = static_cast<int64_t>(p.tiles) * hkv;
-  // One CTA per SM: ~1.5 waves of chunks, >= 4 key blocks each so the
-  // per-CTA prologue (TMEM, barriers, Q tile) is amortised.
-  const int64_t target = static_cast<int64_t>(kNumSMs) * 3 / 2;
-  int64_t n = (target + base - 1) / base;
-  const int64_t max_n = (blocks + 3) / 4;
-  if (n > max_n) n = max_n;
-  if (n < 1) n = 1;
-  p.chunk = ((blocks + n - 1) / n) * BN;
-  p.nchunks = static_cast<int>((keys + p.chunk - 1) / p.chunk);  // <= n
-  p.max_chunks = n;  // n only grows with max_position, so it bounds every smaller plan
+  // One CTA per SM and a per-CTA prologue/epilogue of a few microseconds: with
+  // few (head, tile) units, cut the key range into about one wave of chunks;
+  // with many, use ~4 waves so that short and long causal spans balance out.
+  // Chunks hold >= 4 key blocks.
+  const int64_t waves = base >= kNumSMs ? 4 : 1;
+  int64_t cb = (base * blocks + waves * kNumSMs - 1) / (waves * kNumSMs);
+  if (cb < 4) cb = 4;
+  if (cb > blocks) cb = blocks;
+  if (cb < 1) cb = 1;
+  p.chunk = cb * BN;
+  p.nchunks = static_cast<int>((blocks + cb - 1) / cb);
+  // nchunks = ceil(blocks / cb) <= min(ceil(blocks / 4), ceil(waves * SMs / base)),
+  // a bound that only grows with max_position: it sizes workspaces from cache_rows.
+  int64_t bound = (waves * kNumSMs + base - 1) / base;
+  const int64_t by_blocks = (blocks + 3) / 4;
+  if (bound > by_blocks) bound = by_blocks;
+  if (bound < p.nchunks) bound = p.nchunks;
+  p.max_chunks = bound;
   return p;
 }
 
@@ -590,8 +628,27 @@ inline bool make_kv_map(CUtensorMap* map, const void* ptr, bool bf16, int head_d
   return r == CUDA_SUCCESS;
 }
 
+// Packed queries [rows][q_heads][D] seen as {D, q_heads, rows}; box 64 x G x 128/G
+// covers the 128 m-entries (row, head of the group) of one tile.
+inline bool make_q_map(CUtensorMap* map, const void* ptr, bool bf16, int head_dim, int q_heads, int64_t rows,
+                       int group) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(q_heads),
+                        static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim) * 2,
+                           static_cast<cuuint64_t>(q_heads) * head_dim * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(group), static_cast<cuuint32_t>(BM / group)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <class T, int D, bool SPLIT>
-int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Args& a, cudaStream_t s) {
+int launch(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, const Args& a, cudaStream_t s) {
   constexpr int smem = Layout<D, SPLIT>::BYTES;
   static int configured[64] = {0};
   int dev = 0;
@@ -614,7 +671,7 @@ int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Args& a, cudaStre
     return KVR_ERR_CUDA;
   }
   dim3 grid(a.tiles * a.nchunks, a.hkv);
-  attn_tc_kernel<T, D, SPLIT><<<grid, THREADS, smem, s>>>(mk, mv, a);
+  attn_tc_kernel<T, D, SPLIT><<<grid, THREADS, smem, s>>>(mk, mv, mq, a);
   int st = check_launch();
   if (st != KVR_OK || a.nchunks == 1) return st;
   const int64_t total_m = a.rows * a.group;
@@ -659,13 +716,19 @@ int kvr_selected_attention(const void* q, const void* k_cache, const void* v_cac
   const size_t need = attn::workspace_bytes(p.tiles, p.nchunks, kv_heads, head_dim);
   if (!workspace || workspace_bytes < need || !aligned16(workspace)) return KVR_ERR_INVALID_ARG;
   const bool bf16 = dtype == KVR_DTYPE_BF16;
-  CUtensorMap mk, mv;
+  CUtensorMap mk, mv, mq;
   if (!attn::make_kv_map(&mk, k_cache, bf16, head_dim, cache_rows, kv_heads, cache_head_stride,
                          cache_row_stride) ||
       !attn::make_kv_map(&mv, v_cache, bf16, head_dim, cache_rows, kv_heads, cache_head_stride,
                          cache_row_stride))
     return KVR_ERR_UNSUPPORTED;
+  const int group = q_heads / kv_heads;
+  // Q by TMA when the tile's 128 m-entries are whole rows x group heads.
+  const bool q_by_tma = group <= attn::BM && attn::BM % group == 0 &&
+                        attn::make_q_map(&mq, q, bf16, head_dim, q_heads, rows, group);
+  if (!q_by_tma) mq = mk;  // unused placeholder
   attn::Args a;
+  a.q_by_tma = q_by_tma ? 1 : 0;
   a.q = static_cast<const uint16_t*>(q);
   a.out = static_cast<uint16_t*>(out);
   a.positions = positions;
@@ -685,12 +748,12 @@ int kvr_selected_attention(const void* q, const void* k_cache, const void* v_cac
   const bool split = precision == KVR_ATTN_P_SPLIT;
   if (bf16) {
     if (head_dim == 128)
-      return split ? attn::launch<BF16, 128, true>(mk, mv, a, s) : attn::launch<BF16, 128, false>(mk, mv, a, s);
-    return split ? attn::launch<BF16, 64, true>(mk, mv, a, s) : attn::launch<BF16, 64, false>(mk, mv, a, s);
+      return split ? attn::launch<BF16, 128, true>(mk, mv, mq, a, s) : attn::launch<BF16, 128, false>(mk, mv, mq, a, s);
+    return split ? attn::launch<BF16, 64, true>(mk, mv, mq, a, s) : attn::launch<BF16, 64, false>(mk, mv, mq, a, s);
   }
   if (head_dim == 128)
-    return split ? attn::launch<F16, 128, true>(mk, mv, a, s) : attn::launch<F16, 128, false>(mk, mv, a, s);
-  return split ? attn::launch<F16, 64, true>(mk, mv, a, s) : attn::launch<F16, 64, false>(mk, mv, a, s);
+    return split ? attn::launch<F16, 128, true>(mk, mv, mq, a, s) : attn::launch<F16, 128, false>(mk, mv, mq, a, s);
+  return split ? attn::launch<F16, 64, true>(mk, mv, mq, a, s) : attn::launch<F16, 64, false>(mk, mv, mq, a, s);
 }
 
 }  // extern "C"
