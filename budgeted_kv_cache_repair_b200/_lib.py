@@ -16,7 +16,8 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIBRARY = os.path.join(HERE, "lib", "libkvr_b200.so")
 
-OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT = 0, 1, 2, 3, 4
+OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_SCRATCH_LIMIT = 0, 1, 2, 3, 4, 5
+STATIC_SCRATCH_BYTES = 16 << 20
 DTYPE_BF16, DTYPE_F16 = 0, 1
 ATTN_P_SPLIT, ATTN_P_ROUNDED = 0, 1
 MAX_LAYER_TENSORS = 256
@@ -46,6 +47,7 @@ SIGNATURES = {
     "kvr_attention_workspace_size": (ctypes.c_size_t, [_L, _I, _I, _I, _L]),
     "kvr_selected_attention": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _I, _P,
                                     ctypes.c_size_t, _I, _P]),
+    "kvr_selected_attention_static": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _I, _I, _P]),
 }
 
 _lock = threading.Lock()
@@ -104,7 +106,7 @@ def check(status: int, what: str) -> None:
         return
     lib = load()
     text = lib.kvr_status_string(status).decode()
-    if status in (ERR_INVALID_ARG, ERR_UNSUPPORTED):
+    if status in (ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_SCRATCH_LIMIT):
         raise ValueError(f"{what}: {text}")
     cuda = lib.kvr_last_cuda_error()
     raise KvrError(f"{what}: {text} (cudaError {cuda})")

@@ -756,4 +756,64 @@ int kvr_selected_attention(const void* q, const void* k_cache, const void* v_cac
   return split ? attn::launch<F16, 64, true>(mk, mv, mq, a, s) : attn::launch<F16, 64, false>(mk, mv, mq, a, s);
 }
 
+// ---------------------------------------------------------------------------
+// No-allocation variant. Some callers cannot allocate device memory per call:
+// a host runtime that reaches this library over a plain C FFI with a fixed,
+// pre-planned GPU memory budget and no caching allocator, for which a
+// cudaMalloc would synchronise the device and fragment its pool. For them the
+// split-KV partials live in one file-scope device array of fixed size,
+// reserved on every GPU that loads the library for the life of the process.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_attention_scratch[KVR_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+// Device address of g_attention_scratch, looked up once per device with that
+// device current (host code cannot use the symbol itself as a pointer).
+void* g_scratch_ptr[64] = {nullptr};
+int g_scratch_ready[64] = {0};
+
+int scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return KVR_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= 64) return KVR_ERR_UNSUPPORTED;
+  if (!__atomic_load_n(&g_scratch_ready[dev], __ATOMIC_ACQUIRE)) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_attention_scratch);
+    if (e != cudaSuccess || !ptr) {
+      set_last_cuda_error(e);
+      return KVR_ERR_CUDA;
+    }
+    g_scratch_ptr[dev] = ptr;  // identical value from any racing thread
+    __atomic_store_n(&g_scratch_ready[dev], 1, __ATOMIC_RELEASE);
+  }
+  *out = g_scratch_ptr[dev];
+  return KVR_OK;
+}
+
+}  // namespace
+
+int kvr_selected_attention_static(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                  const int64_t* positions, int64_t rows, int q_heads, int kv_heads,
+                                  int head_dim, int64_t cache_rows, int64_t cache_head_stride,
+                                  int64_t cache_row_stride, int64_t max_position, float scale, int precision,
+                                  int dtype, void* stream) {
+  if (rows < 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads || cache_rows < 0 || max_position < 0)
+    return KVR_ERR_INVALID_ARG;
+  if (rows == 0) return KVR_OK;
+  const attn::Plan p = attn::make_plan(rows, q_heads, kv_heads, max_position);
+  if (attn::workspace_bytes(p.tiles, p.nchunks, kv_heads, head_dim) > KVR_STATIC_SCRATCH_BYTES)
+    return KVR_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  const int st = scratch_address(&scratch);
+  if (st != KVR_OK) return st;
+  return kvr_selected_attention(q, k_cache, v_cache, out, positions, rows, q_heads, kv_heads, head_dim,
+                                cache_rows, cache_head_stride, cache_row_stride, max_position, scale, precision,
+                                scratch, KVR_STATIC_SCRATCH_BYTES, dtype, stream);
+}
+
 }  // extern "C"

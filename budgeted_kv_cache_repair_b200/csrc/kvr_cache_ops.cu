@@ -267,6 +267,7 @@ const char* kvr_status_string(int status) {
     case KVR_ERR_UNSUPPORTED: return "unsupported shape or dtype";
     case KVR_ERR_CUDA: return "CUDA error";
     case KVR_ERR_TIMEOUT: return "bounded device wait timed out";
+    case KVR_ERR_SCRATCH_LIMIT: return "needs more scratch than the static device array holds";
     default: return "unknown status";
   }
 }

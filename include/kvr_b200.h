@@ -36,6 +36,7 @@ extern "C" {
 #define KVR_ERR_UNSUPPORTED 2   /* shape/dtype outside the built kernels */
 #define KVR_ERR_CUDA 3          /* a CUDA runtime call failed; see kvr_last_cuda_error */
 #define KVR_ERR_TIMEOUT 4       /* a bounded device wait gave up */
+#define KVR_ERR_SCRATCH_LIMIT 5 /* problem needs more than the static scratch array holds */
 
 #define KVR_DTYPE_BF16 0
 #define KVR_DTYPE_F16 1
@@ -193,6 +194,34 @@ KVR_API int kvr_selected_attention(const void* q, const void* k_cache, const voi
                                    int64_t cache_head_stride, int64_t cache_row_stride,
                                    int64_t max_position, float scale, int precision,
                                    void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
+/*
+ * kvr_selected_attention without a caller-provided workspace, for callers
+ * that cannot allocate device memory per call (for example a host runtime
+ * reaching this library over a plain C FFI with a fixed, pre-planned GPU
+ * memory budget and no caching allocator, where a cudaMalloc would
+ * synchronise the device). It has no counterpart in the reference.
+ *
+ * Scratch comes from one file-scope device array of KVR_STATIC_SCRATCH_BYTES
+ * (16 MiB) that every GPU loading the library holds until the process exits.
+ * Problems whose partial results need more return KVR_ERR_SCRATCH_LIMIT
+ * before any launch (kvr_attention_workspace_size() tells the need). The
+ * first call on a device looks up the array's device address with that
+ * device current, so make it before any stream capture. All calls share the
+ * array and it keeps the last call's contents (the status word at offset 0 is
+ * cleared on the stream before each launch): calls that overlap on the GPU,
+ * on any streams, race. Nothing here calls cudaMalloc, cudaFree or an
+ * allocating library routine. Arguments and results otherwise match
+ * kvr_selected_attention (the workspace status word lives in the array's
+ * first 4 bytes and is not exposed by this variant).
+ */
+#define KVR_STATIC_SCRATCH_BYTES (16u << 20)
+KVR_API int kvr_selected_attention_static(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                          const int64_t* positions, int64_t rows, int q_heads, int kv_heads,
+                                          int head_dim, int64_t cache_rows,
+                                          int64_t cache_head_stride, int64_t cache_row_stride,
+                                          int64_t max_position, float scale, int precision,
+                                          int dtype, void* stream);
 
 #ifdef __cplusplus
 }
