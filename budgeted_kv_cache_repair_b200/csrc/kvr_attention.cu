@@ -513,9 +513,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // One warp per m-entry: O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
+// Partials are read in batches of up to 8 chunks with all loads issued before
+// any use, so the merge is one memory round trip per batch, not per chunk.
 template <class T, int D>
 __global__ void __launch_bounds__(256) attn_combine_kernel(Args a) {
   constexpr int PER = D / 32;  // values per lane
+  constexpr int BATCH = 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
   const int64_t m_abs = static_cast<int64_t>(blockIdx.x) * 8 + warp;
@@ -530,19 +533,39 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(Args a) {
   int nv = static_cast<int>(pmax / a.chunk) + 1;
   if (nv > a.nchunks) nv = a.nchunks;
   const int64_t w0 = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks;
+  // Pass 1: running max over all chunks.
   float M = -INFINITY;
-  for (int c = 0; c < nv; ++c) M = fmaxf(M, a.ws_ml[((w0 + c) * BM + row) * 2]);
+  for (int c0 = 0; c0 < nv; c0 += BATCH) {
+    float mv[BATCH];
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i)
+      mv[i] = c0 + i < nv ? a.ws_ml[((w0 + c0 + i) * BM + row) * 2] : -INFINITY;
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i) M = fmaxf(M, mv[i]);
+  }
+  // Pass 2: weighted sums.
   float Lsum = 0.f, acc[PER];
 #pragma unroll
   for (int e = 0; e < PER; ++e) acc[e] = 0.f;
-  for (int c = 0; c < nv; ++c) {
-    const float2 ml = *reinterpret_cast<const float2*>(a.ws_ml + ((w0 + c) * BM + row) * 2);
-    const float wgt = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
-    if (wgt == 0.f) continue;
-    Lsum += wgt * ml.y;
-    const float* src = a.ws_o + ((w0 + c) * BM + row) * D + lane * PER;
+  for (int c0 = 0; c0 < nv; c0 += BATCH) {
+    float2 ml[BATCH];
+    float ov[BATCH][PER];
 #pragma unroll
-    for (int e = 0; e < PER; ++e) acc[e] += wgt * src[e];
+    for (int i = 0; i < BATCH; ++i) {
+      const bool in = c0 + i < nv;
+      const int64_t w = w0 + (in ? c0 + i : 0);
+      ml[i] = in ? *reinterpret_cast<const float2*>(a.ws_ml + (w * BM + row) * 2) : make_float2(-INFINITY, 0.f);
+      const float* src = a.ws_o + (w * BM + row) * D + lane * PER;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) ov[i][e] = in ? src[e] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i) {
+      const float wgt = ml[i].x == -INFINITY ? 0.f : exp2f(ml[i].x - M);
+      Lsum += wgt * ml[i].y;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) acc[e] += wgt * ov[i][e];
+    }
   }
   const float inv = 1.0f / Lsum;
   const int64_t r = m_abs / G;

@@ -136,6 +136,20 @@ struct ShiftPtrs {
 };
 
 template <class T, int D>
+__device__ __forceinline__ void rope_pair_regs(const Vec8& lo, const Vec8& hi, Vec8& olo, Vec8& ohi, int j,
+                                               const float* cs) {
+  constexpr int H = D / 2;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int d = j * 8 + e;
+    const float xl = T::to_f(lo.h[e]);
+    const float xh = T::to_f(hi.h[e]);
+    olo.h[e] = rope_elem<T>(xl, -xh, cs[d], cs[D + d]);
+    ohi.h[e] = rope_elem<T>(xh, xl, cs[H + d], cs[D + H + d]);
+  }
+}
+
+template <class T, int D>
 __global__ void __launch_bounds__(256) shift_cache_kernel(ShiftPtrs ptrs, ShiftArgs a,
                                                           const uint16_t* __restrict__ cos_sin) {
   __shared__ float cs[2 * D];
@@ -153,30 +167,52 @@ __global__ void __launch_bounds__(256) shift_cache_kernel(ShiftPtrs ptrs, ShiftA
   uint16_t* dst = static_cast<uint16_t*>(comp ? ptrs.v_new[l] : ptrs.k_new[l]) + h * a.new_hs;
   constexpr int PAIRS = D / 16;
   constexpr int HALF = D / 2;
+  constexpr int U = 4;  // vector pairs in flight per thread
   const bool rotate = comp == 0 && a.apply_rope;
   const int64_t n = a.new_rows * PAIRS;
   const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += step) {
-    const int64_t r = i / PAIRS;
-    const int j = static_cast<int>(i & (PAIRS - 1));
-    int64_t sr;
-    bool tail;
-    if (r < a.prefix) {
-      sr = r;
-      tail = false;
-    } else if (r >= a.new_tail) {
-      sr = r - a.new_tail + a.old_tail;
-      tail = true;
-    } else {
-      continue;  // changed boundary token: recomputed by the caller
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < n; i0 += U * step) {
+    Vec8 lo[U], hi[U];
+    int64_t drow[U];
+    int jj[U];
+    bool live[U], rot[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {  // all loads first
+      const int64_t i = i0 + u * step;
+      const int64_t r = i / PAIRS;
+      jj[u] = static_cast<int>(i & (PAIRS - 1));
+      drow[u] = r;
+      int64_t sr = -1;
+      bool tail = false;
+      if (i < n) {
+        if (r < a.prefix) {
+          sr = r;
+        } else if (r >= a.new_tail) {
+          sr = r - a.new_tail + a.old_tail;
+          tail = true;
+        }
+      }
+      live[u] = sr >= 0;  // rows in [prefix, new_tail) are recomputed by the caller
+      rot[u] = tail && rotate;
+      if (live[u]) {
+        const uint16_t* s = src + sr * a.old_rs + jj[u] * 8;
+        lo[u] = ld_vec8_stream(s);
+        hi[u] = ld_vec8_stream(s + HALF);
+      }
     }
-    const uint16_t* s = src + sr * a.old_rs;
-    uint16_t* d = dst + r * a.new_rs;
-    if (tail && rotate) {
-      rope_pair<T, D>(s, d, j, cs);
-    } else {
-      st_vec8_stream(d + j * 8, ld_vec8_stream(s + j * 8));
-      st_vec8_stream(d + HALF + j * 8, ld_vec8_stream(s + HALF + j * 8));
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (!live[u]) continue;
+      uint16_t* d = dst + drow[u] * a.new_rs + jj[u] * 8;
+      if (rot[u]) {
+        Vec8 olo, ohi;
+        rope_pair_regs<T, D>(lo[u], hi[u], olo, ohi, jj[u], cs);
+        st_vec8_stream(d, olo);
+        st_vec8_stream(d + HALF, ohi);
+      } else {
+        st_vec8_stream(d, lo[u]);
+        st_vec8_stream(d + HALF, hi[u]);
+      }
     }
   }
 }
@@ -373,7 +409,7 @@ int kvr_shift_cache_layers(const void* const* k_old, const void* const* v_old, v
               old_head_stride, old_row_stride, new_head_stride, new_row_stride, apply_rope};
   const int segs = num_layers * heads * 2;
   const int64_t pairs = new_rows * (head_dim / 16);
-  dim3 grid(blocks_per_segment(pairs / 2, segs, 256), segs);
+  dim3 grid(blocks_per_segment(pairs / 4, segs, 256), segs);
   auto s = static_cast<cudaStream_t>(stream);
   const uint16_t* cs = static_cast<const uint16_t*>(cos_sin);
   if (dtype == KVR_DTYPE_BF16) {

@@ -7,7 +7,7 @@ layers scatter on update and whose attention is masked SDPA; this engine reads
 the same parameters and runs, per layer:
 
     add_rmsnorm        residual add + input RMSNorm            (libkvr_b200)
-    q/k/v projections  cuBLAS bf16/fp16 GEMMs                   (torch.mm)
+    q/k/v projections  one cuBLAS GEMM on [Wq; Wk; Wv]          (torch.mm)
     qkv_rope_scatter   q/k-norm, RoPE, q packing, K/V scatter   (libkvr_b200)
     selected_attention GQA split-KV flash attention             (libkvr_b200)
     o projection       cuBLAS
@@ -16,9 +16,11 @@ the same parameters and runs, per layer:
     silu_mul           SiLU(gate) * up                          (libkvr_b200)
     down projection    cuBLAS
 
-Rounding follows the modules op by op (one rounding per torch op), and the
-GEMMs are the same cuBLAS calls ``nn.Linear`` makes, so K/V rows differ from
-the reference only where attention's summation order differs.
+Rounding follows the modules op by op (one rounding per torch op). At a few
+dozen rows the projections stream weights: one GEMM over the concatenated
+q/k/v weights (an engine-owned copy, 1.5 GB for an 8B model, rebuilt when a
+parameter changes) runs at about three times the HBM bandwidth of three
+separate GEMMs whose k/v weights are only 8 MB each.
 
 The last layer stops after its K/V scatter: its attention output, MLP and the
 final norm feed nothing in the returned cache (the reference computes and
@@ -48,6 +50,17 @@ class LayerWeights:
     down: torch.Tensor
     q_norm: torch.Tensor | None
     k_norm: torch.Tensor | None
+    qkv: torch.Tensor | None = None        # engine-owned [Wq; Wk; Wv]
+    qkv_key: tuple | None = None           # identities and versions it was built from
+
+    def fused_qkv(self) -> torch.Tensor:
+        """``cat([Wq, Wk, Wv])`` for one GEMM per layer, rebuilt if any of the
+        three parameters was replaced or modified in place since."""
+        key = tuple((id(t), t._version) for t in (self.q, self.k, self.v))
+        if self.qkv is None or self.qkv_key != key:
+            self.qkv = torch.cat((self.q, self.k, self.v), dim=0).contiguous()
+            self.qkv_key = key
+        return self.qkv
 
 
 class ModelView:
@@ -159,9 +172,7 @@ class Workspace:
         self.hidden = torch.empty((rows, view.hidden), dtype=dt, device=device)
         self.normed = torch.empty((rows, view.hidden), dtype=dt, device=device)
         self.delta = torch.empty((rows, view.hidden), dtype=dt, device=device)
-        self.q = torch.empty((rows, qd), dtype=dt, device=device)
-        self.k = torch.empty((rows, kd), dtype=dt, device=device)
-        self.v = torch.empty((rows, kd), dtype=dt, device=device)
+        self.qkv = torch.empty((rows, qd + 2 * kd), dtype=dt, device=device)
         self.q_rot = torch.empty((rows, qd), dtype=dt, device=device)
         self.attn = torch.empty((rows, qd), dtype=dt, device=device)
         self.gate = torch.empty((rows, view.intermediate), dtype=dt, device=device)
@@ -188,6 +199,8 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
     ws = Workspace(view, rows, cache_rows, device)
     cos, sin = view.rope_tables(positions)
     D, H = view.head_dim, view.hidden
+    qd, kd = view.heads * D, view.kv_heads * D
+    elem = ws.qkv.element_size()
     scale = float(D) ** -0.5
     pos_ptr = positions.data_ptr()
     _lib.check(lib.kvr_embed_rows(view.embed.data_ptr(), view.vocab, H, ids.data_ptr(), ids.numel(),
@@ -200,13 +213,13 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
                                        w.in_norm.data_ptr(), ws.normed.data_ptr(), rows, H, H, H, H,
                                        view.eps, dt, stream), "add_rmsnorm")
         final = index == last
-        if not final:
-            torch.mm(ws.normed, w.q.t(), out=ws.q)
-        torch.mm(ws.normed, w.k.t(), out=ws.k)
-        torch.mm(ws.normed, w.v.t(), out=ws.v)
+        torch.mm(ws.normed, w.fused_qkv().t(), out=ws.qkv)
+        q_ptr = ws.qkv.data_ptr()
+        k_ptr = q_ptr + qd * elem
+        v_ptr = k_ptr + kd * elem
+        rs = ws.qkv.stride(0)
         _lib.check(lib.kvr_qkv_rope_scatter(
-            ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(), ws.q.stride(0), ws.k.stride(0),
-            ws.v.stride(0), w.q_norm.data_ptr() if w.q_norm is not None else None,
+            q_ptr, k_ptr, v_ptr, rs, rs, rs, w.q_norm.data_ptr() if w.q_norm is not None else None,
             w.k_norm.data_ptr() if w.k_norm is not None else None, view.eps, cos.data_ptr(),
             sin.data_ptr(), pos_ptr, rows, view.heads, view.kv_heads, D,
             None if final else ws.q_rot.data_ptr(), key.data_ptr(), value.data_ptr(), cache_rows,

@@ -1,0 +1,111 @@
+"""Run one engine kernel at benchmark geometry, for profilers.
+
+    python -m budgeted_kv_cache_repair_b200.profile_kernels shift     [--reps N]
+    python -m budgeted_kv_cache_repair_b200.profile_kernels attention [--reps N] [--precision rounded|split]
+    python -m budgeted_kv_cache_repair_b200.profile_kernels copy      [--reps N]
+
+Geometry: Llama-3-8B shape (32 layers, 8 KV heads, head_dim 128, bf16),
+8192-token context with 256 tokens deleted at 1024 (7936 rows), 64 selected
+rows in 16 intervals of 4. Inputs are seeded random tensors. After two
+warm-up launches the command times `--reps` launches with CUDA events and
+prints the average; under ncu, capture with `-s 2`.
+"""
+
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import _lib, build
+
+LAYERS, HEADS, KV_HEADS, D, OLD, NEW, DELETE_AT, DELETED = 32, 32, 8, 128, 8192, 7936, 1024, 256
+
+
+def _positions():
+    gen = torch.Generator().manual_seed(1)
+    slots = (NEW - DELETE_AT) // 5
+    starts = sorted(DELETE_AT + s * 5 for s in torch.randperm(slots, generator=gen)[:16].tolist())
+    return sorted(p + i for p in starts for i in range(4))
+
+
+def _time(fn, reps: int) -> float:
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    begin.record()
+    for _ in range(reps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    return begin.elapsed_time(end) / reps * 1e3
+
+
+def shift(reps: int) -> None:
+    lib = _lib.load()
+    ko = [torch.randn(1, KV_HEADS, OLD, D, device="cuda").bfloat16() for _ in range(LAYERS)]
+    vo = [torch.randn(1, KV_HEADS, OLD, D, device="cuda").bfloat16() for _ in range(LAYERS)]
+    kn = [torch.empty(1, KV_HEADS, NEW, D, device="cuda", dtype=torch.bfloat16) for _ in range(LAYERS)]
+    vn = [torch.empty(1, KV_HEADS, NEW, D, device="cuda", dtype=torch.bfloat16) for _ in range(LAYERS)]
+    table = torch.randn(2 * D, device="cuda").bfloat16()
+    stream = _lib.stream_handle()
+    args = (_lib.ptr_array(ko), _lib.ptr_array(vo), _lib.ptr_array(kn), _lib.ptr_array(vn), LAYERS, KV_HEADS, D, NEW,
+            DELETE_AT, DELETE_AT + DELETED, DELETE_AT, OLD * D, D, NEW * D, D, table.data_ptr(), 1, _lib.DTYPE_BF16,
+            stream)
+    us = _time(lambda: _lib.check(lib.kvr_shift_cache_layers(*args), "shift"), reps)
+    algo = 2 * 2 * LAYERS * KV_HEADS * NEW * D * 2
+    print(f"kvr_shift_cache_layers: {us:.1f} us/launch, {algo / us / 1e3:.0f} GB/s on {algo} algorithmic bytes")
+
+
+def copy(reps: int) -> None:
+    lib = _lib.load()
+    src = [torch.randn(1, KV_HEADS, NEW, D, device="cuda").bfloat16() for _ in range(2 * LAYERS)]
+    dst = [torch.empty_like(t) for t in src]
+    stream = _lib.stream_handle()
+    args = (_lib.ptr_array(src), _lib.ptr_array(dst), 2 * LAYERS, KV_HEADS, NEW, D, NEW * D, D, NEW * D, D,
+            _lib.DTYPE_BF16, stream)
+    us = _time(lambda: _lib.check(lib.kvr_copy_layers(*args), "copy"), reps)
+    algo = 2 * 2 * LAYERS * KV_HEADS * NEW * D * 2
+    print(f"kvr_copy_layers: {us:.1f} us/launch, {algo / us / 1e3:.0f} GB/s on {algo} algorithmic bytes")
+
+
+def attention(reps: int, precision: str) -> None:
+    lib = _lib.load()
+    positions = _positions()
+    rows = len(positions)
+    pos = torch.tensor(positions, device="cuda")
+    q = (torch.randn(rows, HEADS, D, device="cuda") * 0.5).bfloat16()
+    k = torch.randn(1, KV_HEADS, NEW, D, device="cuda").bfloat16()
+    v = torch.randn(1, KV_HEADS, NEW, D, device="cuda").bfloat16()
+    out = torch.empty_like(q)
+    need = lib.kvr_attention_workspace_size(rows, HEADS, KV_HEADS, D, NEW)
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    mode = _lib.ATTN_P_SPLIT if precision == "split" else _lib.ATTN_P_ROUNDED
+    stream = _lib.stream_handle()
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), pos.data_ptr(), rows, HEADS, KV_HEADS, D, NEW,
+            NEW * D, D, positions[-1], D ** -0.5, mode, ws.data_ptr(), need, _lib.DTYPE_BF16, stream)
+    us = _time(lambda: _lib.check(lib.kvr_selected_attention(*args), "attention"), reps)
+    kv = 2 * KV_HEADS * (positions[-1] + 1) * D * 2
+    flops = 4.0 * HEADS * D * sum(p + 1 for p in positions)
+    print(f"kvr_selected_attention ({precision}): {us:.1f} us/call, {kv / us / 1e3:.0f} GB/s of K/V, "
+          f"{flops / us / 1e6:.1f} TFLOP/s; status {int(ws[:4].view(torch.int32).item())}")
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("kernel", choices=["shift", "attention", "copy"])
+    parser.add_argument("--reps", type=int, default=10)
+    parser.add_argument("--precision", choices=["rounded", "split"], default="rounded")
+    args = parser.parse_args()
+    build.build()
+    if args.kernel == "shift":
+        shift(args.reps)
+    elif args.kernel == "copy":
+        copy(args.reps)
+    else:
+        attention(args.reps, args.precision)
+
+
+if __name__ == "__main__":
+    main()
