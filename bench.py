@@ -172,6 +172,41 @@ def _barrier(world):
         dist.barrier()
 
 
+def _time_attention(cache, intervals, cfg, device, reps=20):
+    """kvr_selected_attention alone on layer 0 of the request: (launches, total ms)."""
+    from budgeted_kv_cache_repair_b200 import _lib
+    from budgeted_kv_cache_repair_b200.engine import ATTENTION_PRECISION
+    from budgeted_kv_cache_repair_b200.validate import cache_layers
+
+    lib = _lib.load()
+    k, v = cache_layers(cache)[0]
+    positions = [p for a, b in intervals for p in range(a, b)]
+    pos = torch.tensor(positions, device=device)
+    rows, heads, kv, d, n = len(positions), cfg["heads"], cfg["kv_heads"], cfg["head_dim"], k.shape[2]
+    q = (torch.randn(rows, heads, d, device=device) * 0.5).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    need = lib.kvr_attention_workspace_size(rows, heads, kv, d, n)
+    ws = torch.empty(need, dtype=torch.uint8, device=device)
+    stream = _lib.stream_handle(device)
+
+    def call():
+        _lib.check(lib.kvr_selected_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                              pos.data_ptr(), rows, heads, kv, d, n, k.stride(1), k.stride(2),
+                                              positions[-1], d ** -0.5, ATTENTION_PRECISION, ws.data_ptr(), need,
+                                              _lib.DTYPE_BF16, stream), "attention")
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b.record()
+    for _ in range(reps):
+        call()
+    e.record()
+    torch.cuda.synchronize()
+    return {"selected_attention": (reps, b.elapsed_time(e))}
+
+
 def rope_fix_bytes(cfg, new_rows, suffix_rows):
     """Algorithmic bytes: the fused shift kernel reads and writes every kept K
     and V row; the delta-RoPE part alone is the K suffix read + write."""
@@ -311,7 +346,6 @@ def our_arm(args):
         out, receipt = packed_interval_repair(shim, shifted, ids_dev, intervals)
         del out
     torch.cuda.synchronize()
-    timer = engine.KernelTimer()
     step_events = []
     sampler = ClockSampler(device.index)
     _barrier(world)
@@ -321,7 +355,6 @@ def our_arm(args):
     with sampler:
         region_begin = torch.cuda.Event(enable_timing=True)
         region_begin.record(stream)
-        engine.set_kernel_timer(timer)
         for _ in range(args.steps):
             b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             b.record(stream)
@@ -329,7 +362,6 @@ def our_arm(args):
             e.record(stream)
             step_events.append((b, e))
             del out
-        engine.set_kernel_timer(None)
         region_end = torch.cuda.Event(enable_timing=True)
         region_end.record(stream)
         torch.cuda.synchronize()
@@ -371,7 +403,18 @@ def our_arm(args):
             dist.destroy_process_group()
         return
 
+    # Kernel attribution in a separate pass (event brackets add host work, so
+    # they stay out of the timed region): the ownership copy inside the API
+    # call, and the attention kernel alone on one layer of this request.
+    timer = engine.KernelTimer()
+    engine.set_kernel_timer(timer)
+    for _ in range(3):
+        out, _ = packed_interval_repair(shim, shifted, ids_dev, intervals)
+        del out
+    engine.set_kernel_timer(None)
+    torch.cuda.synchronize()
     totals = timer.totals_ms()
+    totals.update(_time_attention(shifted, intervals, cfg, device))
     kernels = {}
     algo_bytes, params = refresh_bytes(cfg, length)
     cache_bytes = 2 * cfg["layers"] * cfg["kv_heads"] * length * cfg["head_dim"] * 2
@@ -379,7 +422,8 @@ def our_arm(args):
         n, ms = totals["copy_layers"]
         gbs = 2 * cache_bytes / (ms / n / 1e3) / 1e9
         kernels["copy_layers"] = {"launches": n, "avg_us": ms / n * 1e3, "bytes_per_launch": 2 * cache_bytes,
-                                  "achieved_gbs": gbs, "frac_hbm": gbs / hbm, "share_of_step": ms / sum(step_ms)}
+                                  "achieved_gbs": gbs, "frac_hbm": gbs / hbm,
+                                  "est_share_of_step": ms / n / statistics.median(step_ms)}
     if "selected_attention" in totals:
         n, ms = totals["selected_attention"]
         kv_bytes = 2 * cfg["kv_heads"] * (max(p for a, b in intervals for p in range(a, b)) + 1) * cfg["head_dim"] * 2
@@ -387,7 +431,9 @@ def our_arm(args):
         kernels["selected_attention"] = {
             "launches": n, "avg_us": ms / n * 1e3, "kv_bytes_per_launch": kv_bytes,
             "achieved_gbs": kv_bytes / (ms / n / 1e3) / 1e9, "frac_hbm": kv_bytes / (ms / n / 1e3) / 1e9 / hbm,
-            "achieved_tflops": flops / (ms / n / 1e3) / 1e12, "share_of_step": ms / sum(step_ms)}
+            "achieved_tflops": flops / (ms / n / 1e3) / 1e12,
+            "est_share_of_step": ms / n * (cfg["layers"] - 1) / statistics.median(step_ms),
+            "note": "isolated launches on layer 0 of the request (back to back, L2-warm K/V)"}
     rope_gbs = fused_bytes / rope_t / 1e9
     clocks = sampler.summary()
     cpu = run_cpu_baseline(cfg, sample_layers=2, threads=os.cpu_count() or 1) if world == 1 and not args.no_cpu else None

@@ -28,6 +28,29 @@ _L = ctypes.c_int64
 _F = ctypes.c_float
 _PP = ctypes.POINTER(ctypes.c_void_p)
 
+class LayerWeights(ctypes.Structure):
+    """kvr_layer_weights"""
+    _fields_ = [(name, ctypes.c_void_p) for name in
+                ("input_norm", "qkv", "q", "k", "v", "q_norm", "k_norm", "o", "post_norm", "gate", "up", "down")]
+
+
+class Model(ctypes.Structure):
+    """kvr_model"""
+    _fields_ = [("num_layers", ctypes.c_int), ("hidden", ctypes.c_int), ("q_heads", ctypes.c_int),
+                ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("intermediate", ctypes.c_int),
+                ("vocab", ctypes.c_int64), ("eps", ctypes.c_float), ("dtype", ctypes.c_int),
+                ("embed", ctypes.c_void_p), ("layers", ctypes.POINTER(LayerWeights))]
+
+
+class RefreshRequest(ctypes.Structure):
+    """kvr_refresh_request"""
+    _fields_ = [("k_cache", ctypes.POINTER(ctypes.c_void_p)), ("v_cache", ctypes.POINTER(ctypes.c_void_p)),
+                ("cache_rows", ctypes.c_int64), ("cache_head_stride", ctypes.c_int64),
+                ("cache_row_stride", ctypes.c_int64), ("ids", ctypes.c_void_p), ("id_count", ctypes.c_int64),
+                ("positions", ctypes.c_void_p), ("rows", ctypes.c_int64), ("max_position", ctypes.c_int64),
+                ("cos_tab", ctypes.c_void_p), ("sin_tab", ctypes.c_void_p), ("attention_precision", ctypes.c_int)]
+
+
 # name -> (restype, argtypes); mirrors include/kvr_b200.h one to one.
 SIGNATURES = {
     "kvr_version": (ctypes.c_char_p, []),
@@ -47,6 +70,8 @@ SIGNATURES = {
     "kvr_attention_workspace_size": (ctypes.c_size_t, [_L, _I, _I, _I, _L]),
     "kvr_selected_attention": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _I, _P,
                                     ctypes.c_size_t, _I, _P]),
+    "kvr_packed_refresh_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(Model), _L, _L]),
+    "kvr_packed_refresh": (_I, [ctypes.POINTER(Model), ctypes.POINTER(RefreshRequest), _P, ctypes.c_size_t, _P]),
     "kvr_selected_attention_static": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _I, _I, _P]),
 }
 
@@ -95,10 +120,8 @@ def stream_handle(device: torch.device | None = None) -> int:
 
 
 def ptr_array(tensors) -> ctypes.Array:
-    arr = (ctypes.c_void_p * len(tensors))()
-    for i, t in enumerate(tensors):
-        arr[i] = t.data_ptr() if isinstance(t, torch.Tensor) else int(t)
-    return arr
+    return (ctypes.c_void_p * len(tensors))(*[t.data_ptr() if isinstance(t, torch.Tensor) else int(t)
+                                               for t in tensors])
 
 
 def check(status: int, what: str) -> None:

@@ -23,6 +23,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
 LIBRARY = os.path.join(LIBDIR, "libkvr_b200.so")
 INCLUDE = os.path.join(ROOT, "include")
+CUDA_LIB = "/usr/local/cuda/lib64"  # fallback search path for libcublas when torch has not loaded it
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
@@ -75,7 +76,8 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
         for _, log in results:
             print(log)
     tmp = LIBRARY + ".tmp"
-    cmd = [compiler, *ARCH, "-shared", "-o", tmp, *[o for o, _ in results], "-lcudart"]
+    cmd = [compiler, *ARCH, "-shared", "-o", tmp, *[o for o, _ in results], "-lcudart", "-lcublas",
+           "-Xlinker", "-rpath=" + CUDA_LIB]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode:
         raise RuntimeError(f"link failed:\n{proc.stdout}\n{proc.stderr}")

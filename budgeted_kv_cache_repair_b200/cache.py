@@ -78,33 +78,57 @@ def _uniform_strides(tensors, what):
     return strides.pop()
 
 
+def allocate_layers(count: int, heads: int, rows: int, dim: int, dtype, device):
+    """``count`` new ``(K, V)`` pairs of ``[1, heads, rows, dim]``, contiguous.
+
+    One allocation backs every layer (per-layer tensors are views of it), so a
+    request costs one allocator call instead of two per layer. The block is
+    released once no layer of the cache is referenced any more.
+    """
+    arena = torch.empty((count * 2, 1, heads, rows, dim), dtype=dtype, device=device)
+    views = arena.unbind(0)
+    return [(views[2 * i], views[2 * i + 1]) for i in range(count)]
+
+
+def uniform_layout(pairs, what: str):
+    """Check every K/V tensor against the first one (CUDA, bf16/fp16, shape,
+    strides, 16-byte rows) and return ``(heads, rows, dim, dtype, device,
+    head_stride, row_stride)``."""
+    first = pairs[0][0]
+    require_cuda_tensors([first], what)
+    _check_kv_layout([first], what)
+    shape, stride, dtype, device = first.shape, first.stride(), first.dtype, first.device
+    for pair in pairs:
+        for t in pair:
+            if t.shape != shape or t.stride() != stride or t.dtype != dtype or t.device != device:
+                raise ValueError(f"{what}: every layer must share one shape, stride pair, dtype and device")
+            if t.data_ptr() % 16:
+                raise ValueError(f"{what}: cache rows must be 16-byte aligned")
+    return shape[1], shape[2], shape[3], dtype, device, stride[1], stride[2]
+
+
 def copy_layers(pairs, length: int | None = None):
     """Independent copies of every layer's K/V (prefix ``length`` if given) in one launch."""
-    tensors = [t for pair in pairs for t in pair]
-    if not tensors:
+    if not pairs:
         return []
-    device = require_cuda_tensors(tensors, "clone_cache")
-    _check_kv_layout(tensors, "clone_cache")
-    key = tensors[0]
-    _, heads, rows, dim = key.shape
-    rows = rows if length is None else int(length)
-    if len(tensors) > _lib.MAX_LAYER_TENSORS:
+    if len(pairs) * 2 > _lib.MAX_LAYER_TENSORS:
         raise ValueError("clone_cache: more layers than one launch takes")
-    src_hs, src_rs = _uniform_strides(tensors, "clone_cache")
-    outs = [torch.empty((1, heads, rows, dim), dtype=key.dtype, device=device) for _ in tensors]
+    heads, rows, dim, dtype, device, src_hs, src_rs = uniform_layout(pairs, "clone_cache")
+    rows = rows if length is None else int(length)
+    outs = allocate_layers(len(pairs), heads, rows, dim, dtype, device)
     if rows:
         from .engine import kernel_timer
 
         timer = kernel_timer()
         token = timer.start("copy_layers") if timer else None
         lib = _lib.load()
-        _lib.check(lib.kvr_copy_layers(_lib.ptr_array(tensors), _lib.ptr_array(outs), len(tensors), heads,
-                                       rows, dim, src_hs, src_rs, rows * dim, dim,
-                                       _lib.dtype_code(key.dtype), _lib.stream_handle(device)),
-                   "copy_layers")
+        src = _lib.ptr_array([t for pair in pairs for t in pair])
+        dst = _lib.ptr_array([t for pair in outs for t in pair])
+        _lib.check(lib.kvr_copy_layers(src, dst, len(pairs) * 2, heads, rows, dim, src_hs, src_rs, rows * dim, dim,
+                                       _lib.dtype_code(dtype), _lib.stream_handle(device)), "copy_layers")
         if token:
             timer.stop(token)
-    return [(outs[i], outs[i + 1]) for i in range(0, len(outs), 2)]
+    return outs
 
 
 def clone_cache(cache: Any, length: int | None = None):
@@ -164,8 +188,9 @@ def shift_layers(model: Any, pairs, alignment: dict, recompute_end: int, old_tai
         raise ValueError("build_halo_cache: more layers than one launch takes")
     hs, rs = _uniform_strides(tensors, "build_halo_cache")
     shift = int(alignment["position_shift"])
-    k_new = [torch.empty((1, heads, new_rows, dim), dtype=key.dtype, device=device) for _ in pairs]
-    v_new = [torch.empty((1, heads, new_rows, dim), dtype=key.dtype, device=device) for _ in pairs]
+    fresh = allocate_layers(len(pairs), heads, new_rows, dim, key.dtype, device)
+    k_new = [k for k, _ in fresh]
+    v_new = [v for _, v in fresh]
     if new_rows:
         table = _shift_table(model, key, shift) if shift and old_rows > old_tail_start else None
         from .engine import kernel_timer

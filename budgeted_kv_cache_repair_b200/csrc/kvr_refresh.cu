@@ -1,0 +1,197 @@
+// Native layer loop of the packed refresh: one C-ABI call runs the selected
+// rows through every decoder layer on the caller's stream.
+//
+// Per layer: residual add + input RMSNorm, q/k/v projection (cuBLAS, one GEMM
+// over fused weights when given), fused q/k-norm + RoPE + K/V scatter into the
+// cache, selected-query attention, o projection, residual add + post-attention
+// RMSNorm, gate/up projections, SiLU(gate)*up, down projection. The last layer
+// stops after its K/V scatter: nothing after it reaches the cache.
+//
+// Host work per layer is a handful of launches from C++, so the GPU, not the
+// Python interpreter, sets the pace at a few dozen rows.
+#include <cublas_v2.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "kvr_common.cuh"
+
+namespace kvr {
+namespace {
+
+constexpr size_t kAlign = 256;
+
+inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+struct Buffers {
+  size_t hidden, normed, delta, qkv, q_rot, attn, gate, up, act, attn_ws, total;
+};
+
+Buffers layout(const kvr_model* m, int64_t rows, int64_t cache_rows) {
+  const size_t e = 2;  // bf16 / fp16
+  const size_t qd = static_cast<size_t>(m->q_heads) * m->head_dim;
+  const size_t kd = static_cast<size_t>(m->kv_heads) * m->head_dim;
+  Buffers b;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes);
+    return at;
+  };
+  b.hidden = take(rows * m->hidden * e);
+  b.normed = take(rows * m->hidden * e);
+  b.delta = take(rows * m->hidden * e);
+  b.qkv = take(rows * (qd + 2 * kd) * e);
+  b.q_rot = take(rows * qd * e);
+  b.attn = take(rows * qd * e);
+  b.gate = take(rows * static_cast<size_t>(m->intermediate) * e);
+  b.up = take(rows * static_cast<size_t>(m->intermediate) * e);
+  b.act = take(rows * static_cast<size_t>(m->intermediate) * e);
+  b.attn_ws = take(kvr_attention_workspace_size(rows, m->q_heads, m->kv_heads, m->head_dim, cache_rows));
+  b.total = off;
+  return b;
+}
+
+// One cuBLAS handle per (thread, device); cuBLAS handles are not shared
+// across threads.
+cublasHandle_t handle_for_current_device(int* status) {
+  thread_local std::unordered_map<int, cublasHandle_t> handles;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    *status = KVR_ERR_CUDA;
+    return nullptr;
+  }
+  auto it = handles.find(dev);
+  if (it != handles.end()) return it->second;
+  cublasHandle_t h = nullptr;
+  if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) {
+    *status = KVR_ERR_CUDA;
+    return nullptr;
+  }
+  handles.emplace(dev, h);
+  return h;
+}
+
+// Y[M, N] = X[M, K] * W[N, K]^T, row-major, fp32 accumulation (nn.Linear).
+int gemm(cublasHandle_t h, const void* x, int64_t ldx, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
+         int64_t k, cudaDataType_t t) {
+  const float one = 1.0f, zero = 0.0f;
+  const cublasStatus_t st = cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(n), static_cast<int>(m),
+                                         static_cast<int>(k), &one, w, t, static_cast<int>(k), x, t,
+                                         static_cast<int>(ldx), &zero, y, t, static_cast<int>(ldy),
+                                         CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+  return st == CUBLAS_STATUS_SUCCESS ? KVR_OK : KVR_ERR_CUDA;
+}
+
+bool valid_model(const kvr_model* m) {
+  if (!m || !m->layers || !m->embed || m->num_layers <= 0 || m->num_layers > KVR_MAX_LAYER_TENSORS / 2) return false;
+  if (m->hidden <= 0 || m->hidden % 8 || m->q_heads <= 0 || m->kv_heads <= 0 || m->q_heads % m->kv_heads) return false;
+  if ((m->head_dim != 64 && m->head_dim != 128) || m->intermediate <= 0 || m->intermediate % 8 || m->vocab <= 0)
+    return false;
+  if (m->dtype != KVR_DTYPE_BF16 && m->dtype != KVR_DTYPE_F16) return false;
+  for (int l = 0; l < m->num_layers; ++l) {
+    const kvr_layer_weights& w = m->layers[l];
+    if (!w.input_norm || !w.o || !w.post_norm || !w.gate || !w.up || !w.down) return false;
+    if (!w.qkv && (!w.q || !w.k || !w.v)) return false;
+    if ((w.q_norm == nullptr) != (w.k_norm == nullptr)) return false;
+  }
+  return true;
+}
+
+}  // namespace
+}  // namespace kvr
+
+using namespace kvr;
+
+extern "C" {
+
+size_t kvr_packed_refresh_workspace_size(const kvr_model* model, int64_t rows, int64_t cache_rows) {
+  if (!valid_model(model) || rows <= 0 || cache_rows <= 0) return 0;
+  return layout(model, rows, cache_rows).total;
+}
+
+int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if (!valid_model(model) || !req) return KVR_ERR_INVALID_ARG;
+  const kvr_model& m = *model;
+  const kvr_refresh_request& r = *req;
+  if (r.rows < 0 || r.cache_rows <= 0 || !r.k_cache || !r.v_cache) return KVR_ERR_INVALID_ARG;
+  if (r.rows == 0) return KVR_OK;
+  if (!r.ids || !r.positions || !r.cos_tab || !r.sin_tab || r.id_count <= 0 || r.max_position < 0 ||
+      r.max_position >= r.cache_rows)
+    return KVR_ERR_INVALID_ARG;
+  if (r.rows > 0x7fffffffLL) return KVR_ERR_UNSUPPORTED;
+  for (int l = 0; l < m.num_layers; ++l)
+    if (!r.k_cache[l] || !r.v_cache[l]) return KVR_ERR_INVALID_ARG;
+  const Buffers b = layout(&m, r.rows, r.cache_rows);
+  if (!workspace || workspace_bytes < b.total || !aligned16(workspace)) return KVR_ERR_INVALID_ARG;
+
+  int st = KVR_OK;
+  cublasHandle_t h = handle_for_current_device(&st);
+  if (!h) return st;
+  auto s = static_cast<cudaStream_t>(stream);
+  if (cublasSetStream(h, s) != CUBLAS_STATUS_SUCCESS) return KVR_ERR_CUDA;
+  const cudaDataType_t t = m.dtype == KVR_DTYPE_BF16 ? CUDA_R_16BF : CUDA_R_16F;
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* hidden = ws + b.hidden;
+  void* normed = ws + b.normed;
+  void* delta = ws + b.delta;
+  uint8_t* qkv = ws + b.qkv;
+  void* q_rot = ws + b.q_rot;
+  void* attn = ws + b.attn;
+  void* gate = ws + b.gate;
+  void* up = ws + b.up;
+  void* act = ws + b.act;
+  void* attn_ws = ws + b.attn_ws;
+  const size_t attn_ws_bytes = b.total - b.attn_ws;
+
+  const int64_t rows = r.rows;
+  const int H = m.hidden, D = m.head_dim, I = m.intermediate;
+  const int64_t qd = static_cast<int64_t>(m.q_heads) * D, kd = static_cast<int64_t>(m.kv_heads) * D;
+  const int64_t qkv_w = qd + 2 * kd;
+  const float scale = 1.0f / sqrtf(static_cast<float>(D));
+
+#define KVR_TRY(expr)            \
+  do {                           \
+    const int _st = (expr);      \
+    if (_st != KVR_OK) return _st; \
+  } while (0)
+
+  KVR_TRY(kvr_embed_rows(m.embed, m.vocab, H, r.ids, r.id_count, r.positions, rows, hidden, nullptr, m.dtype,
+                         stream));
+  for (int l = 0; l < m.num_layers; ++l) {
+    const kvr_layer_weights& w = m.layers[l];
+    const bool final = l == m.num_layers - 1;
+    KVR_TRY(kvr_add_rmsnorm(hidden, l ? delta : nullptr, w.input_norm, normed, rows, H, H, H, H, m.eps, m.dtype,
+                            stream));
+    if (w.qkv) {
+      KVR_TRY(gemm(h, normed, H, w.qkv, qkv, qkv_w, rows, qkv_w, H, t));
+    } else {
+      if (!final) KVR_TRY(gemm(h, normed, H, w.q, qkv, qkv_w, rows, qd, H, t));
+      KVR_TRY(gemm(h, normed, H, w.k, qkv + qd * 2, qkv_w, rows, kd, H, t));
+      KVR_TRY(gemm(h, normed, H, w.v, qkv + (qd + kd) * 2, qkv_w, rows, kd, H, t));
+    }
+    KVR_TRY(kvr_qkv_rope_scatter(qkv, qkv + qd * 2, qkv + (qd + kd) * 2, qkv_w, qkv_w, qkv_w, w.q_norm, w.k_norm,
+                                 m.eps, r.cos_tab, r.sin_tab, r.positions, rows, m.q_heads, m.kv_heads, D,
+                                 final ? nullptr : q_rot, r.k_cache[l], r.v_cache[l], r.cache_rows,
+                                 r.cache_head_stride, r.cache_row_stride, nullptr, m.dtype, stream));
+    if (final) break;
+    KVR_TRY(kvr_selected_attention(q_rot, r.k_cache[l], r.v_cache[l], attn, r.positions, rows, m.q_heads,
+                                   m.kv_heads, D, r.cache_rows, r.cache_head_stride, r.cache_row_stride,
+                                   r.max_position, scale, r.attention_precision, attn_ws, attn_ws_bytes, m.dtype,
+                                   stream));
+    KVR_TRY(gemm(h, attn, qd, w.o, delta, H, rows, H, qd, t));
+    KVR_TRY(kvr_add_rmsnorm(hidden, delta, w.post_norm, normed, rows, H, H, H, H, m.eps, m.dtype, stream));
+    KVR_TRY(gemm(h, normed, H, w.gate, gate, I, rows, I, H, t));
+    KVR_TRY(gemm(h, normed, H, w.up, up, I, rows, I, H, t));
+    KVR_TRY(kvr_silu_mul(gate, up, act, rows, I, I, I, I, m.dtype, stream));
+    KVR_TRY(gemm(h, act, I, w.down, delta, H, rows, H, I, t));
+  }
+#undef KVR_TRY
+  return KVR_OK;
+}
+
+}  // extern "C"

@@ -4,10 +4,11 @@ This is the device side of ``packed_interval_repair``
 (kernels/packed_cache.py:225-298 of the reference). The reference drives the
 transformers decoder modules through a shallow "native view" whose cache
 layers scatter on update and whose attention is masked SDPA; this engine reads
-the same parameters and runs, per layer:
+the same parameters and makes one native call (``kvr_packed_refresh``) whose
+C++ layer loop runs, per layer:
 
     add_rmsnorm        residual add + input RMSNorm            (libkvr_b200)
-    q/k/v projections  one cuBLAS GEMM on [Wq; Wk; Wv]          (torch.mm)
+    q/k/v projections  one cuBLAS GEMM on [Wq; Wk; Wv]
     qkv_rope_scatter   q/k-norm, RoPE, q packing, K/V scatter   (libkvr_b200)
     selected_attention GQA split-KV flash attention             (libkvr_b200)
     o projection       cuBLAS
@@ -56,7 +57,7 @@ class LayerWeights:
     def fused_qkv(self) -> torch.Tensor:
         """``cat([Wq, Wk, Wv])`` for one GEMM per layer, rebuilt if any of the
         three parameters was replaced or modified in place since."""
-        key = tuple((id(t), t._version) for t in (self.q, self.k, self.v))
+        key = tuple((id(t), t.data_ptr(), t._version) for t in (self.q, self.k, self.v))
         if self.qkv is None or self.qkv_key != key:
             self.qkv = torch.cat((self.q, self.k, self.v), dim=0).contiguous()
             self.qkv_key = key
@@ -163,24 +164,28 @@ def model_view(base) -> ModelView:
     return view
 
 
-class Workspace:
-    """Per-request activation buffers ``[B, *]`` from torch's caching allocator."""
-
-    def __init__(self, view: ModelView, rows: int, cache_rows: int, device):
-        dt = view.dtype
-        qd, kd = view.heads * view.head_dim, view.kv_heads * view.head_dim
-        self.hidden = torch.empty((rows, view.hidden), dtype=dt, device=device)
-        self.normed = torch.empty((rows, view.hidden), dtype=dt, device=device)
-        self.delta = torch.empty((rows, view.hidden), dtype=dt, device=device)
-        self.qkv = torch.empty((rows, qd + 2 * kd), dtype=dt, device=device)
-        self.q_rot = torch.empty((rows, qd), dtype=dt, device=device)
-        self.attn = torch.empty((rows, qd), dtype=dt, device=device)
-        self.gate = torch.empty((rows, view.intermediate), dtype=dt, device=device)
-        self.up = torch.empty((rows, view.intermediate), dtype=dt, device=device)
-        self.act = torch.empty((rows, view.intermediate), dtype=dt, device=device)
-        ws = _lib.load().kvr_attention_workspace_size(rows, view.heads, view.kv_heads, view.head_dim,
-                                                      cache_rows)
-        self.attn_ws = torch.empty(max(int(ws), 16), dtype=torch.uint8, device=device)
+def _native_model(view: ModelView):
+    """The kvr_model struct for this view, refreshed when fused weights were rebuilt."""
+    qkv = [w.fused_qkv() for w in view.layers]
+    # Any replaced parameter storage changes a data pointer: rebuild the struct.
+    key = tuple(t.data_ptr() for t in qkv) + (view.embed.data_ptr(),) + tuple(
+        t.data_ptr() for w in view.layers for t in (w.in_norm, w.o, w.post_norm, w.gate, w.up, w.down))
+    if getattr(view, "_native_key", None) != key:
+        arr = (_lib.LayerWeights * len(view.layers))()
+        for i, (w, fused) in enumerate(zip(view.layers, qkv)):
+            arr[i] = _lib.LayerWeights(
+                input_norm=w.in_norm.data_ptr(), qkv=fused.data_ptr(), q=w.q.data_ptr(), k=w.k.data_ptr(),
+                v=w.v.data_ptr(), q_norm=w.q_norm.data_ptr() if w.q_norm is not None else None,
+                k_norm=w.k_norm.data_ptr() if w.k_norm is not None else None, o=w.o.data_ptr(),
+                post_norm=w.post_norm.data_ptr(), gate=w.gate.data_ptr(), up=w.up.data_ptr(),
+                down=w.down.data_ptr())
+        view._native_layers = arr
+        view._native = _lib.Model(
+            num_layers=len(view.layers), hidden=view.hidden, q_heads=view.heads, kv_heads=view.kv_heads,
+            head_dim=view.head_dim, intermediate=view.intermediate, vocab=view.vocab, eps=view.eps,
+            dtype=_lib.dtype_code(view.dtype), embed=view.embed.data_ptr(), layers=arr)
+        view._native_key = key
+    return view._native
 
 
 def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Tensor,
@@ -188,58 +193,29 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
     """Recompute the selected rows through every layer, writing K/V in place.
 
     ``layers``: the owned output cache, ``[(K, V)]`` each ``[1, Hkv, N, D]``
-    with unit D stride; ``ids``: ``[N]`` int64 on the device; ``positions``:
-    ``[B]`` int64 sorted, on the device. Runs on the current stream.
+    with unit D stride and one (head, row) stride pair; ``ids``: ``[N]`` int64
+    on the device; ``positions``: ``[B]`` int64 sorted, on the device. One
+    ``kvr_packed_refresh`` call runs every layer on the current stream.
     """
     lib = _lib.load()
     device = positions.device
     rows = positions.numel()
-    dt = _lib.dtype_code(view.dtype)
-    stream = _lib.stream_handle(device)
-    ws = Workspace(view, rows, cache_rows, device)
+    strides = {(t.stride(1), t.stride(2)) for pair in layers for t in pair}
+    if len(strides) != 1:
+        raise ValueError("every cache layer must share one (head, row) stride pair")
+    head_stride, row_stride = strides.pop()
+    model = _native_model(view)
     cos, sin = view.rope_tables(positions)
-    D, H = view.head_dim, view.hidden
-    qd, kd = view.heads * D, view.kv_heads * D
-    elem = ws.qkv.element_size()
-    scale = float(D) ** -0.5
-    pos_ptr = positions.data_ptr()
-    _lib.check(lib.kvr_embed_rows(view.embed.data_ptr(), view.vocab, H, ids.data_ptr(), ids.numel(),
-                                  pos_ptr, rows, ws.hidden.data_ptr(), None, dt, stream), "embed_rows")
-    last = len(view.layers) - 1
-    for index, w in enumerate(view.layers):
-        key, value = layers[index]
-        c_hs, c_rs = key.stride(1), key.stride(2)
-        _lib.check(lib.kvr_add_rmsnorm(ws.hidden.data_ptr(), ws.delta.data_ptr() if index else None,
-                                       w.in_norm.data_ptr(), ws.normed.data_ptr(), rows, H, H, H, H,
-                                       view.eps, dt, stream), "add_rmsnorm")
-        final = index == last
-        torch.mm(ws.normed, w.fused_qkv().t(), out=ws.qkv)
-        q_ptr = ws.qkv.data_ptr()
-        k_ptr = q_ptr + qd * elem
-        v_ptr = k_ptr + kd * elem
-        rs = ws.qkv.stride(0)
-        _lib.check(lib.kvr_qkv_rope_scatter(
-            q_ptr, k_ptr, v_ptr, rs, rs, rs, w.q_norm.data_ptr() if w.q_norm is not None else None,
-            w.k_norm.data_ptr() if w.k_norm is not None else None, view.eps, cos.data_ptr(),
-            sin.data_ptr(), pos_ptr, rows, view.heads, view.kv_heads, D,
-            None if final else ws.q_rot.data_ptr(), key.data_ptr(), value.data_ptr(), cache_rows,
-            c_hs, c_rs, None, dt, stream), "qkv_rope_scatter")
-        if final:
-            break
-        token = _timer.start("selected_attention") if _timer else None
-        _lib.check(lib.kvr_selected_attention(
-            ws.q_rot.data_ptr(), key.data_ptr(), value.data_ptr(), ws.attn.data_ptr(), pos_ptr, rows,
-            view.heads, view.kv_heads, D, cache_rows, c_hs, c_rs, max_position, scale, ATTENTION_PRECISION,
-            ws.attn_ws.data_ptr(), ws.attn_ws.numel(), dt, stream), "selected_attention")
-        if token:
-            _timer.stop(token)
-        torch.mm(ws.attn, w.o.t(), out=ws.delta)
-        _lib.check(lib.kvr_add_rmsnorm(ws.hidden.data_ptr(), ws.delta.data_ptr(), w.post_norm.data_ptr(),
-                                       ws.normed.data_ptr(), rows, H, H, H, H, view.eps, dt, stream),
-                   "add_rmsnorm")
-        torch.mm(ws.normed, w.gate.t(), out=ws.gate)
-        torch.mm(ws.normed, w.up.t(), out=ws.up)
-        I = view.intermediate
-        _lib.check(lib.kvr_silu_mul(ws.gate.data_ptr(), ws.up.data_ptr(), ws.act.data_ptr(), rows, I, I, I,
-                                    I, dt, stream), "silu_mul")
-        torch.mm(ws.act, w.down.t(), out=ws.delta)
+    k_ptrs = _lib.ptr_array([k for k, _ in layers])
+    v_ptrs = _lib.ptr_array([v for _, v in layers])
+    request = _lib.RefreshRequest(
+        k_cache=k_ptrs, v_cache=v_ptrs, cache_rows=cache_rows, cache_head_stride=head_stride,
+        cache_row_stride=row_stride, ids=ids.data_ptr(), id_count=ids.numel(), positions=positions.data_ptr(),
+        rows=rows, max_position=max_position, cos_tab=cos.data_ptr(), sin_tab=sin.data_ptr(),
+        attention_precision=ATTENTION_PRECISION)
+    need = lib.kvr_packed_refresh_workspace_size(model, rows, cache_rows)
+    if not need:
+        raise ValueError("model geometry is outside the built kernels")
+    workspace = torch.empty(need, dtype=torch.uint8, device=device)
+    _lib.check(lib.kvr_packed_refresh(model, request, workspace.data_ptr(), need, _lib.stream_handle(device)),
+               "packed_refresh")

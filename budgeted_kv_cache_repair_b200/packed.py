@@ -62,7 +62,9 @@ def _device_ids(edited_ids_t: torch.Tensor, device: torch.device) -> torch.Tenso
     ids = edited_ids_t[0]
     if ids.device != device:
         if ids.device.type == "cpu" and not ids.is_pinned():
-            ids = ids.pin_memory()
+            from .staging import upload_int64
+
+            return upload_int64(ids, device)
         ids = ids.to(device, non_blocking=True)
     if ids.dtype != torch.int64:
         ids = ids.to(torch.int64)

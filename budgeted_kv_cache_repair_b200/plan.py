@@ -82,19 +82,18 @@ class IndexedPlan:
             raise ValueError("device plan requires a CUDA device")
         if device.index is None:
             device = torch.device("cuda", torch.cuda.current_device())
+        from .staging import upload_int64
+
         with torch.cuda.device(device), torch.inference_mode(False):
-            host = torch.tensor(
-                [*self.positions, *self.full_prefix_tiles, *self.total_tiles], dtype=torch.int64
-            ).pin_memory()
-            packed = host.to(device, non_blocking=True)
+            # One stream-ordered copy through the pinned staging ring (no sync).
+            packed = upload_int64([*self.positions, *self.full_prefix_tiles, *self.total_tiles], device)
             count, tiles = len(self.positions), len(self.full_prefix_tiles)
             positions = packed[:count]
             full = packed[count:count + tiles]
             total = packed[count + tiles:]
         tensors = (positions, full, total)
         seal = (id(self), tuple(id(t) for t in tensors), tuple(t._version for t in tensors))
-        # Keep the pinned staging buffer alive until the copy has run.
-        return DeviceIndexedPlan(self, positions, full, total, seal, host)
+        return DeviceIndexedPlan(self, positions, full, total, seal)
 
 
 @dataclass(frozen=True)
@@ -107,7 +106,6 @@ class DeviceIndexedPlan:
     full_prefix_tiles: torch.Tensor
     total_tiles: torch.Tensor
     _seal: tuple | None = field(default=None, repr=False, compare=False)
-    _staging: torch.Tensor | None = field(default=None, repr=False, compare=False)
 
     @property
     def logical_length(self) -> int:

@@ -7,6 +7,7 @@ api.py:135-166, kernels/writeback.py:6-15).
 
 from __future__ import annotations
 
+import weakref
 from numbers import Integral
 from typing import Any, Sequence
 
@@ -109,6 +110,62 @@ def require_cuda_tensors(tensors, what: str) -> torch.device:
     return device
 
 
+class _ModuleScan:
+    """Flattened module/parameter lists of one model, so per-call checks need
+    no recursive traversal; rebuilt when the decoder's structure changes."""
+
+    __slots__ = ("fingerprint", "modules", "in_base", "params", "param_state")
+
+    def __init__(self, model, base, fingerprint):
+        self.fingerprint = fingerprint
+        base_ids = {id(m) for m in base.modules()}
+        self.modules = list(model.modules())
+        self.in_base = [id(m) in base_ids for m in self.modules]
+        self.params = [(p, inb) for m, inb in zip(self.modules, self.in_base)
+                       for p in m._parameters.values() if p is not None]
+        self.param_state = None
+
+
+_scans: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+
+
+def _fingerprint(model, base):
+    """Identities of the decoder's modules two levels below each layer."""
+    ids = [id(base), id(base.layers), id(getattr(model, "lm_head", None))]
+    for layer in base.layers:
+        ids.append(id(layer))
+        for child in layer._modules.values():
+            ids.append(id(child))
+            if child is not None:
+                ids.extend(map(id, child._modules.values()))
+    return tuple(ids)
+
+
+def _check_modules(model, base, device, dtype):
+    fp = _fingerprint(model, base)
+    scan = _scans.get(model)
+    if scan is None or scan.fingerprint != fp:
+        scan = _ModuleScan(model, base, fp)
+        _scans[model] = scan
+    for module, in_base in zip(scan.modules, scan.in_base):
+        if module.training:
+            raise ValueError("packed executor requires eval mode on all decoder modules")
+        state = module.__dict__
+        if state.get("_hf_hook") is not None:
+            raise ValueError("packed executor does not support dispatch/offload hooks")
+        if in_base and "forward" in state:
+            raise ValueError("packed executor does not support per-instance decoder forward overrides")
+    # Parameter placement only needs re-checking when some parameter moved.
+    state = (device, dtype, tuple(p.data_ptr() for p, _ in scan.params))
+    if scan.param_state != state:
+        for p, in_base in scan.params:
+            if p.device != device:
+                raise ValueError("packed executor requires all model parameters on the request device")
+            if in_base and p.dtype != dtype:
+                raise ValueError("model parameters and cache must share one bfloat16/float16 dtype")
+        scan.param_state = state
+
+
 def qualify_model(model: Any, base: Any, layer_count: int, device: torch.device, dtype: torch.dtype) -> None:
     """Model contract of the packed path (kernels/packed_cache.py:123-163, api.py:135-166).
 
@@ -122,8 +179,6 @@ def qualify_model(model: Any, base: Any, layer_count: int, device: torch.device,
     pairs = {(LlamaForCausalLM, LlamaModel), (Qwen3ForCausalLM, Qwen3Model)}
     if (type(model), type(base)) not in pairs and type(model) not in (LlamaModel, Qwen3Model):
         raise ValueError("packed executor requires exact native dense Llama or Qwen3 classes")
-    if model.training or base.training or any(module.training for module in base.modules()):
-        raise ValueError("packed executor requires eval mode on all decoder modules")
     config = model.config
     if config.num_hidden_layers != layer_count or len(base.layers) != layer_count:
         raise ValueError("model and cache layer counts must agree")
@@ -138,17 +193,10 @@ def qualify_model(model: Any, base: Any, layer_count: int, device: torch.device,
         raise ValueError("packed executor requires full attention")
     if any(kind != "full_attention" for kind in getattr(config, "layer_types", []) or []):
         raise ValueError("packed executor rejects sliding/hybrid attention")
-    if any(parameter.device != device for parameter in model.parameters()):
-        raise ValueError("packed executor requires all model parameters on the request device")
-    if any(getattr(module, "_hf_hook", None) is not None for module in model.modules()):
-        raise ValueError("packed executor does not support dispatch/offload hooks")
-    if any("forward" in module.__dict__ for module in base.modules()):
-        raise ValueError("packed executor does not support per-instance decoder forward overrides")
+    _check_modules(model, base, device, dtype)
     if getattr(model, "is_quantized", False):
         raise ValueError("packed executor does not support quantized models")
     if getattr(config, "hidden_act", "silu") != "silu":
         raise ValueError("packed executor implements the SiLU-gated MLP only")
     if getattr(config, "attention_bias", False) or getattr(config, "mlp_bias", False):
         raise ValueError("packed executor implements bias-free projections only")
-    if any(parameter.dtype != dtype for parameter in base.parameters()):
-        raise ValueError("model parameters and cache must share one bfloat16/float16 dtype")

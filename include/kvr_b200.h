@@ -196,6 +196,64 @@ KVR_API int kvr_selected_attention(const void* q, const void* k_cache, const voi
                                    void* workspace, size_t workspace_bytes, int dtype, void* stream);
 
 /*
+ * Whole packed refresh in one call: the selected rows run through every
+ * decoder layer of a dense Llama/Qwen3 model on `stream`, and each layer's
+ * fresh K/V rows are written into the cache at their absolute positions.
+ * Replaces the native transformers forward of packed_interval_repair
+ * (kernels/packed_cache.py:284-297: _make_native_view, the _PackedLayer cache
+ * and the per-layer decoder modules). Weights are the model's own tensors
+ * (row-major [out, in], nn.Linear layout); `qkv` may point to the rows of
+ * Wq, Wk, Wv stacked into one matrix (one GEMM per layer) or be NULL with
+ * q/k/v set. q_norm/k_norm are the Qwen3 per-head RMSNorm weights or NULL.
+ * The caller owns the output cache and has already copied the base into it;
+ * cos_tab/sin_tab are the model's rotary cos/sin at the selected positions
+ * ([rows, head_dim], model dtype). `workspace` holds
+ * kvr_packed_refresh_workspace_size() bytes of activations and attention
+ * scratch (any contents). Projections run on cuBLAS (fp32 accumulation).
+ */
+typedef struct kvr_layer_weights {
+  const void* input_norm;  /* [hidden] */
+  const void* qkv;         /* [(q_heads + 2*kv_heads) * head_dim, hidden] or NULL */
+  const void* q;           /* [q_heads * head_dim, hidden] (when qkv == NULL) */
+  const void* k;           /* [kv_heads * head_dim, hidden] */
+  const void* v;           /* [kv_heads * head_dim, hidden] */
+  const void* q_norm;      /* [head_dim] or NULL */
+  const void* k_norm;      /* [head_dim] or NULL */
+  const void* o;           /* [hidden, q_heads * head_dim] */
+  const void* post_norm;   /* [hidden] */
+  const void* gate;        /* [intermediate, hidden] */
+  const void* up;          /* [intermediate, hidden] */
+  const void* down;        /* [hidden, intermediate] */
+} kvr_layer_weights;
+
+typedef struct kvr_model {
+  int num_layers, hidden, q_heads, kv_heads, head_dim, intermediate;
+  int64_t vocab;
+  float eps;               /* rms_norm_eps */
+  int dtype;               /* KVR_DTYPE_* of weights, cache and activations */
+  const void* embed;       /* [vocab, hidden] */
+  const kvr_layer_weights* layers;  /* num_layers entries (host memory) */
+} kvr_model;
+
+typedef struct kvr_refresh_request {
+  void* const* k_cache;    /* num_layers device pointers, [kv_heads, cache_rows, head_dim] */
+  void* const* v_cache;
+  int64_t cache_rows, cache_head_stride, cache_row_stride;
+  const int64_t* ids;      /* device [id_count] token ids of the edited prompt */
+  int64_t id_count;
+  const int64_t* positions;  /* device [rows], strictly increasing */
+  int64_t rows;
+  int64_t max_position;    /* positions[rows-1], from the host plan */
+  const void* cos_tab;     /* device [rows, head_dim] */
+  const void* sin_tab;
+  int attention_precision; /* KVR_ATTN_P_* */
+} kvr_refresh_request;
+
+KVR_API size_t kvr_packed_refresh_workspace_size(const kvr_model* model, int64_t rows, int64_t cache_rows);
+KVR_API int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* request, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/*
  * kvr_selected_attention without a caller-provided workspace, for callers
  * that cannot allocate device memory per call (for example a host runtime
  * reaching this library over a plain C FFI with a fixed, pre-planned GPU
