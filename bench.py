@@ -469,6 +469,117 @@ def our_arm(args):
         dist.destroy_process_group()
 
 
+CONFIG_70B = dict(name="llama3-70b-shape", layers=80, hidden=8192, heads=64, kv_heads=8, head_dim=128,
+                  intermediate=28672, vocab=128256, theta=500000.0, context=16384, delete_at=2048, delete=512,
+                  intervals=16, budget_percent=10)
+METRIC_TP = "repaired rows/s (packed refresh stage, Llama-3-70B shape, 16384 ctx, 10% budget, head-sharded TP)"
+
+
+def tp_arm(args):
+    """Llama-3-70B shape, KV heads sharded across the
+    ranks, NCCL all-reduce after o_proj and down_proj (inside the native loop).
+    Each rank generates its own weight shard (seeded per layer and rank) and
+    its heads of a stale cache; one request is refreshed by all ranks together
+    (strong scaling)."""
+    import datetime
+    import math
+
+    import torch.distributed as dist
+
+    from budgeted_kv_cache_repair_b200 import _lib
+    from budgeted_kv_cache_repair_b200 import build as native_build
+    from budgeted_kv_cache_repair_b200.cache import allocate_layers, copy_layers
+    from budgeted_kv_cache_repair_b200.plan import IndexedPlan
+    from budgeted_kv_cache_repair_b200.tp import ShardView, TPGroup, refresh_rows_tp
+
+    world, rank, local = _dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    native_build.build()
+    _lib.load()
+    cfg = dict(CONFIG_70B)
+    h, d, inter = cfg["hidden"], cfg["head_dim"], cfg["intermediate"]
+    heads, kv = cfg["heads"], cfg["kv_heads"]
+    hq, hk, im = heads // world, kv // world, inter // world
+    gen = torch.Generator(device=device)
+
+    def w(seed, *shape):
+        gen.manual_seed(seed)
+        return (0.02 * torch.randn(shape, device=device, generator=gen, dtype=torch.float32)).to(torch.bfloat16)
+
+    layers = []
+    for l in range(cfg["layers"]):
+        s0 = 1000003 * (l + 1) + 7919 * rank
+        layers.append({"in_norm": torch.ones(h, device=device, dtype=torch.bfloat16),
+                       "post_norm": torch.ones(h, device=device, dtype=torch.bfloat16),
+                       "q": w(s0, hq * d, h), "k": w(s0 + 1, hk * d, h), "v": w(s0 + 2, hk * d, h),
+                       "o": w(s0 + 3, h, hq * d), "gate": w(s0 + 4, im, h), "up": w(s0 + 5, im, h),
+                       "down": w(s0 + 6, h, im)})
+    embed = w(17, cfg["vocab"], h)
+    inv_freq = 1.0 / (cfg["theta"] ** (torch.arange(0, d, 2, dtype=torch.int64).float() / d))
+    view = ShardView(embed=embed, layers=layers, hidden=h, heads=heads, kv_heads=kv, head_dim=d, intermediate=inter,
+                     eps=1e-5, inv_freq=inv_freq, rank=0, world=world)
+    length = cfg["context"] - cfg["delete"]
+    suffix = length - cfg["delete_at"]
+    rows = math.ceil(suffix * cfg["budget_percent"] / 100)
+    width = rows // cfg["intervals"]
+    intervals = make_intervals(4, cfg["delete_at"], length, cfg["intervals"], width)
+    extra = rows - width * cfg["intervals"]
+    if extra:  # widen the last interval so the budget is exact
+        a, b = intervals[-1]
+        intervals[-1] = (a, b + extra)
+    positions = [p for a, b in intervals for p in range(a, b)]
+    gen.manual_seed(99)
+    ids = torch.randint(0, cfg["vocab"], (length,), device=device, generator=gen)
+    base = allocate_layers(cfg["layers"], hk, length, d, torch.bfloat16, device)
+    for k_, v_ in base:
+        k_.normal_(generator=gen)
+        v_.normal_(generator=gen).mul_(0.5)
+    plan = IndexedPlan(positions, length)
+    group = TPGroup(rank, world, device) if world > 1 else None
+
+    def step():
+        owned = copy_layers(base)
+        dp = plan.to(device)
+        refresh_rows_tp(view, owned, ids, dp.positions, plan.max_position, length, group)
+        return owned
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    stream = torch.cuda.current_stream()
+    b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b.record(stream)
+    for _ in range(args.steps):
+        step()
+    e.record(stream)
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(b.elapsed_time(e), world) / args.steps
+    launches = _lib.load().kvr_kernel_launches()
+    if group is not None:
+        group.close()
+    if rank == 0:
+        hbm, tflops, src = _peaks()
+        params = (h * hq * d + 2 * h * hk * d + hq * d * h + 3 * h * im)
+        gemm_flops = 2.0 * params * rows * cfg["layers"]
+        attn_flops = 4.0 * hq * d * sum(p + 1 for p in positions) * cfg["layers"]
+        per_gpu_tflops = (gemm_flops + attn_flops) / (ms / 1e3) / 1e12
+        line = {"metric": METRIC_TP, "value": rows / (ms / 1e3), "unit": "rows/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random shards)",
+                "config": {"workload": "config4: Llama-3-70B shape, 16384 ctx, delete 512@2048, 10% budget",
+                           "rows": rows, "logical_length": length, "intervals": len(intervals),
+                           "parallelism": f"tp{world}"},
+                "per_gpu": {"tflops": per_gpu_tflops, "frac_bf16_peak": per_gpu_tflops / tflops,
+                            "peak_source": src}}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
@@ -476,11 +587,15 @@ def main():
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    parser.add_argument("--workload", choices=["config2", "70b-tp"], default="config2",
+                        help="config2: Llama-3-8B refresh (DP replicas when N>1); 70b-tp: configs[4], head-sharded")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
     if args.impl == "reference":
         reference_arm(args)
+    elif args.workload == "70b-tp":
+        tp_arm(args)
     else:
         our_arm(args)
 

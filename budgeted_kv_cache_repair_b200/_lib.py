@@ -20,6 +20,7 @@ OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_SCRATCH_LIMIT =
 STATIC_SCRATCH_BYTES = 16 << 20
 DTYPE_BF16, DTYPE_F16 = 0, 1
 ATTN_P_SPLIT, ATTN_P_ROUNDED = 0, 1
+TP_ID_BYTES = 128
 MAX_LAYER_TENSORS = 256
 
 _P = ctypes.c_void_p
@@ -48,7 +49,8 @@ class RefreshRequest(ctypes.Structure):
                 ("cache_rows", ctypes.c_int64), ("cache_head_stride", ctypes.c_int64),
                 ("cache_row_stride", ctypes.c_int64), ("ids", ctypes.c_void_p), ("id_count", ctypes.c_int64),
                 ("positions", ctypes.c_void_p), ("rows", ctypes.c_int64), ("max_position", ctypes.c_int64),
-                ("cos_tab", ctypes.c_void_p), ("sin_tab", ctypes.c_void_p), ("attention_precision", ctypes.c_int)]
+                ("cos_tab", ctypes.c_void_p), ("sin_tab", ctypes.c_void_p), ("attention_precision", ctypes.c_int),
+                ("tp_comm", ctypes.c_void_p)]
 
 
 # name -> (restype, argtypes); mirrors include/kvr_b200.h one to one.
@@ -72,6 +74,9 @@ SIGNATURES = {
                                     ctypes.c_size_t, _I, _P]),
     "kvr_packed_refresh_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(Model), _L, _L]),
     "kvr_packed_refresh": (_I, [ctypes.POINTER(Model), ctypes.POINTER(RefreshRequest), _P, ctypes.c_size_t, _P]),
+    "kvr_tp_unique_id": (_I, [_P]),
+    "kvr_tp_comm_init": (_I, [_P, _I, _I, ctypes.POINTER(ctypes.c_void_p)]),
+    "kvr_tp_comm_destroy": (_I, [_P]),
     "kvr_selected_attention_static": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _I, _I, _P]),
 }
 

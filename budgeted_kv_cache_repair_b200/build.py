@@ -76,7 +76,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
         for _, log in results:
             print(log)
     tmp = LIBRARY + ".tmp"
-    cmd = [compiler, *ARCH, "-shared", "-o", tmp, *[o for o, _ in results], "-lcudart", "-lcublas",
+    cmd = [compiler, *ARCH, "-shared", "-o", tmp, *[o for o, _ in results], "-lcudart", "-lcublas", "-lnccl",
            "-Xlinker", "-rpath=" + CUDA_LIB]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode:

@@ -9,7 +9,15 @@
 //
 // Host work per layer is a handful of launches from C++, so the GPU, not the
 // Python interpreter, sets the pace at a few dozen rows.
+//
+// Tensor parallelism (optional): each rank holds its share of the query/KV
+// heads (column-parallel q/k/v and gate/up, row-parallel o and down, its heads'
+// cache) and the two row-parallel projections' partial sums are all-reduced in
+// place with NCCL on the same stream, before the residual add.
 #include <cublas_v2.h>
+#include <nccl.h>
+
+#include <string.h>
 
 #include <mutex>
 #include <unordered_map>
@@ -83,6 +91,13 @@ int gemm(cublasHandle_t h, const void* x, int64_t ldx, const void* w, void* y, i
                                          static_cast<int>(ldx), &zero, y, t, static_cast<int>(ldy),
                                          CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
   return st == CUBLAS_STATUS_SUCCESS ? KVR_OK : KVR_ERR_CUDA;
+}
+
+int allreduce(void* buf, int64_t count, int dtype, void* comm, cudaStream_t s) {
+  const ncclResult_t st = ncclAllReduce(buf, buf, static_cast<size_t>(count),
+                                        dtype == KVR_DTYPE_BF16 ? ncclBfloat16 : ncclFloat16, ncclSum,
+                                        static_cast<ncclComm_t>(comm), s);
+  return st == ncclSuccess ? KVR_OK : KVR_ERR_CUDA;
 }
 
 bool valid_model(const kvr_model* m) {
@@ -184,14 +199,40 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
                                    r.max_position, scale, r.attention_precision, attn_ws, attn_ws_bytes, m.dtype,
                                    stream));
     KVR_TRY(gemm(h, attn, qd, w.o, delta, H, rows, H, qd, t));
+    if (r.tp_comm) KVR_TRY(allreduce(delta, rows * H, m.dtype, r.tp_comm, s));
     KVR_TRY(kvr_add_rmsnorm(hidden, delta, w.post_norm, normed, rows, H, H, H, H, m.eps, m.dtype, stream));
     KVR_TRY(gemm(h, normed, H, w.gate, gate, I, rows, I, H, t));
     KVR_TRY(gemm(h, normed, H, w.up, up, I, rows, I, H, t));
     KVR_TRY(kvr_silu_mul(gate, up, act, rows, I, I, I, I, m.dtype, stream));
     KVR_TRY(gemm(h, act, I, w.down, delta, H, rows, H, I, t));
+    if (r.tp_comm) KVR_TRY(allreduce(delta, rows * H, m.dtype, r.tp_comm, s));
   }
 #undef KVR_TRY
   return KVR_OK;
+}
+
+int kvr_tp_unique_id(void* out) {
+  if (!out) return KVR_ERR_INVALID_ARG;
+  static_assert(sizeof(ncclUniqueId) == KVR_TP_ID_BYTES, "NCCL unique id size");
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return KVR_ERR_CUDA;
+  memcpy(out, &id, sizeof(id));
+  return KVR_OK;
+}
+
+int kvr_tp_comm_init(const void* unique_id, int nranks, int rank, void** comm_out) {
+  if (!unique_id || !comm_out || nranks < 1 || rank < 0 || rank >= nranks) return KVR_ERR_INVALID_ARG;
+  ncclUniqueId id;
+  memcpy(&id, unique_id, sizeof(id));
+  ncclComm_t comm = nullptr;
+  if (ncclCommInitRank(&comm, nranks, id, rank) != ncclSuccess) return KVR_ERR_CUDA;
+  *comm_out = comm;
+  return KVR_OK;
+}
+
+int kvr_tp_comm_destroy(void* comm) {
+  if (!comm) return KVR_OK;
+  return ncclCommDestroy(static_cast<ncclComm_t>(comm)) == ncclSuccess ? KVR_OK : KVR_ERR_CUDA;
 }
 
 }  // extern "C"

@@ -189,7 +189,7 @@ def _native_model(view: ModelView):
 
 
 def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Tensor,
-                 max_position: int, cache_rows: int) -> None:
+                 max_position: int, cache_rows: int, tp_comm=None) -> None:
     """Recompute the selected rows through every layer, writing K/V in place.
 
     ``layers``: the owned output cache, ``[(K, V)]`` each ``[1, Hkv, N, D]``
@@ -212,7 +212,7 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
         k_cache=k_ptrs, v_cache=v_ptrs, cache_rows=cache_rows, cache_head_stride=head_stride,
         cache_row_stride=row_stride, ids=ids.data_ptr(), id_count=ids.numel(), positions=positions.data_ptr(),
         rows=rows, max_position=max_position, cos_tab=cos.data_ptr(), sin_tab=sin.data_ptr(),
-        attention_precision=ATTENTION_PRECISION)
+        attention_precision=ATTENTION_PRECISION, tp_comm=tp_comm)
     need = lib.kvr_packed_refresh_workspace_size(model, rows, cache_rows)
     if not need:
         raise ValueError("model geometry is outside the built kernels")

@@ -247,7 +247,22 @@ typedef struct kvr_refresh_request {
   const void* cos_tab;     /* device [rows, head_dim] */
   const void* sin_tab;
   int attention_precision; /* KVR_ATTN_P_* */
+  void* tp_comm;           /* NULL, or a communicator from kvr_tp_comm_init: the model is this
+                              rank's head/column shard and the o/down partial sums are
+                              all-reduced (sum) across the group after each projection */
 } kvr_refresh_request;
+
+/*
+ * Tensor-parallel group for kvr_packed_refresh (NCCL over NVLink). No
+ * counterpart in the reference, which runs on one device (api.py:156-160).
+ * kvr_tp_unique_id writes KVR_TP_ID_BYTES bytes on one rank; every rank passes
+ * the same bytes to kvr_tp_comm_init (collective over the group, with each
+ * rank's device current). kvr_tp_comm_destroy releases it.
+ */
+#define KVR_TP_ID_BYTES 128
+KVR_API int kvr_tp_unique_id(void* out);
+KVR_API int kvr_tp_comm_init(const void* unique_id, int nranks, int rank, void** comm_out);
+KVR_API int kvr_tp_comm_destroy(void* comm);
 
 KVR_API size_t kvr_packed_refresh_workspace_size(const kvr_model* model, int64_t rows, int64_t cache_rows);
 KVR_API int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* request, void* workspace,
