@@ -20,9 +20,11 @@ flush is needed between steps. Times are CUDA events on the launching stream,
 max over ranks. With N GPUs each rank repairs its own request (different seed,
 no collective on the data path): weak scaling.
 
-``--impl reference`` times the reference algorithm's CPU restatement (oracle/,
-the reference package itself cannot be installed on the GPU box) on all host
-cores on a bounded sample of the same workload, on rank 0 only.
+``--impl reference`` times the reference's packed path restated on the same
+transformers modules (oracle/hf_packed.py; the reference package itself cannot
+be installed on the GPU box) on all host cores, on a bounded sample of the same
+workload (2 of 32 layers, scaled), on rank 0 only. ``--impl reference --device
+cuda`` times that path on one B200 at full depth (the GPU comparator).
 """
 
 from __future__ import annotations
@@ -228,47 +230,73 @@ def refresh_bytes(cfg, length):
     return weights + 2 * cache + cache, params
 
 
-def run_cpu_baseline(cfg, sample_layers, threads, seed=0):
-    """Reference algorithm (oracle CPU restatement) on a bounded sample:
-    ``sample_layers`` of the workload's layers, full context and rows; rows/s
-    scaled to the full depth."""
-    from oracle import packed_oracle as oracle
-
-    torch.set_num_threads(threads)
-    gen = torch.Generator().manual_seed(seed)
-    h, i, d = cfg["hidden"], cfg["intermediate"], cfg["head_dim"]
-    q, kv = cfg["heads"] * d, cfg["kv_heads"] * d
-
-    def w(*shape):
-        return (0.02 * torch.randn(shape, generator=gen)).to(torch.bfloat16)
-
-    layers = [dict(in_norm=torch.ones(h, dtype=torch.bfloat16), q=w(q, h), k=w(kv, h), v=w(kv, h), o=w(h, q),
-                   post_norm=torch.ones(h, dtype=torch.bfloat16), gate=w(i, h), up=w(i, h), down=w(h, i))
-              for _ in range(sample_layers)]
-    model = oracle.OracleModel(embed=w(cfg["vocab"], h), layers=layers, heads=cfg["heads"],
-                               kv_heads=cfg["kv_heads"], head_dim=d, eps=1e-5,
-                               inv_freq=oracle.default_inv_freq(cfg["theta"], d), qk_norm=False)
+def _sample_request(cfg, seed, device, layers):
+    """Shifted-cache stand-in (K ~ N(0,1), V ~ N(0,0.5)), edited ids and the
+    benchmark's intervals for ``layers`` layers on ``device``."""
+    gen = torch.Generator(device=device).manual_seed(seed)
     length = cfg["context"] - cfg["delete"]
-    ids = torch.randint(0, cfg["vocab"], (length,), generator=gen)
-    base = [((torch.randn((1, cfg["kv_heads"], length, d), generator=gen)).to(torch.bfloat16),
-             (0.5 * torch.randn((1, cfg["kv_heads"], length, d), generator=gen)).to(torch.bfloat16))
-            for _ in range(sample_layers)]
+    ids = torch.randint(0, cfg["vocab"], (1, length), device=device, generator=gen)
+    shape = (1, cfg["kv_heads"], length, cfg["head_dim"])
+    base = [(torch.randn(shape, device=device, generator=gen).to(torch.bfloat16),
+             (0.5 * torch.randn(shape, device=device, generator=gen)).to(torch.bfloat16)) for _ in range(layers)]
     width = cfg["rows"] // cfg["intervals"]
     intervals = make_intervals(seed, cfg["delete_at"], length, cfg["intervals"], width)
-    positions = [p for a, b in intervals for p in range(a, b)]
-    oracle.packed_refresh(model, base, ids, positions)  # warm-up
+    return ids, base, [p for a, b in intervals for p in range(a, b)]
+
+
+def run_cpu_baseline(cfg, sample_layers, threads, seed=0):
+    """The reference's packed path (oracle/hf_packed.py: transformers modules,
+    index_copy_ cache layers, masked SDPA, two-copy clone) on the host cores,
+    on a bounded sample: ``sample_layers`` of the model's layers at full
+    context and rows; rows/s scaled to the full depth."""
+    from oracle.hf_packed import packed_refresh_hf
+
+    torch.set_num_threads(threads)
+    small = dict(cfg, layers=sample_layers)
+    model = build_model(small, seed, torch.device("cpu"))
+    ids, base, positions = _sample_request(cfg, seed, torch.device("cpu"), sample_layers)
+    packed_refresh_hf(model.model, base, ids, positions)  # warm-up
     reps, t0 = 0, time.perf_counter()
     while True:
-        oracle.packed_refresh(model, base, ids, positions)
+        packed_refresh_hf(model.model, base, ids, positions)
         reps += 1
         if time.perf_counter() - t0 > 8.0 or reps >= 5:
             break
     per_step = (time.perf_counter() - t0) / reps
     per_request = per_step * cfg["layers"] / sample_layers
     return {"value": len(positions) / per_request, "unit": "rows/s", "cores": threads, "kind": "port",
-            "sample": f"{sample_layers} of {cfg['layers']} layers (full context {length}, {len(positions)} rows), "
-                      f"{reps} timed reps, scaled x{cfg['layers'] / sample_layers:g} to full depth",
+            "sample": f"{sample_layers} of {cfg['layers']} layers (full context {ids.shape[1]}, {len(positions)} rows), "
+                      f"{reps} timed reps, scaled x{cfg['layers'] / sample_layers:g} to full depth; the reference's "
+                      f"packed path restated on the same transformers modules (oracle/hf_packed.py)",
             "ms_per_request": per_request * 1e3}
+
+
+def gpu_comparator(args):
+    """The reference's packed SDPA path (oracle/hf_packed.py) on one B200 at
+    full depth: the "reference CUDA SDPA path" the north star compares with.
+    Same workload as our arm; CUDA events around each call, median."""
+    device = torch.device("cuda", 0)
+    cfg = dict(CONFIG)
+    from oracle.hf_packed import packed_refresh_hf
+
+    model = build_model(cfg, 1, device)
+    ids, base, positions = _sample_request(cfg, 1, device, cfg["layers"])
+    for _ in range(args.warmup):
+        packed_refresh_hf(model.model, base, ids, positions)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b.record()
+        packed_refresh_hf(model.model, base, ids, positions)
+        e.record()
+        e.synchronize()
+        times.append(b.elapsed_time(e))
+    ms = statistics.median(times)
+    print(json.dumps({"impl": "reference-cuda-comparator", "metric": METRIC, "value": len(positions) / (ms / 1e3),
+                      "unit": "rows/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                      "n_gpus": 1, "note": "reference packed SDPA path restated on transformers (oracle/hf_packed.py)"}),
+          flush=True)
 
 
 def reference_arm(args):
@@ -587,12 +615,16 @@ def main():
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    parser.add_argument("--device", choices=["cpu", "cuda"], default="cpu",
+                        help="with --impl reference: cpu (the reference arm) or cuda (the GPU comparator)")
     parser.add_argument("--workload", choices=["config2", "70b-tp"], default="config2",
                         help="config2: Llama-3-8B refresh (DP replicas when N>1); 70b-tp: configs[4], head-sharded")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
-    if args.impl == "reference":
+    if args.impl == "reference" and args.device == "cuda":
+        gpu_comparator(args)
+    elif args.impl == "reference":
         reference_arm(args)
     elif args.workload == "70b-tp":
         tp_arm(args)

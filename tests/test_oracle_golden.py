@@ -104,3 +104,22 @@ def test_attention_oracles_agree_on_closed_form():
         torch.testing.assert_close(out[row], torch.full((4, 8), p / 2))
     fp64 = oracle.selected_attention_fp64(q.permute(1, 0, 2)[None], k[None], v[None], positions)
     torch.testing.assert_close(fp64[0].permute(1, 0, 2).float(), out)
+
+
+@pytest.mark.parametrize("name", golden_cases())
+def test_transformers_restatement_matches_reference(name):
+    """oracle.hf_packed (the timed reference arm and GPU comparator) reproduces
+    the reference's packed outputs on the same transformers modules."""
+    from helpers import fixture_model
+    from oracle.hf_packed import packed_refresh_hf
+
+    record = load_golden(name)
+    model = fixture_model(record, "cpu")
+    out = packed_refresh_hf(model.model, record["shifted_layers"], record["new_ids"], record["positions"])
+    pos = torch.tensor(record["positions"])
+    for (k, v), (ek, ev), (bk, bv) in zip(out, record["packed_rows"], record["shifted_layers"]):
+        for got, expected in ((k[:, :, pos], ek), (v[:, :, pos], ev)):
+            torch.testing.assert_close(got, expected, rtol=1e-5, atol=2e-6)
+        keep = torch.ones(k.shape[2], dtype=torch.bool)
+        keep[pos] = False
+        assert torch.equal(k[:, :, keep], bk[:, :, keep]) and torch.equal(v[:, :, keep], bv[:, :, keep])
