@@ -50,7 +50,17 @@ class RefreshRequest(ctypes.Structure):
                 ("cache_row_stride", ctypes.c_int64), ("ids", ctypes.c_void_p), ("id_count", ctypes.c_int64),
                 ("positions", ctypes.c_void_p), ("rows", ctypes.c_int64), ("max_position", ctypes.c_int64),
                 ("cos_tab", ctypes.c_void_p), ("sin_tab", ctypes.c_void_p), ("attention_precision", ctypes.c_int),
-                ("tp_comm", ctypes.c_void_p)]
+                ("tp_comm", ctypes.c_void_p), ("projections", ctypes.c_int)]
+
+
+LINEAR_MAX_SEGMENTS = 4
+PROJ_CUBLAS, PROJ_SM100 = 0, 1
+
+
+class LinearSegment(ctypes.Structure):
+    """kvr_linear_segment"""
+    _fields_ = [("weight", ctypes.c_void_p), ("weight_up", ctypes.c_void_p), ("n", ctypes.c_int64),
+                ("out", ctypes.c_void_p), ("out_stride", ctypes.c_int64)]
 
 
 # name -> (restype, argtypes); mirrors include/kvr_b200.h one to one.
@@ -69,6 +79,8 @@ SIGNATURES = {
     "kvr_qkv_rope_scatter": (_I, [_P, _P, _P, _L, _L, _L, _P, _P, _F, _P, _P, _P, _L, _I, _I, _I,
                                   _P, _P, _P, _L, _L, _L, _P, _I, _P]),
     "kvr_silu_mul": (_I, [_P, _P, _P, _L, _L, _L, _L, _L, _I, _P]),
+    "kvr_linear_workspace_size": (ctypes.c_size_t, [_L, _L, ctypes.POINTER(LinearSegment), _I]),
+    "kvr_linear": (_I, [_P, _L, _L, _L, ctypes.POINTER(LinearSegment), _I, _P, ctypes.c_size_t, _I, _P]),
     "kvr_attention_workspace_size": (ctypes.c_size_t, [_L, _I, _I, _I, _L]),
     "kvr_selected_attention": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _I, _P,
                                     ctypes.c_size_t, _I, _P]),

@@ -144,6 +144,8 @@ template <class T, int D, bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                    const __grid_constant__ CUtensorMap tmap_q, Args a) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
   using L = Layout<D, SPLIT>;
   constexpr int DS = L::DS, NS = L::NS, NP = L::NP;
   constexpr int HD = D / 2;  // output columns per softmax thread in the epilogue
@@ -517,6 +519,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 // any use, so the merge is one memory round trip per batch, not per chunk.
 template <class T, int D>
 __global__ void __launch_bounds__(256) attn_combine_kernel(Args a) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
   constexpr int PER = D / 32;  // values per lane
   constexpr int BATCH = 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -671,7 +675,8 @@ inline bool make_q_map(CUtensorMap* map, const void* ptr, bool bf16, int head_di
 }
 
 template <class T, int D, bool SPLIT>
-int launch(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, const Args& a, cudaStream_t s) {
+int launch(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, const Args& a, cudaStream_t s,
+           bool status_zeroed) {
   constexpr int smem = Layout<D, SPLIT>::BYTES;
   static int configured[64] = {0};
   int dev = 0;
@@ -688,18 +693,19 @@ int launch(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, 
     }
     if (dev >= 0 && dev < 64) __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
   }
-  e = cudaMemsetAsync(a.status, 0, sizeof(int), s);
-  if (e != cudaSuccess) {
-    set_last_cuda_error(e);
-    return KVR_ERR_CUDA;
+  if (!status_zeroed) {
+    e = cudaMemsetAsync(a.status, 0, sizeof(int), s);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return KVR_ERR_CUDA;
+    }
   }
   dim3 grid(a.tiles * a.nchunks, a.hkv);
-  attn_tc_kernel<T, D, SPLIT><<<grid, THREADS, smem, s>>>(mk, mv, mq, a);
-  int st = check_launch();
+  int st = launch_pdl<attn_tc_kernel<T, D, SPLIT>>(grid, dim3(THREADS), smem, s, 1, mk, mv, mq, a);
   if (st != KVR_OK || a.nchunks == 1) return st;
   const int64_t total_m = a.rows * a.group;
-  attn_combine_kernel<T, D><<<dim3(static_cast<unsigned>((total_m + 7) / 8), a.hkv), 256, 0, s>>>(a);
-  return check_launch();
+  return launch_pdl<attn_combine_kernel<T, D>>(dim3(static_cast<unsigned>((total_m + 7) / 8), a.hkv), dim3(256), 0,
+                                               s, 1, a);
 }
 
 }  // namespace attn
@@ -723,6 +729,20 @@ int kvr_selected_attention(const void* q, const void* k_cache, const void* v_cac
                            int64_t cache_row_stride, int64_t max_position, float scale,
                            int precision, void* workspace, size_t workspace_bytes, int dtype,
                            void* stream) {
+  return kvr::selected_attention(q, k_cache, v_cache, out, positions, rows, q_heads, kv_heads, head_dim, cache_rows,
+                                 cache_head_stride, cache_row_stride, max_position, scale, precision, workspace,
+                                 workspace_bytes, dtype, stream, false);
+}
+
+}  // extern "C"
+
+namespace kvr {
+
+int selected_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                       const int64_t* positions, int64_t rows, int q_heads, int kv_heads, int head_dim,
+                       int64_t cache_rows, int64_t cache_head_stride, int64_t cache_row_stride,
+                       int64_t max_position, float scale, int precision, void* workspace, size_t workspace_bytes,
+                       int dtype, void* stream, bool status_zeroed) {
   if (dtype != KVR_DTYPE_BF16 && dtype != KVR_DTYPE_F16) return KVR_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return KVR_ERR_UNSUPPORTED;
   if (precision != KVR_ATTN_P_SPLIT && precision != KVR_ATTN_P_ROUNDED) return KVR_ERR_INVALID_ARG;
@@ -771,13 +791,17 @@ int kvr_selected_attention(const void* q, const void* k_cache, const void* v_cac
   const bool split = precision == KVR_ATTN_P_SPLIT;
   if (bf16) {
     if (head_dim == 128)
-      return split ? attn::launch<BF16, 128, true>(mk, mv, mq, a, s) : attn::launch<BF16, 128, false>(mk, mv, mq, a, s);
-    return split ? attn::launch<BF16, 64, true>(mk, mv, mq, a, s) : attn::launch<BF16, 64, false>(mk, mv, mq, a, s);
+      return split ? attn::launch<BF16, 128, true>(mk, mv, mq, a, s, status_zeroed) : attn::launch<BF16, 128, false>(mk, mv, mq, a, s, status_zeroed);
+    return split ? attn::launch<BF16, 64, true>(mk, mv, mq, a, s, status_zeroed) : attn::launch<BF16, 64, false>(mk, mv, mq, a, s, status_zeroed);
   }
   if (head_dim == 128)
-    return split ? attn::launch<F16, 128, true>(mk, mv, mq, a, s) : attn::launch<F16, 128, false>(mk, mv, mq, a, s);
-  return split ? attn::launch<F16, 64, true>(mk, mv, mq, a, s) : attn::launch<F16, 64, false>(mk, mv, mq, a, s);
+    return split ? attn::launch<F16, 128, true>(mk, mv, mq, a, s, status_zeroed) : attn::launch<F16, 128, false>(mk, mv, mq, a, s, status_zeroed);
+  return split ? attn::launch<F16, 64, true>(mk, mv, mq, a, s, status_zeroed) : attn::launch<F16, 64, false>(mk, mv, mq, a, s, status_zeroed);
 }
+
+}  // namespace kvr
+
+extern "C" {
 
 // ---------------------------------------------------------------------------
 // No-allocation variant. Some callers cannot allocate device memory per call:

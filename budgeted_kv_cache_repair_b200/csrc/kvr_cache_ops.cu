@@ -31,6 +31,8 @@ struct CopyArgs {
 };
 
 __global__ void __launch_bounds__(256) copy_layers_kernel(LayerPtrs ptrs, CopyArgs a) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
   const int seg = blockIdx.y;                    // tensor * heads + head
   const int t = seg / a.heads;
   const int h = seg - t * a.heads;
@@ -98,6 +100,8 @@ __device__ __forceinline__ void rope_pair(const uint16_t* src_row, uint16_t* dst
 template <class T, int D>
 __global__ void __launch_bounds__(256) rope_shift_kernel(LayerPtrs ptrs, RopeArgs a,
                                                          const uint16_t* __restrict__ cos_sin) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
   __shared__ float cs[2 * D];
   for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) cs[i] = T::to_f(cos_sin[i]);
   __syncthreads();
@@ -152,6 +156,8 @@ __device__ __forceinline__ void rope_pair_regs(const Vec8& lo, const Vec8& hi, V
 template <class T, int D>
 __global__ void __launch_bounds__(256) shift_cache_kernel(ShiftPtrs ptrs, ShiftArgs a,
                                                           const uint16_t* __restrict__ cos_sin) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
   __shared__ float cs[2 * D];
   // The table is only passed (non-null) when the tail is rotated.
   if (a.apply_rope)
@@ -225,6 +231,8 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(
     const uint16_t* __restrict__ kf, const uint16_t* __restrict__ vf, uint16_t* kc, uint16_t* vc,
     const int64_t* __restrict__ positions, int64_t rows, int heads, int vpr, int64_t cache_rows,
     int64_t f_hs, int64_t f_rs, int64_t c_hs, int64_t c_rs, int* error_count) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
   const int64_t n = static_cast<int64_t>(heads) * rows * vpr;
   const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += step) {
@@ -251,6 +259,8 @@ __global__ void __launch_bounds__(256) embed_rows_kernel(
     const uint16_t* __restrict__ embed, int64_t vocab, int vpr, const int64_t* __restrict__ ids,
     int64_t id_count, const int64_t* __restrict__ positions, int64_t rows, uint16_t* out,
     int* error_count) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
   const int64_t r = blockIdx.x;
   if (r >= rows) return;
   const int64_t p = positions[r];
@@ -340,8 +350,7 @@ int kvr_copy_layers(const void* const* src, void* const* dst, int num_tensors, i
   a.dense = src_row_stride == head_dim && dst_row_stride == head_dim;
   const int segs = num_tensors * heads;
   dim3 grid(blocks_per_segment(rows * a.vecs_per_row / 4, segs, 256), segs);
-  copy_layers_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p, a);
-  return check_launch();
+  return launch_pdl<copy_layers_kernel>(grid, dim3(256), 0, static_cast<cudaStream_t>(stream), 1, p, a);
 }
 
 int kvr_rope_shift_layers(const void* const* src, void* const* dst, int num_layers, int heads,
@@ -369,14 +378,15 @@ int kvr_rope_shift_layers(const void* const* src, void* const* dst, int num_laye
   dim3 grid(blocks_per_segment(pairs / 2, segs, 256), segs);
   auto s = static_cast<cudaStream_t>(stream);
   const uint16_t* cs = static_cast<const uint16_t*>(cos_sin);
+  int st = KVR_OK;
   if (dtype == KVR_DTYPE_BF16) {
-    if (head_dim == 128) rope_shift_kernel<BF16, 128><<<grid, 256, 0, s>>>(p, a, cs);
-    else rope_shift_kernel<BF16, 64><<<grid, 256, 0, s>>>(p, a, cs);
+    if (head_dim == 128) st = launch_pdl<rope_shift_kernel<BF16, 128>>(grid, dim3(256), 0, s, 1, p, a, cs);
+    else st = launch_pdl<rope_shift_kernel<BF16, 64>>(grid, dim3(256), 0, s, 1, p, a, cs);
   } else {
-    if (head_dim == 128) rope_shift_kernel<F16, 128><<<grid, 256, 0, s>>>(p, a, cs);
-    else rope_shift_kernel<F16, 64><<<grid, 256, 0, s>>>(p, a, cs);
+    if (head_dim == 128) st = launch_pdl<rope_shift_kernel<F16, 128>>(grid, dim3(256), 0, s, 1, p, a, cs);
+    else st = launch_pdl<rope_shift_kernel<F16, 64>>(grid, dim3(256), 0, s, 1, p, a, cs);
   }
-  return check_launch();
+  return st;
 }
 
 int kvr_shift_cache_layers(const void* const* k_old, const void* const* v_old, void* const* k_new,
@@ -412,14 +422,15 @@ int kvr_shift_cache_layers(const void* const* k_old, const void* const* v_old, v
   dim3 grid(blocks_per_segment(pairs / 4, segs, 256), segs);
   auto s = static_cast<cudaStream_t>(stream);
   const uint16_t* cs = static_cast<const uint16_t*>(cos_sin);
+  int st = KVR_OK;
   if (dtype == KVR_DTYPE_BF16) {
-    if (head_dim == 128) shift_cache_kernel<BF16, 128><<<grid, 256, 0, s>>>(p, a, cs);
-    else shift_cache_kernel<BF16, 64><<<grid, 256, 0, s>>>(p, a, cs);
+    if (head_dim == 128) st = launch_pdl<shift_cache_kernel<BF16, 128>>(grid, dim3(256), 0, s, 1, p, a, cs);
+    else st = launch_pdl<shift_cache_kernel<BF16, 64>>(grid, dim3(256), 0, s, 1, p, a, cs);
   } else {
-    if (head_dim == 128) shift_cache_kernel<F16, 128><<<grid, 256, 0, s>>>(p, a, cs);
-    else shift_cache_kernel<F16, 64><<<grid, 256, 0, s>>>(p, a, cs);
+    if (head_dim == 128) st = launch_pdl<shift_cache_kernel<F16, 128>>(grid, dim3(256), 0, s, 1, p, a, cs);
+    else st = launch_pdl<shift_cache_kernel<F16, 64>>(grid, dim3(256), 0, s, 1, p, a, cs);
   }
-  return check_launch();
+  return st;
 }
 
 int kvr_scatter_rows(const void* k_fresh, const void* v_fresh, void* k_cache, void* v_cache,
@@ -437,12 +448,11 @@ int kvr_scatter_rows(const void* k_fresh, const void* v_fresh, void* k_cache, vo
     return KVR_ERR_INVALID_ARG;
   const int vpr = head_dim / 8;
   const int64_t n = static_cast<int64_t>(heads) * rows * vpr;
-  scatter_rows_kernel<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  return launch_pdl<scatter_rows_kernel>(grid_for(n, 256), dim3(256), 0, static_cast<cudaStream_t>(stream), 1, 
       static_cast<const uint16_t*>(k_fresh), static_cast<const uint16_t*>(v_fresh),
       static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), positions, rows, heads,
       vpr, cache_rows, fresh_head_stride, fresh_row_stride, cache_head_stride, cache_row_stride,
       error_count);
-  return check_launch();
 }
 
 int kvr_embed_rows(const void* embed, int64_t vocab, int hidden, const int64_t* ids,
@@ -455,10 +465,9 @@ int kvr_embed_rows(const void* embed, int64_t vocab, int hidden, const int64_t* 
   if (!embed || !ids || !positions || !out || !aligned16(embed) || !aligned16(out))
     return KVR_ERR_INVALID_ARG;
   if (rows > 0x7fffffff) return KVR_ERR_UNSUPPORTED;
-  embed_rows_kernel<<<static_cast<unsigned>(rows), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+  return launch_pdl<embed_rows_kernel>(static_cast<unsigned>(rows), dim3(128), 0, static_cast<cudaStream_t>(stream), 1, 
       static_cast<const uint16_t*>(embed), vocab, hidden / 8, ids, id_count, positions, rows,
       static_cast<uint16_t*>(out), error_count);
-  return check_launch();
 }
 
 }  // extern "C"

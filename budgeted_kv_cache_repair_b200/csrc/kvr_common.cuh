@@ -18,7 +18,15 @@ void set_last_cuda_error(cudaError_t e);
 // Adds to the process-wide launch counter behind kvr_kernel_launches().
 void count_launch();
 
-// Call right after each <<<>>> launch.
+// kvr_selected_attention; with status_zeroed the caller has zeroed the status
+// word at the start of `workspace` and no memset is issued.
+int selected_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                       const int64_t* positions, int64_t rows, int q_heads, int kv_heads, int head_dim,
+                       int64_t cache_rows, int64_t cache_head_stride, int64_t cache_row_stride,
+                       int64_t max_position, float scale, int precision, void* workspace, size_t workspace_bytes,
+                       int dtype, void* stream, bool status_zeroed);
+
+// Call right after each kernel launch.
 inline int check_launch() {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -30,6 +38,73 @@ inline int check_launch() {
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch. Every kernel of the library is launched with
+// programmatic stream serialization allowed, so it may start while the
+// kernel before it in the stream is still running. Its threads call
+// pdl_wait() before touching any memory that an earlier kernel writes or
+// reads (then all earlier kernels have completed and their writes are
+// visible), and pdl_launch_dependents() first thing, so that the kernel after
+// it may start its own independent prologue early (the projection kernel uses
+// that time to load its first weight tiles; everything it does before its own
+// pdl_wait() reads only weights). Without the launch attribute both are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+// Per-device once: prefer the largest shared-memory split of L1 for `kernel`,
+// so that the SM keeps one configuration across the library's kernels (the
+// projection and attention kernels need it) instead of switching between
+// consecutive launches.
+template <auto kernel>
+inline void prefer_shared_once() {
+  static int done[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return;
+  }
+  if (__atomic_load_n(&done[dev], __ATOMIC_ACQUIRE)) return;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+    cudaGetLastError();  // a preference only
+  __atomic_store_n(&done[dev], 1, __ATOMIC_RELEASE);
+}
+
+// Launch `kernel` on `stream` with programmatic dependent launch allowed
+// (optionally in clusters of `cluster` CTAs along x); counts the launch.
+template <auto kernel, class... Args>
+inline int launch_pdl(dim3 grid, dim3 block, size_t smem, cudaStream_t stream, int cluster, Args... args) {
+  prefer_shared_once<kernel>();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    n = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    cudaGetLastError();
+    return KVR_ERR_CUDA;
+  }
+  return check_launch();
+}
 
 // ---------------------------------------------------------------------------
 // Element types. Storage is 16-bit; arithmetic is fp32 with one rounding per
@@ -68,6 +143,26 @@ struct F16 {
 template <class T>
 __device__ __forceinline__ float rnd(float f) {
   return T::to_f(T::from_f(f));
+}
+
+// SiLU(gate) * up with the transformers MLP's roundings (act_fn(gate_proj(x)) *
+// up_proj(x) on 16-bit tensors): SiLU of the rounded gate in fp32, rounded,
+// then the product rounded. `gate` and `up` are already element-type values.
+template <class T>
+__device__ __forceinline__ uint16_t silu_mul_elem(float gate, float up) {
+  const float act = rnd<T>(gate / (1.0f + expf(-gate)));
+  return T::from_f(__fmul_rn(act, up));
+}
+
+// The same with the quotient of SiLU from the fast division (within 2 fp32
+// ulps of gate / (1 + exp(-gate)); the rounded 16-bit result differs from the
+// exact one only when the fp32 quotient lies within 2 ulps of a rounding
+// boundary, about 2^-14 of inputs). IEEE division carries a slow-path call
+// that made the projection epilogue several times slower.
+template <class T>
+__device__ __forceinline__ uint16_t silu_mul_elem_fast(float gate, float up) {
+  const float act = rnd<T>(__fdividef(gate, 1.0f + expf(-gate)));
+  return T::from_f(__fmul_rn(act, up));
 }
 
 // 8 x 16-bit elements = one 128-bit access.

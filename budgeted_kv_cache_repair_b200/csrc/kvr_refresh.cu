@@ -1,11 +1,16 @@
 // Native layer loop of the packed refresh: one C-ABI call runs the selected
 // rows through every decoder layer on the caller's stream.
 //
-// Per layer: residual add + input RMSNorm, q/k/v projection (cuBLAS, one GEMM
-// over fused weights when given), fused q/k-norm + RoPE + K/V scatter into the
-// cache, selected-query attention, o projection, residual add + post-attention
-// RMSNorm, gate/up projections, SiLU(gate)*up, down projection. The last layer
-// stops after its K/V scatter: nothing after it reaches the cache.
+// Per layer: residual add + input RMSNorm, q/k/v projection, fused q/k-norm +
+// RoPE + K/V scatter into the cache, selected-query attention, o projection,
+// residual add + post-attention RMSNorm, gate/up projections with
+// SiLU(gate)*up, down projection. The last layer stops after its K/V scatter
+// (and projects no queries): nothing after it reaches the cache.
+//
+// Projections run on cuBLAS, or (request.projections) up to kMaxRows rows on
+// the sm_100a weight-streaming kernel (kvr_linear.cu: q/k/v in one launch,
+// gate/up fused with the SiLU product); more rows always run on cuBLAS, where
+// the GEMMs are no longer weight-bound.
 //
 // Host work per layer is a handful of launches from C++, so the GPU, not the
 // Python interpreter, sets the pace at a few dozen rows.
@@ -23,6 +28,7 @@
 #include <unordered_map>
 
 #include "kvr_common.cuh"
+#include "kvr_linear.h"
 
 namespace kvr {
 namespace {
@@ -32,14 +38,39 @@ constexpr size_t kAlign = 256;
 inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct Buffers {
-  size_t hidden, normed, delta, qkv, q_rot, attn, gate, up, act, attn_ws, total;
+  bool lin;  // room for the sm_100a projection kernel (rows <= kMaxRows)
+  size_t hidden, normed, delta, qkv, q_rot, attn, gate, up, act, lin_ws, lin_bytes, lin_zero, attn_ws, total;
 };
+
+// Workspace of the projection launches of one layer: the largest of the four
+// (q/k/v, o, gate/up, down); every launch leaves its counters zero, so one
+// memset of the largest counter region serves the whole call.
+void linear_plan(const kvr_model* m, int64_t rows, size_t* bytes, size_t* zero) {
+  const int64_t qd = static_cast<int64_t>(m->q_heads) * m->head_dim;
+  const int64_t kd = static_cast<int64_t>(m->kv_heads) * m->head_dim;
+  const int64_t H = m->hidden, I = m->intermediate;
+  const int64_t n_qkv[3] = {qd, kd, kd};
+  const bool plain[3] = {false, false, false};
+  const bool gated[1] = {true};
+  size_t b = linear_workspace_bytes(rows, H, n_qkv, plain, 3);
+  const size_t b_o = linear_workspace_bytes(rows, qd, &H, plain, 1);
+  const size_t b_mlp = linear_workspace_bytes(rows, H, &I, gated, 1);
+  const size_t b_down = linear_workspace_bytes(rows, I, &H, plain, 1);
+  b = b > b_o ? b : b_o;
+  b = b > b_mlp ? b : b_mlp;
+  *bytes = b > b_down ? b : b_down;
+  int64_t tiles = (qd + 127) / 128 + 2 * ((kd + 127) / 128);
+  if ((H + 127) / 128 > tiles) tiles = (H + 127) / 128;
+  if ((I + 63) / 64 > tiles) tiles = (I + 63) / 64;
+  *zero = linear_zero_bytes(tiles);
+}
 
 Buffers layout(const kvr_model* m, int64_t rows, int64_t cache_rows) {
   const size_t e = 2;  // bf16 / fp16
   const size_t qd = static_cast<size_t>(m->q_heads) * m->head_dim;
   const size_t kd = static_cast<size_t>(m->kv_heads) * m->head_dim;
   Buffers b;
+  b.lin = rows <= kMaxRows;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t at = off;
@@ -55,6 +86,9 @@ Buffers layout(const kvr_model* m, int64_t rows, int64_t cache_rows) {
   b.gate = take(rows * static_cast<size_t>(m->intermediate) * e);
   b.up = take(rows * static_cast<size_t>(m->intermediate) * e);
   b.act = take(rows * static_cast<size_t>(m->intermediate) * e);
+  b.lin_bytes = b.lin_zero = 0;
+  if (b.lin) linear_plan(m, rows, &b.lin_bytes, &b.lin_zero);
+  b.lin_ws = take(b.lin_bytes);
   b.attn_ws = take(kvr_attention_workspace_size(rows, m->q_heads, m->kv_heads, m->head_dim, cache_rows));
   b.total = off;
   return b;
@@ -138,6 +172,7 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
       r.max_position >= r.cache_rows)
     return KVR_ERR_INVALID_ARG;
   if (r.rows > 0x7fffffffLL) return KVR_ERR_UNSUPPORTED;
+  if (r.projections != KVR_PROJ_CUBLAS && r.projections != KVR_PROJ_SM100) return KVR_ERR_INVALID_ARG;
   for (int l = 0; l < m.num_layers; ++l)
     if (!r.k_cache[l] || !r.v_cache[l]) return KVR_ERR_INVALID_ARG;
   const Buffers b = layout(&m, r.rows, r.cache_rows);
@@ -175,6 +210,24 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
     if (_st != KVR_OK) return _st; \
   } while (0)
 
+  void* lin_ws = ws + b.lin_ws;
+  const bool lin = b.lin && r.projections == KVR_PROJ_SM100;
+  // Projection on the sm_100a kernel: `count` segments sharing input x.
+  auto project = [&](const void* x, int64_t x_stride, int64_t k, const kvr_linear_segment* segs, int count) {
+    return linear_forward(x, x_stride, rows, k, segs, count, lin_ws, b.lin_bytes, m.dtype, true, s);
+  };
+  // Status words (attention, projections) and tile counters start at zero;
+  // each launch leaves its counters zero, so the layer loop needs no memset
+  // between kernels (a memset would break the programmatic launch chain).
+  {
+    cudaError_t e = cudaMemsetAsync(attn_ws, 0, sizeof(int), s);
+    if (e == cudaSuccess && lin) e = cudaMemsetAsync(lin_ws, 0, b.lin_zero, s);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return KVR_ERR_CUDA;
+    }
+  }
+
   KVR_TRY(kvr_embed_rows(m.embed, m.vocab, H, r.ids, r.id_count, r.positions, rows, hidden, nullptr, m.dtype,
                          stream));
   for (int l = 0; l < m.num_layers; ++l) {
@@ -182,7 +235,19 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
     const bool final = l == m.num_layers - 1;
     KVR_TRY(kvr_add_rmsnorm(hidden, l ? delta : nullptr, w.input_norm, normed, rows, H, H, H, H, m.eps, m.dtype,
                             stream));
-    if (w.qkv) {
+    if (lin) {
+      // q/k/v from separate weights or from row ranges of the stacked matrix.
+      const uint8_t* wq = static_cast<const uint8_t*>(w.qkv ? w.qkv : w.q);
+      const void* wk = w.qkv ? wq + qd * H * 2 : w.k;
+      const void* wv = w.qkv ? wq + (qd + kd) * H * 2 : w.v;
+      kvr_linear_segment segs[3] = {
+          {wq, nullptr, qd, qkv, qkv_w},
+          {wk, nullptr, kd, qkv + qd * 2, qkv_w},
+          {wv, nullptr, kd, qkv + (qd + kd) * 2, qkv_w},
+      };
+      // The last layer needs no queries.
+      KVR_TRY(final ? project(normed, H, H, segs + 1, 2) : project(normed, H, H, segs, 3));
+    } else if (w.qkv) {
       KVR_TRY(gemm(h, normed, H, w.qkv, qkv, qkv_w, rows, qkv_w, H, t));
     } else {
       if (!final) KVR_TRY(gemm(h, normed, H, w.q, qkv, qkv_w, rows, qd, H, t));
@@ -194,17 +259,28 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
                                  final ? nullptr : q_rot, r.k_cache[l], r.v_cache[l], r.cache_rows,
                                  r.cache_head_stride, r.cache_row_stride, nullptr, m.dtype, stream));
     if (final) break;
-    KVR_TRY(kvr_selected_attention(q_rot, r.k_cache[l], r.v_cache[l], attn, r.positions, rows, m.q_heads,
-                                   m.kv_heads, D, r.cache_rows, r.cache_head_stride, r.cache_row_stride,
-                                   r.max_position, scale, r.attention_precision, attn_ws, attn_ws_bytes, m.dtype,
-                                   stream));
-    KVR_TRY(gemm(h, attn, qd, w.o, delta, H, rows, H, qd, t));
+    KVR_TRY(selected_attention(q_rot, r.k_cache[l], r.v_cache[l], attn, r.positions, rows, m.q_heads, m.kv_heads,
+                               D, r.cache_rows, r.cache_head_stride, r.cache_row_stride, r.max_position, scale,
+                               r.attention_precision, attn_ws, attn_ws_bytes, m.dtype, stream, true));
+    if (lin) {
+      const kvr_linear_segment o_seg = {w.o, nullptr, H, delta, H};
+      KVR_TRY(project(attn, qd, qd, &o_seg, 1));
+    } else {
+      KVR_TRY(gemm(h, attn, qd, w.o, delta, H, rows, H, qd, t));
+    }
     if (r.tp_comm) KVR_TRY(allreduce(delta, rows * H, m.dtype, r.tp_comm, s));
     KVR_TRY(kvr_add_rmsnorm(hidden, delta, w.post_norm, normed, rows, H, H, H, H, m.eps, m.dtype, stream));
-    KVR_TRY(gemm(h, normed, H, w.gate, gate, I, rows, I, H, t));
-    KVR_TRY(gemm(h, normed, H, w.up, up, I, rows, I, H, t));
-    KVR_TRY(kvr_silu_mul(gate, up, act, rows, I, I, I, I, m.dtype, stream));
-    KVR_TRY(gemm(h, act, I, w.down, delta, H, rows, H, I, t));
+    if (lin) {
+      const kvr_linear_segment mlp = {w.gate, w.up, I, act, I};
+      const kvr_linear_segment down = {w.down, nullptr, H, delta, H};
+      KVR_TRY(project(normed, H, H, &mlp, 1));
+      KVR_TRY(project(act, I, I, &down, 1));
+    } else {
+      KVR_TRY(gemm(h, normed, H, w.gate, gate, I, rows, I, H, t));
+      KVR_TRY(gemm(h, normed, H, w.up, up, I, rows, I, H, t));
+      KVR_TRY(kvr_silu_mul(gate, up, act, rows, I, I, I, I, m.dtype, stream));
+      KVR_TRY(gemm(h, act, I, w.down, delta, H, rows, H, I, t));
+    }
     if (r.tp_comm) KVR_TRY(allreduce(delta, rows * H, m.dtype, r.tp_comm, s));
   }
 #undef KVR_TRY

@@ -14,6 +14,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
     uint16_t* hidden, const uint16_t* __restrict__ delta, const uint16_t* __restrict__ weight,
     uint16_t* out, int vpr, int64_t h_stride, int64_t d_stride, int64_t o_stride, float inv_h,
     float eps) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
   const int64_t r = blockIdx.x;
   uint16_t* hrow = hidden + r * h_stride;
   Vec8 x[kNormMaxVecs];
@@ -93,6 +95,8 @@ struct QkvArgs {
 
 template <class T, int D>
 __global__ void __launch_bounds__(256) qkv_rope_scatter_kernel(QkvArgs a) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
   constexpr int E = D / 32;  // 4 for D=128, 2 for D=64
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -164,6 +168,8 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const uint16_t* __restric
                                                        const uint16_t* __restrict__ up,
                                                        uint16_t* out, int64_t rows, int vpr,
                                                        int64_t g_rs, int64_t u_rs, int64_t o_rs) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
   const int64_t n = rows * vpr;
   const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += step) {
@@ -173,11 +179,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const uint16_t* __restric
     Vec8 u = ld_vec8(up + r * u_rs + v * 8);
     Vec8 o;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float x = T::to_f(g.h[e]);
-      const float act = rnd<T>(x / (1.0f + expf(-x)));
-      o.h[e] = T::from_f(__fmul_rn(act, T::to_f(u.h[e])));
-    }
+    for (int e = 0; e < 8; ++e) o.h[e] = silu_mul_elem<T>(T::to_f(g.h[e]), T::to_f(u.h[e]));
     st_vec8(out + r * o_rs + v * 8, o);
   }
 }
@@ -203,17 +205,18 @@ int kvr_add_rmsnorm(void* hidden, const void* delta, const void* weight, void* o
   auto s = static_cast<cudaStream_t>(stream);
   const int vpr = hidden_size / 8;
   const float inv_h = 1.0f / static_cast<float>(hidden_size);
+  int st = KVR_OK;
   if (dtype == KVR_DTYPE_BF16)
-    add_rmsnorm_kernel<BF16><<<static_cast<unsigned>(rows), kNormThreads, 0, s>>>(
+    st = launch_pdl<add_rmsnorm_kernel<BF16>>(static_cast<unsigned>(rows), dim3(kNormThreads), 0, s, 1, 
         static_cast<uint16_t*>(hidden), static_cast<const uint16_t*>(delta),
         static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), vpr, hidden_stride,
         delta_stride, out_stride, inv_h, eps);
   else
-    add_rmsnorm_kernel<F16><<<static_cast<unsigned>(rows), kNormThreads, 0, s>>>(
+    st = launch_pdl<add_rmsnorm_kernel<F16>>(static_cast<unsigned>(rows), dim3(kNormThreads), 0, s, 1, 
         static_cast<uint16_t*>(hidden), static_cast<const uint16_t*>(delta),
         static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), vpr, hidden_stride,
         delta_stride, out_stride, inv_h, eps);
-  return check_launch();
+  return st;
 }
 
 int kvr_qkv_rope_scatter(const void* q_in, const void* k_in, const void* v_in,
@@ -265,14 +268,15 @@ int kvr_qkv_rope_scatter(const void* q_in, const void* k_in, const void* v_in,
   const int64_t blocks = (warps + 7) / 8;
   if (blocks > 0x7fffffff) return KVR_ERR_UNSUPPORTED;
   auto s = static_cast<cudaStream_t>(stream);
+  int st = KVR_OK;
   if (dtype == KVR_DTYPE_BF16) {
-    if (head_dim == 128) qkv_rope_scatter_kernel<BF16, 128><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
-    else qkv_rope_scatter_kernel<BF16, 64><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+    if (head_dim == 128) st = launch_pdl<qkv_rope_scatter_kernel<BF16, 128>>(static_cast<unsigned>(blocks), dim3(256), 0, s, 1, a);
+    else st = launch_pdl<qkv_rope_scatter_kernel<BF16, 64>>(static_cast<unsigned>(blocks), dim3(256), 0, s, 1, a);
   } else {
-    if (head_dim == 128) qkv_rope_scatter_kernel<F16, 128><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
-    else qkv_rope_scatter_kernel<F16, 64><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+    if (head_dim == 128) st = launch_pdl<qkv_rope_scatter_kernel<F16, 128>>(static_cast<unsigned>(blocks), dim3(256), 0, s, 1, a);
+    else st = launch_pdl<qkv_rope_scatter_kernel<F16, 64>>(static_cast<unsigned>(blocks), dim3(256), 0, s, 1, a);
   }
-  return check_launch();
+  return st;
 }
 
 int kvr_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int64_t width,
@@ -288,17 +292,18 @@ int kvr_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int6
   const int vpr = static_cast<int>(width / 8);
   auto s = static_cast<cudaStream_t>(stream);
   const int grid = grid_for(rows * vpr, 256);
+  int st = KVR_OK;
   if (dtype == KVR_DTYPE_BF16)
-    silu_mul_kernel<BF16><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(gate),
+    st = launch_pdl<silu_mul_kernel<BF16>>(grid, dim3(256), 0, s, 1, static_cast<const uint16_t*>(gate),
                                                 static_cast<const uint16_t*>(up),
                                                 static_cast<uint16_t*>(out), rows, vpr, gate_stride,
                                                 up_stride, out_stride);
   else
-    silu_mul_kernel<F16><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(gate),
+    st = launch_pdl<silu_mul_kernel<F16>>(grid, dim3(256), 0, s, 1, static_cast<const uint16_t*>(gate),
                                                static_cast<const uint16_t*>(up),
                                                static_cast<uint16_t*>(out), rows, vpr, gate_stride,
                                                up_stride, out_stride);
-  return check_launch();
+  return st;
 }
 
 }  // extern "C"

@@ -1,6 +1,8 @@
-// Thin inline-PTX wrappers for the sm_100a features the attention kernel uses:
+// Thin inline-PTX wrappers for the sm_100a features the attention and
+// projection kernels use:
 // mbarriers with bounded waits, TMA tile loads (no multicast), tcgen05 MMA
-// with TMEM accumulators, and shared-memory matrix descriptors.
+// with TMEM accumulators, shared-memory matrix descriptors, and cluster
+// barriers with bulk copies into a peer CTA's shared memory.
 //
 // Descriptor and instruction-descriptor bit layouts follow the PTX ISA
 // tcgen05 "shared memory descriptor" and "instruction descriptor" tables
@@ -69,9 +71,65 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
       : "memory");
 }
+// 2-D tile load (same rules: no multicast).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
+
+// Barrier over the first `count` threads of the CTA (whole warps), id 1..15.
+__device__ __forceinline__ void bar_sync_named(int id, int count) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
+// Same barrier, returning whether `pred` holds on every participating thread.
+__device__ __forceinline__ bool bar_and_named(int id, int count, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(out)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
+}
+
+// ------------------------------------------------------------ thread-block clusters
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA in the cluster: arrive (release) then wait
+// (acquire). Orders this CTA's shared-memory writes before peers' reads.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// Address of the same shared-memory byte in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_peer(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+// Bulk copy of `bytes` (multiple of 16, 16-byte aligned ends) from this CTA's
+// shared memory to a cluster peer's (`dst`, `bar` from map_peer), completing
+// `bytes` on the peer's mbarrier. Then commit, and wait until the copies of
+// this thread no longer read their source.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+      "r"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
 
 // Generic-proxy shared-memory writes -> visible to the async proxy (MMA/TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -112,6 +112,9 @@ _views: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
 # Probabilities enter P.V as P_hi + P_lo (close to fp32 P, as the reference's
 # own indexed kernel keeps them); ATTN_P_ROUNDED rounds P once like fused SDPA.
 ATTENTION_PRECISION = _lib.ATTN_P_SPLIT
+# Projection GEMMs of the layer loop: cuBLAS, or the sm_100a weight-streaming
+# kernel (kvr_linear) for requests of up to 256 rows.
+PROJECTIONS = _lib.PROJ_CUBLAS
 
 
 class KernelTimer:
@@ -188,6 +191,39 @@ def _native_model(view: ModelView):
     return view._native
 
 
+def linear(x: torch.Tensor, weights, outs=None) -> list[torch.Tensor]:
+    """``x @ W.T`` for each entry of ``weights`` in ONE ``kvr_linear`` launch.
+
+    ``x``: ``[rows, k]`` (unit column stride); ``weights``: up to four entries,
+    each an ``[n, k]`` nn.Linear weight or a ``(gate, up)`` pair, which yields
+    ``silu(x @ gate.T) * (x @ up.T)`` with the MLP's roundings. Returns one
+    ``[rows, n]`` tensor per entry (or writes ``outs``).
+    """
+    lib = _lib.load()
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be [rows, k] with a unit column stride")
+    rows, k = x.shape
+    segs = (_lib.LinearSegment * len(weights))()
+    result = []
+    for i, w in enumerate(weights):
+        gate, up = (w if isinstance(w, (tuple, list)) else (w, None))
+        out = outs[i] if outs is not None else torch.empty(rows, gate.shape[0], dtype=x.dtype, device=x.device)
+        for t in (gate, up):
+            if t is not None and (t.shape[1] != k or not t.is_contiguous() or t.dtype != x.dtype):
+                raise ValueError("weights must be contiguous [n, k] tensors of the input dtype")
+        if out.stride(1) != 1:
+            raise ValueError("outputs need a unit column stride")
+        segs[i] = _lib.LinearSegment(weight=gate.data_ptr(), weight_up=up.data_ptr() if up is not None else None,
+                                     n=gate.shape[0], out=out.data_ptr(), out_stride=out.stride(0))
+        result.append(out)
+    need = lib.kvr_linear_workspace_size(rows, k, segs, len(weights))
+    workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=x.device)
+    _lib.check(lib.kvr_linear(x.data_ptr(), x.stride(0), rows, k, segs, len(weights), workspace.data_ptr(), need,
+                              _lib.dtype_code(x.dtype), _lib.stream_handle(x.device)), "linear")
+    linear.last_workspace = workspace
+    return result
+
+
 def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Tensor,
                  max_position: int, cache_rows: int, tp_comm=None) -> None:
     """Recompute the selected rows through every layer, writing K/V in place.
@@ -212,7 +248,7 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
         k_cache=k_ptrs, v_cache=v_ptrs, cache_rows=cache_rows, cache_head_stride=head_stride,
         cache_row_stride=row_stride, ids=ids.data_ptr(), id_count=ids.numel(), positions=positions.data_ptr(),
         rows=rows, max_position=max_position, cos_tab=cos.data_ptr(), sin_tab=sin.data_ptr(),
-        attention_precision=ATTENTION_PRECISION, tp_comm=tp_comm)
+        attention_precision=ATTENTION_PRECISION, tp_comm=tp_comm, projections=PROJECTIONS)
     need = lib.kvr_packed_refresh_workspace_size(model, rows, cache_rows)
     if not need:
         raise ValueError("model geometry is outside the built kernels")

@@ -5,7 +5,7 @@ Mirrors ``IndexedPlan`` / ``DeviceIndexedPlan`` of the reference
 metadata (BLOCK_M=16 query rows, BLOCK_N=64 keys: ``full_prefix_tiles`` key
 tiles visible to every row of a query tile, ``total_tiles`` tiles reaching its
 last row), validation messages and sealing against mutation. The sm_100a
-attention kernel tiles differently (64 packed (row, head) entries per CTA) and
+attention kernel tiles differently (128 packed (row, head) entries per CTA) and
 derives its own bounds on the device from ``positions``; the tile fields stay
 for callers that read them.
 """

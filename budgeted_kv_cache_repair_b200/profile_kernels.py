@@ -3,10 +3,15 @@
     python -m budgeted_kv_cache_repair_b200.profile_kernels shift     [--reps N]
     python -m budgeted_kv_cache_repair_b200.profile_kernels attention [--reps N] [--precision rounded|split]
     python -m budgeted_kv_cache_repair_b200.profile_kernels copy      [--reps N]
+    python -m budgeted_kv_cache_repair_b200.profile_kernels linear    [--reps N] [--only NAME]
 
 Geometry: Llama-3-8B shape (32 layers, 8 KV heads, head_dim 128, bf16),
 8192-token context with 256 tokens deleted at 1024 (7936 rows), 64 selected
-rows in 16 intervals of 4. Inputs are seeded random tensors. After two
+rows in 16 intervals of 4 (`linear`: the per-layer projections of that model
+at 64 rows, each timed beside torch's cuBLAS GEMMs for the same products, with
+enough weight copies in rotation that no launch finds its weights in L2, and
+replayed from a CUDA graph so that host launch cost is not measured).
+Inputs are seeded random tensors. After two
 warm-up launches the command times `--reps` launches with CUDA events and
 prints the average; under ncu, capture with `-s 2`.
 """
@@ -92,9 +97,81 @@ def attention(reps: int, precision: str) -> None:
           f"{flops / us / 1e6:.1f} TFLOP/s; status {int(ws[:4].view(torch.int32).item())}")
 
 
+HIDDEN, INTER, ROWS = 4096, 14336, 64
+
+
+def _graph_time(fn, calls: int) -> float:
+    """Average device time of `calls` back-to-back calls replayed from one
+    CUDA graph (no host launch overhead in the measurement)."""
+    for i in range(2):
+        fn(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(calls):
+            fn(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    begin.record()
+    graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    return begin.elapsed_time(end) / calls * 1e3
+
+
+def linear(reps: int, only: str | None) -> None:
+    lib = _lib.load()
+    x = (torch.randn(ROWS, INTER, device="cuda") * 0.5).bfloat16()
+    shapes = {  # name -> (k, [(n, paired)])
+        "qkv": (HIDDEN, [(HEADS * D, False), (KV_HEADS * D, False), (KV_HEADS * D, False)]),
+        "o": (HIDDEN, [(HIDDEN, False)]),
+        "gate_up": (HIDDEN, [(INTER, True)]),
+        "down": (INTER, [(HIDDEN, False)]),
+    }
+    for name, (k, spec) in shapes.items():
+        if only and name != only:
+            continue
+        per_set = sum(n * k * 2 * (2 if paired else 1) for n, paired in spec)
+        sets = max(1, -(-400_000_000 // per_set))  # > 3x L2 in rotation
+        weights = [[(torch.randn(n, k, device="cuda").bfloat16(), torch.randn(n, k, device="cuda").bfloat16())
+                    if paired else torch.randn(n, k, device="cuda").bfloat16() for n, paired in spec]
+                   for _ in range(sets)]
+        xi = x[:, :k]
+        outs = [torch.empty(ROWS, n, device="cuda", dtype=torch.bfloat16) for n, _ in spec]
+        segs = []
+        for ws_set in weights:
+            arr = (_lib.LinearSegment * len(spec))()
+            for i, (w, out) in enumerate(zip(ws_set, outs)):
+                gate, up = w if isinstance(w, tuple) else (w, None)
+                arr[i] = _lib.LinearSegment(weight=gate.data_ptr(), weight_up=up.data_ptr() if up is not None else None,
+                                            n=gate.shape[0], out=out.data_ptr(), out_stride=out.stride(0))
+            segs.append(arr)
+        need = lib.kvr_linear_workspace_size(ROWS, k, segs[0], len(spec))
+        workspace = torch.empty(need, dtype=torch.uint8, device="cuda")
+
+        def ours(i):
+            _lib.check(lib.kvr_linear(xi.data_ptr(), xi.stride(0), ROWS, k, segs[i % sets], len(spec),
+                                      workspace.data_ptr(), need, _lib.DTYPE_BF16, _lib.stream_handle()), "linear")
+
+        def cublas(i):
+            for w, out in zip(weights[i % sets], outs):
+                if isinstance(w, tuple):
+                    torch.mul(torch.nn.functional.silu(xi @ w[0].T), xi @ w[1].T, out=out)
+                else:
+                    torch.matmul(xi, w.T, out=out)
+
+        us = _graph_time(ours, reps * sets)
+        ref = _graph_time(cublas, reps * sets)
+        print(f"kvr_linear {name}: {us:.1f} us/launch, {per_set / us / 1e3:.0f} GB/s of weights; "
+              f"cuBLAS path {ref:.1f} us ({per_set / ref / 1e3:.0f} GB/s); "
+              f"status {int(workspace[:4].view(torch.int32).item())}")
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("kernel", choices=["shift", "attention", "copy"])
+    parser.add_argument("kernel", choices=["shift", "attention", "copy", "linear"])
+    parser.add_argument("--only", default=None, help="linear: one of qkv, o, gate_up, down")
     parser.add_argument("--reps", type=int, default=10)
     parser.add_argument("--precision", choices=["rounded", "split"], default="rounded")
     args = parser.parse_args()
@@ -103,6 +180,8 @@ def main() -> None:
         shift(args.reps)
     elif args.kernel == "copy":
         copy(args.reps)
+    elif args.kernel == "linear":
+        linear(args.reps, args.only)
     else:
         attention(args.reps, args.precision)
 

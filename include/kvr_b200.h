@@ -163,6 +163,38 @@ KVR_API int kvr_silu_mul(const void* gate, const void* up, void* out, int64_t ro
                  int dtype, void* stream);
 
 /*
+ * Projections of the selected rows on sm_100a tensor cores, for the few
+ * dozen rows of a refresh: out = x . weight^T (nn.Linear, fp32 accumulation,
+ * one rounding), for up to KVR_LINEAR_MAX_SEGMENTS weight matrices that share
+ * the input x in ONE launch (q/k/v as three segments). A segment with
+ * weight_up set is the gated MLP: out = round(round(silu(round(x . weight^T)))
+ * * round(x . weight_up^T)) (LlamaMLP's act_fn(gate_proj(x)) * up_proj(x)).
+ * Replaces the nn.Linear calls of the decoder modules that the reference's
+ * packed forward runs (q/k/v/o_proj, gate/up/down_proj under
+ * kernels/packed_cache.py:284-297); cuBLAS stays the path for many rows.
+ *
+ * x: [rows, k] with row stride x_stride (16-byte aligned base, stride and k
+ * multiples of 8). weight(_up): [n, k] contiguous, 16-byte aligned. out:
+ * [rows, n] with row stride out_stride. Summation order is fixed: results do
+ * not depend on the run. `workspace` (kvr_linear_workspace_size bytes, any
+ * contents) starts with a status word: 0, or the code of a bounded
+ * device-side wait that gave up. Calls that overlap on the GPU must not share
+ * a workspace.
+ */
+#define KVR_LINEAR_MAX_SEGMENTS 4
+typedef struct kvr_linear_segment {
+  const void* weight;      /* [n, k] */
+  const void* weight_up;   /* NULL, or [n, k]: gated-MLP segment */
+  int64_t n;
+  void* out;               /* [rows, out_stride] */
+  int64_t out_stride;
+} kvr_linear_segment;
+KVR_API size_t kvr_linear_workspace_size(int64_t rows, int64_t k, const kvr_linear_segment* segments, int count);
+KVR_API int kvr_linear(const void* x, int64_t x_stride, int64_t rows, int64_t k,
+                       const kvr_linear_segment* segments, int count, void* workspace,
+                       size_t workspace_bytes, int dtype, void* stream);
+
+/*
  * Selected-query absolute-causal attention with GQA on sm_100a tensor cores
  * (tcgen05 MMA with TMEM accumulators, TMA-fed K/V).
  * q [rows, q_heads, D] contiguous; K/V [kv_heads, cache_rows, D] with strides;
@@ -209,7 +241,8 @@ KVR_API int kvr_selected_attention(const void* q, const void* k_cache, const voi
  * cos_tab/sin_tab are the model's rotary cos/sin at the selected positions
  * ([rows, head_dim], model dtype). `workspace` holds
  * kvr_packed_refresh_workspace_size() bytes of activations and attention
- * scratch (any contents). Projections run on cuBLAS (fp32 accumulation).
+ * scratch (any contents). Projections run on cuBLAS or on the kvr_linear
+ * kernel (request.projections), with fp32 accumulation either way.
  */
 typedef struct kvr_layer_weights {
   const void* input_norm;  /* [hidden] */
@@ -250,7 +283,11 @@ typedef struct kvr_refresh_request {
   void* tp_comm;           /* NULL, or a communicator from kvr_tp_comm_init: the model is this
                               rank's head/column shard and the o/down partial sums are
                               all-reduced (sum) across the group after each projection */
+  int projections;         /* KVR_PROJ_*: which GEMMs run the q/k/v, o, gate/up and down
+                              projections (requests above 256 rows always use cuBLAS) */
 } kvr_refresh_request;
+#define KVR_PROJ_CUBLAS 0  /* cuBLAS GEMMs, fp32 accumulation */
+#define KVR_PROJ_SM100 1   /* kvr_linear's weight-streaming kernel, gate/up fused with SiLU */
 
 /*
  * Tensor-parallel group for kvr_packed_refresh (NCCL over NVLink). No

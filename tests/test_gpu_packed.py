@@ -21,8 +21,17 @@ def _check_rows(actual_rows, expected_rows, what, min_cos=0.999):
     assert (err <= bound).all(), (what, err.max().item())
 
 
+@pytest.fixture(params=["cublas", "sm100"])
+def projections(request, monkeypatch):
+    """Both projection paths of the layer loop: cuBLAS and the kvr_linear kernel."""
+    from budgeted_kv_cache_repair_b200 import _lib, engine
+
+    monkeypatch.setattr(engine, "PROJECTIONS", {"cublas": _lib.PROJ_CUBLAS, "sm100": _lib.PROJ_SM100}[request.param])
+    return request.param
+
+
 @pytest.mark.parametrize("name", CASES)
-def test_packed_matches_reference_outputs(name):
+def test_packed_matches_reference_outputs(name, projections):
     from budgeted_kv_cache_repair_b200 import OperatorShim, packed_interval_repair
 
     record = load_golden(name)

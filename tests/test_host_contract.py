@@ -51,6 +51,17 @@ def test_native_argument_checks_run_without_a_gpu(built):
     assert lib.kvr_silu_mul(None, None, None, 0, 16, 16, 16, 16, 7, None) == _lib.ERR_UNSUPPORTED
     # Empty work is a no-op success.
     assert lib.kvr_scatter_rows(None, None, None, None, None, 0, 1, 64, 9, 0, 0, 0, 0, None, 0, None) == _lib.OK
+    seg = _lib.LinearSegment(weight=256, weight_up=None, n=128, out=512, out_stride=128)
+    assert lib.kvr_linear(256, 64, 4, 60, ctypes.byref(seg), 1, 1024, 1 << 20, 0, None) == _lib.ERR_INVALID_ARG
+    assert lib.kvr_linear(256, 64, 4, 64, ctypes.byref(seg), 5, 1024, 1 << 20, 0, None) == _lib.ERR_INVALID_ARG
+    assert lib.kvr_linear(256, 64, 4, 64, ctypes.byref(seg), 1, 1024, 1 << 20, 9, None) == _lib.ERR_UNSUPPORTED
+    assert lib.kvr_linear(None, 64, 0, 64, ctypes.byref(seg), 1, None, 0, 0, None) == _lib.OK
+    # fewer tiles than SMs: split-K in clusters, status word only
+    assert lib.kvr_linear_workspace_size(64, 64, ctypes.byref(seg), 1) == 256
+    # 224 gated tiles: 148 whole tiles, 76 tiles x 64 k-chunks stream-K over 148 CTAs
+    # -> status + 76 counters (304 bytes -> 512) + 148 CTAs x 2 slots x 64 x 128 fp32
+    gated = _lib.LinearSegment(weight=256, weight_up=256, n=14336, out=512, out_stride=14336)
+    assert lib.kvr_linear_workspace_size(64, 4096, ctypes.byref(gated), 1) == 256 + 512 + 148 * 2 * 64 * 128 * 4
     assert lib.kvr_attention_workspace_size(64, 32, 8, 128, 7936) > 0
     assert lib.kvr_attention_workspace_size(20000, 32, 8, 128, 7936) == 256  # enough tiles: status word only
 
