@@ -8,16 +8,20 @@
 // repeat_kv). Rows are sorted by absolute position; a tile's causal span is
 // [0, pos(last row)].
 //
-// One CTA per SM, 6 warps:
-//   warp 4  TMA producer: K and V blocks of 128 keys, 128B-swizzled, into a
-//           ring of NS stages (bounded-wait mbarriers, no multicast)
-//   warp 5  MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S
-//           buffers, then O += P_j V_j into the TMEM O accumulator
-//   warps 0-3  softmax: thread t owns TMEM lane t = m-entry t. It loads its S
-//           row, applies the causal/chunk mask, keeps a running max, writes
-//           P = 2^(s - m) to shared memory as the A operand of the PV MMA, and
-//           rescales its O row in TMEM only when the max grew by more than
-//           2^8 (exact: the final normalisation uses the same stale max).
+// One CTA per SM, 10 warps:
+//   warp 8  TMA producer: K and V blocks of 128 keys, 128B-swizzled, into
+//           rings of NS stages with separate K and V barriers, so a K stage is
+//           refilled as soon as its Q.K^T is done (bounded waits, no multicast)
+//   warp 9  MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S
+//           buffers, then O += P_j V_j into the TMEM O accumulators
+//   warps 0-7  softmax: two threads per m-entry row (TMEM lane = row), each
+//           owning 64 keys of every block with its own running max, sum and
+//           TMEM O accumulator. A thread loads its S half-row, applies the
+//           causal/chunk mask, keeps a running max, writes P = 2^(s - m) to
+//           shared memory as the A operand of the PV MMA, and rescales its O
+//           half in TMEM only when the max grew by more than 2^8 (exact: the
+//           final normalisation uses the same stale max). The two halves merge
+//           once, in the epilogue.
 // QK^T of block j+1 overlaps the softmax of block j.
 //
 // Precision: QK^T and PV run on bf16/fp16 operands with fp32 accumulation.
@@ -73,26 +77,24 @@ struct Args {
 template <int D, bool SPLIT>
 struct Layout {
   static constexpr int DS = D / 64;  // 64-element (128 B) sub-tiles across head_dim
-  static constexpr int NS = (D == 128 || SPLIT) ? 2 : 3;  // K/V ring stages
+  // K/V ring stages. P lives in tensor memory (over its own S columns), so
+  // shared memory holds only Q and the rings.
+  static constexpr int NS = D == 128 ? 3 : 4;
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + DS * SUB;
   static constexpr int V_OFF = K_OFF + NS * DS * SUB;
-  // P buffers (A operand of P.V, [128 rows x 128 keys]): double-buffered so the
-  // softmax of block j overlaps the P.V MMA of block j-1, except for split P at
-  // head_dim 128, where two halves of two buffers do not fit next to K/V.
-  static constexpr int NP = (SPLIT && D == 128) ? 1 : 2;
-  static constexpr int P_BYTES = (SPLIT ? 4 : 2) * SUB;  // hi (+ lo) halves, 2 sub-tiles each
-  static constexpr int P_OFF = V_OFF + NS * DS * SUB;
-  static constexpr int BAR_OFF = P_OFF + NP * P_BYTES;
-  // q_full, kv_full[NS], kv_empty[NS], s_full[2], s_free[2], p_full[NP], pv_done[NP], drain, red_bar
-  static constexpr int NBAR = 1 + 2 * NS + 4 + 2 * NP + 1 + 1;
+  static constexpr int NP = 2;  // P buffers = the two S buffers
+  static constexpr int BAR_OFF = V_OFF + NS * DS * SUB;
+  // q_full, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS], s_full[2], s_free[2], p_full[NP],
+  // pv_done[NP], drain, red_bar
+  static constexpr int NBAR = 1 + 4 * NS + 4 + 2 * NP + 1 + 1;
   static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;
   static constexpr int RED_OFF = MISC_OFF + 16;  // float [2 halves][128 rows][max, sum]
   static constexpr int USED = RED_OFF + 2 * BM * 2 * 4;
   // Swizzled tiles need a 1 KB-aligned base; the allocation carries what slack
   // fits under the per-CTA limit and the kernel checks it at run time.
   static constexpr int BYTES = USED + 1024 <= 232448 ? USED + 1024 : 232448;
-  static constexpr uint32_t STAGE_TX = 2u * DS * SUB;
+  static constexpr uint32_t HALF_TX = DS * SUB;  // one K or one V block
   static_assert(USED <= 232448, "dynamic shared memory above the 227 KB per-CTA limit");
 };
 
@@ -133,6 +135,38 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Two fp32 values in one 64-bit register, for the packed fp32 ALU ops of
+// sm_100 (one instruction for two lanes of a row).
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // Byte offset of 16-byte chunk c (0..7) of row r in a 128B-swizzled sub-tile.
@@ -177,14 +211,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t bar0 = base + L::BAR_OFF;
   const uint32_t q_full = bar0;
-  auto kv_full = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto kv_empty = [&](int s) { return bar0 + 8u * (1 + NS + s); };
-  auto s_full = [&](int b) { return bar0 + 8u * (1 + 2 * NS + b); };
-  auto s_free = [&](int b) { return bar0 + 8u * (3 + 2 * NS + b); };
-  auto p_full = [&](int pb) { return bar0 + 8u * (5 + 2 * NS + pb); };
-  auto pv_done = [&](int pb) { return bar0 + 8u * (5 + 2 * NS + NP + pb); };
-  const uint32_t drain = bar0 + 8u * (5 + 2 * NS + 2 * NP);
-  const uint32_t red_bar = bar0 + 8u * (6 + 2 * NS + 2 * NP);
+  // K and V blocks have their own barriers: a K stage is refilled as soon as
+  // its Q.K^T MMA is done, a V stage once its P.V MMA is done.
+  auto k_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto k_empty = [&](int s) { return bar0 + 8u * (1 + NS + s); };
+  auto v_full = [&](int s) { return bar0 + 8u * (1 + 2 * NS + s); };
+  auto v_empty = [&](int s) { return bar0 + 8u * (1 + 3 * NS + s); };
+  auto s_full = [&](int b) { return bar0 + 8u * (1 + 4 * NS + b); };
+  auto s_free = [&](int b) { return bar0 + 8u * (3 + 4 * NS + b); };
+  auto p_full = [&](int pb) { return bar0 + 8u * (5 + 4 * NS + pb); };
+  auto pv_done = [&](int pb) { return bar0 + 8u * (5 + 4 * NS + NP + pb); };
+  const uint32_t drain = bar0 + 8u * (5 + 4 * NS + 2 * NP);
+  const uint32_t red_bar = bar0 + 8u * (6 + 4 * NS + 2 * NP);
   volatile int* abort = reinterpret_cast<volatile int*>(gbase + L::MISC_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L::MISC_OFF + 4);
   float* red = reinterpret_cast<float*>(gbase + L::RED_OFF);  // [2 halves][128 rows][max, sum]
@@ -194,12 +232,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     *abort = 0;
     sm100::mbar_init(q_full, a.q_by_tma ? 1 : kSoftmaxThreads);
     for (int s = 0; s < NS; ++s) {
-      sm100::mbar_init(kv_full(s), 1);
-      sm100::mbar_init(kv_empty(s), 1);
+      sm100::mbar_init(k_full(s), 1);
+      sm100::mbar_init(k_empty(s), 1);
+      sm100::mbar_init(v_full(s), 1);
+      sm100::mbar_init(v_empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       sm100::mbar_init(s_full(b), 1);
-      sm100::mbar_init(s_free(b), kSoftmaxThreads);
+      sm100::mbar_init(s_free(b), 1);  // committed after the P.V that reads P (in S's columns)
     }
     for (int pb = 0; pb < NP; ++pb) {
       sm100::mbar_init(p_full(pb), kSoftmaxThreads);
@@ -235,26 +275,33 @@ __global__ void __launch_bounds__(THREADS, 1)
           sm100::tma_load_3d(base + L::Q_OFF + ds * SUB, &tmap_q, q_full, ds * 64, h * G,
                              static_cast<int>(m0 / G));
       }
-      int issued = 0;
+      int issued_k = 0, issued_v = 0;
       for (int j = 0; j < nblk; ++j) {
         const int s = j % NS;
-        if (j >= NS && !sm100::mbar_wait(kv_empty(s), ((j / NS) - 1) & 1, abort, err, ERR_KV_EMPTY, WAIT_LIMIT))
-          break;
-        sm100::mbar_arrive_expect_tx(kv_full(s), L::STAGE_TX);
         const int key0 = static_cast<int>(k_begin + static_cast<int64_t>(j) * BN);
+        if (j >= NS && !sm100::mbar_wait(k_empty(s), ((j / NS) - 1) & 1, abort, err, ERR_KV_EMPTY, WAIT_LIMIT))
+          break;
+        sm100::mbar_arrive_expect_tx(k_full(s), L::HALF_TX);
 #pragma unroll
-        for (int ds = 0; ds < DS; ++ds) {
-          sm100::tma_load_3d(base + L::K_OFF + (s * DS + ds) * SUB, &tmap_k, kv_full(s), ds * 64, key0, h);
-          sm100::tma_load_3d(base + L::V_OFF + (s * DS + ds) * SUB, &tmap_v, kv_full(s), ds * 64, key0, h);
-        }
-        issued = j + 1;
+        for (int ds = 0; ds < DS; ++ds)
+          sm100::tma_load_3d(base + L::K_OFF + (s * DS + ds) * SUB, &tmap_k, k_full(s), ds * 64, key0, h);
+        issued_k = j + 1;
+        if (j >= NS && !sm100::mbar_wait(v_empty(s), ((j / NS) - 1) & 1, abort, err, ERR_KV_EMPTY, WAIT_LIMIT))
+          break;
+        sm100::mbar_arrive_expect_tx(v_full(s), L::HALF_TX);
+#pragma unroll
+        for (int ds = 0; ds < DS; ++ds)
+          sm100::tma_load_3d(base + L::V_OFF + (s * DS + ds) * SUB, &tmap_v, v_full(s), ds * 64, key0, h);
+        issued_v = j + 1;
       }
       // Never leave the CTA while one of our copies may still land in shared memory.
       if (*abort) {
         volatile int keep_waiting = 0;
         if (a.q_by_tma) sm100::mbar_wait(q_full, 0, &keep_waiting, nullptr, 0, WAIT_LIMIT);
-        for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
-          sm100::mbar_wait(kv_full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
+        for (int j = issued_k > NS ? issued_k - NS : 0; j < issued_k; ++j)
+          sm100::mbar_wait(k_full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
+        for (int j = issued_v > NS ? issued_v - NS : 0; j < issued_v; ++j)
+          sm100::mbar_wait(v_full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -265,7 +312,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = sm100::mbar_wait(q_full, 0, abort, err, ERR_Q_FULL, WAIT_LIMIT);
       auto issue_qk = [&](int j) -> bool {
         const int s = j % NS, b = j & 1;
-        if (!sm100::mbar_wait(kv_full(s), (j / NS) & 1, abort, err, ERR_KV_FULL, WAIT_LIMIT)) return false;
+        if (!sm100::mbar_wait(k_full(s), (j / NS) & 1, abort, err, ERR_KV_FULL, WAIT_LIMIT)) return false;
         if (j >= 2 && !sm100::mbar_wait(s_free(b), ((j >> 1) - 1) & 1, abort, err, ERR_S_FREE, WAIT_LIMIT))
           return false;
         sm100::tc_fence_after();
@@ -277,16 +324,20 @@ __global__ void __launch_bounds__(THREADS, 1)
           sm100::mma_f16_ss(tmem + b * BN, da, db, IQK, k > 0);
         }
         sm100::mma_commit(s_full(b));
+        sm100::mma_commit(k_empty(s));  // K block free once Q.K^T is done
         return true;
       };
       if (ok) ok = issue_qk(0);
       for (int j = 0; ok && j < nblk; ++j) {
         if (j + 1 < nblk && !issue_qk(j + 1)) break;
-        const int pb = j % NP;
-        if (!sm100::mbar_wait(p_full(pb), (j / NP) & 1, abort, err, ERR_P_FULL, WAIT_LIMIT)) break;
+        const int pb = j & 1;  // P of block j sits in S buffer j & 1
+        if (!sm100::mbar_wait(p_full(pb), (j >> 1) & 1, abort, err, ERR_P_FULL, WAIT_LIMIT)) break;
+        if (!sm100::mbar_wait(v_full(j % NS), (j / NS) & 1, abort, err, ERR_KV_FULL, WAIT_LIMIT)) break;
         sm100::tc_fence_after();
         const int s = j % NS;
-        const uint32_t pbase = base + L::P_OFF + pb * L::P_BYTES;
+        // P of key half `half`: 32 TMEM columns at pb*BN + half*64 (two 16-bit
+        // values per column), the low halves of split P in the next 32.
+        const uint32_t pcol = tmem + static_cast<uint32_t>(pb * BN);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
 #pragma unroll
@@ -294,17 +345,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             // V block: MN-major (head_dim contiguous); 16 keys = two 8-row groups.
             const uint64_t db =
                 sm100::desc_sw128(base + L::V_OFF + s * DS * SUB + (half * 4 + k) * 2048, SUB, 1024);
-            const uint64_t da = sm100::desc_sw128(pbase + half * SUB + k * 32, 16, 1024);
             const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
-            sm100::mma_f16_ss(tmem + TM_O + half * D, da, db, IPV, acc);
-            if constexpr (SPLIT) {
-              const uint64_t dl = sm100::desc_sw128(pbase + 2 * SUB + half * SUB + k * 32, 16, 1024);
-              sm100::mma_f16_ss(tmem + TM_O + half * D, dl, db, IPV, 1u);
-            }
+            sm100::mma_f16_ts(tmem + TM_O + half * D, pcol + half * 64 + k * 8, db, IPV, acc);
+            if constexpr (SPLIT) sm100::mma_f16_ts(tmem + TM_O + half * D, pcol + half * 64 + 32 + k * 8, db, IPV, 1u);
           }
         }
         sm100::mma_commit(pv_done(pb));
-        sm100::mma_commit(kv_empty(s));
+        sm100::mma_commit(v_empty(s));
+        sm100::mma_commit(s_free(pb));  // S/P buffer free for block j + 2
       }
       // Nothing of ours may still be writing TMEM when it is freed.
       sm100::mma_commit(drain);
@@ -350,36 +398,32 @@ __global__ void __launch_bounds__(THREADS, 1)
       sm100::tmem_ld32(tmem + lane_base + b * BN + scol, sv[0]);
       sm100::tmem_ld32(tmem + lane_base + b * BN + scol + 32, sv[1]);
       sm100::tmem_wait_ld();
-      sm100::tc_fence_before();
-      sm100::mbar_arrive(s_free(b));
 
       const int64_t key0 = k_begin + static_cast<int64_t>(j) * BN + half * 64;
       // Visible columns of this half-block for this row: [0, lim).
       const int64_t lim64 = (pos + 1 < k_end ? pos + 1 : k_end) - key0;
       const int lim = lim64 < 0 ? 0 : (lim64 > 64 ? 64 : static_cast<int>(lim64));
-      // Eight independent max chains (no 64-deep dependency).
-      float mx8[8];
+      // Masked columns become -inf (then P = 2^-inf = 0); four independent
+      // three-input max chains.
+      if (lim < 64) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
-      if (lim == 64) {
-#pragma unroll
-        for (int e = 0; e < 64; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sv[e >> 5][e & 31]));
-      } else {
-#pragma unroll
-        for (int e = 0; e < 64; ++e) {
-          const float x = e < lim ? __uint_as_float(sv[e >> 5][e & 31]) : -INFINITY;
-          sv[e >> 5][e & 31] = __float_as_uint(x);
-          mx8[e & 7] = fmaxf(mx8[e & 7], x);
-        }
+        for (int e = 0; e < 64; ++e)
+          if (e >= lim) sv[e >> 5][e & 31] = __float_as_uint(-INFINITY);
       }
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int e = 0; e < 64; e += 8) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          mx4[q] = max3(mx4[q], __uint_as_float(sv[e >> 5][(e + 2 * q) & 31]),
+                        __uint_as_float(sv[e >> 5][(e + 2 * q + 1) & 31]));
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       const float m_new = fmaxf(m_used, mx * sl2);  // scale > 0: max commutes with scaling
-      const int pb = j % NP;
       const bool rescale = m_used != -INFINITY && m_new > m_used + 8.0f;
       if (__any_sync(0xffffffffu, rescale)) {
         // This half's O must be final up to block j-1 before it is rescaled in TMEM.
-        if (j > 0 && !__all_sync(0xffffffffu, sm100::mbar_wait(pv_done((j - 1) % NP), ((j - 1) / NP) & 1, abort,
+        if (j > 0 && !__all_sync(0xffffffffu, sm100::mbar_wait(pv_done((j - 1) & 1), ((j - 1) >> 1) & 1, abort,
                                                                 err, ERR_PV_DONE, WAIT_LIMIT))) {
           ok = false;
           break;
@@ -403,47 +447,41 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (m_used == -INFINITY) m_used = m_new;  // first visible keys: this O row is still zero
       const float neg_mb = m_used == -INFINITY ? 0.f : -m_used;
-      // P buffer pb is free once the P.V that last read it (block j - NP) is done.
-      if (j >= NP && !__all_sync(0xffffffffu, sm100::mbar_wait(pv_done(pb), ((j / NP) - 1) & 1, abort, err,
-                                                                ERR_PV_DONE, WAIT_LIMIT))) {
-        ok = false;
-        break;
-      }
-      uint8_t* pdst = gbase + L::P_OFF + pb * L::P_BYTES + half * SUB;  // this half's keys = sub-tile `half`
-      float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent sum chains
+      // P overwrites this thread's own S columns (already loaded): hi in the
+      // first 32, split lo in the next 32; two 16-bit values per column.
+      uint32_t phi[32], plo[32];
+      // P = 2^(s*scale*log2e - m) two columns at a time (packed fp32 FMA and
+      // adds, MUFU ex2 per value); four independent pair sums.
+      const uint64_t scale2 = f2(sl2, sl2), shift2 = f2(neg_mb, neg_mb);
+      uint64_t sum2[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 hi, lw;
-        if (c * 8 >= lim) {  // fully masked group: P = 0 without exp
-          hi = make_uint4(0, 0, 0, 0);
-          lw = hi;
-        } else {
-          float p[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            // 2^(s*scale*log2e - m); masked columns hold -inf and give 0.
-            p[e] = ex2_approx(fmaf(__uint_as_float(sv[c >> 2][(c & 3) * 8 + e]), sl2, neg_mb));
-            ls8[e] += p[e];
-          }
-          hi.x = pack2_hw<T>(p[0], p[1]);
-          hi.y = pack2_hw<T>(p[2], p[3]);
-          hi.z = pack2_hw<T>(p[4], p[5]);
-          hi.w = pack2_hw<T>(p[6], p[7]);
-          if constexpr (SPLIT) {
-            lw.x = pack2_hw<T>(p[0] - lo_half<T>(hi.x), p[1] - hi_half<T>(hi.x));
-            lw.y = pack2_hw<T>(p[2] - lo_half<T>(hi.y), p[3] - hi_half<T>(hi.y));
-            lw.z = pack2_hw<T>(p[4] - lo_half<T>(hi.z), p[5] - hi_half<T>(hi.z));
-            lw.w = pack2_hw<T>(p[6] - lo_half<T>(hi.w), p[7] - hi_half<T>(hi.w));
-          }
+      for (int e = 0; e < 64; e += 2) {
+        float t0, t1;
+        f2_split(f2_fma(f2(__uint_as_float(sv[e >> 5][e & 31]), __uint_as_float(sv[e >> 5][(e + 1) & 31])), scale2,
+                        shift2),
+                 t0, t1);
+        const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
+        const uint64_t pp = f2(p0, p1);
+        sum2[(e >> 1) & 3] = f2_add(sum2[(e >> 1) & 3], pp);
+        const uint32_t h2 = pack2_hw<T>(p0, p1);
+        phi[e >> 1] = h2;
+        if constexpr (SPLIT) {
+          // Low halves: P - round(P), exact in fp32, rounded once more.
+          float d0, d1;
+          f2_split(f2_sub(pp, f2(lo_half<T>(h2), hi_half<T>(h2))), d0, d1);
+          plo[e >> 1] = pack2_hw<T>(d0, d1);
         }
-        const uint32_t off = swz(row, c);
-        *reinterpret_cast<uint4*>(pdst + off) = hi;
-        if constexpr (SPLIT) *reinterpret_cast<uint4*>(pdst + 2 * SUB + off) = lw;
       }
-      lsum += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
-      sm100::fence_proxy_async_smem();
+      {
+        float a0, a1;
+        f2_split(f2_add(f2_add(sum2[0], sum2[1]), f2_add(sum2[2], sum2[3])), a0, a1);
+        lsum += a0 + a1;
+      }
+      sm100::tmem_st32(tmem + lane_base + b * BN + scol, phi);
+      if constexpr (SPLIT) sm100::tmem_st32(tmem + lane_base + b * BN + scol + 32, plo);
+      sm100::tmem_wait_st();
       sm100::tc_fence_before();
-      sm100::mbar_arrive(p_full(pb));
+      sm100::mbar_arrive(p_full(b));
     }
     // Merge the two halves of each row: both threads of a row read (max, sum)
     // of both halves, then each produces HD output columns from both O halves.
@@ -462,7 +500,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         lrow = w_self * lsum + w_other * l_o;
       }
     }
-    if (ok && __all_sync(0xffffffffu, sm100::mbar_wait(pv_done((nblk - 1) % NP), ((nblk - 1) / NP) & 1, abort,
+    if (ok && __all_sync(0xffffffffu, sm100::mbar_wait(pv_done((nblk - 1) & 1), ((nblk - 1) >> 1) & 1, abort,
                                                        err, ERR_PV_DONE, WAIT_LIMIT))) {
       sm100::tc_fence_after();
       // O columns [half*HD, half*HD+HD) of this row = w_self*O_self + w_other*O_other.
@@ -515,14 +553,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // One warp per m-entry: O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
-// Partials are read in batches of up to 8 chunks with all loads issued before
-// any use, so the merge is one memory round trip per batch, not per chunk.
+// One pass over the chunks in batches of up to 16: every load of a batch is
+// issued before any use (one memory round trip per batch), and batches merge
+// with a running max. The chunk order is fixed, so the result is too.
 template <class T, int D>
 __global__ void __launch_bounds__(256) attn_combine_kernel(Args a) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
   pdl_wait();  // every input may come from the previous kernel
-  constexpr int PER = D / 32;  // values per lane
-  constexpr int BATCH = 8;
+  constexpr int PER = D / 32;  // values per lane: 4 (D=128) or 2 (D=64)
+  constexpr int BATCH = 16;
+  using Vec = typename std::conditional<PER == 4, float4, float2>::type;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
   const int64_t m_abs = static_cast<int64_t>(blockIdx.x) * 8 + warp;
@@ -537,39 +577,36 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(Args a) {
   int nv = static_cast<int>(pmax / a.chunk) + 1;
   if (nv > a.nchunks) nv = a.nchunks;
   const int64_t w0 = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks;
-  // Pass 1: running max over all chunks.
-  float M = -INFINITY;
-  for (int c0 = 0; c0 < nv; c0 += BATCH) {
-    float mv[BATCH];
-#pragma unroll
-    for (int i = 0; i < BATCH; ++i)
-      mv[i] = c0 + i < nv ? a.ws_ml[((w0 + c0 + i) * BM + row) * 2] : -INFINITY;
-#pragma unroll
-    for (int i = 0; i < BATCH; ++i) M = fmaxf(M, mv[i]);
-  }
-  // Pass 2: weighted sums.
-  float Lsum = 0.f, acc[PER];
+  float M = -INFINITY, Lsum = 0.f, acc[PER];
 #pragma unroll
   for (int e = 0; e < PER; ++e) acc[e] = 0.f;
   for (int c0 = 0; c0 < nv; c0 += BATCH) {
     float2 ml[BATCH];
-    float ov[BATCH][PER];
+    Vec ov[BATCH];
 #pragma unroll
     for (int i = 0; i < BATCH; ++i) {
       const bool in = c0 + i < nv;
       const int64_t w = w0 + (in ? c0 + i : 0);
       ml[i] = in ? *reinterpret_cast<const float2*>(a.ws_ml + (w * BM + row) * 2) : make_float2(-INFINITY, 0.f);
-      const float* src = a.ws_o + (w * BM + row) * D + lane * PER;
-#pragma unroll
-      for (int e = 0; e < PER; ++e) ov[i][e] = in ? src[e] : 0.f;
+      if (in) ov[i] = *reinterpret_cast<const Vec*>(a.ws_o + (w * BM + row) * D + lane * PER);
     }
+    float mb = M;
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i) mb = fmaxf(mb, ml[i].x);
+    const float keep = (M == -INFINITY) ? 0.f : exp2f(M - mb);  // rescale what earlier batches summed
+    Lsum *= keep;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) acc[e] *= keep;
 #pragma unroll
     for (int i = 0; i < BATCH; ++i) {
-      const float wgt = ml[i].x == -INFINITY ? 0.f : exp2f(ml[i].x - M);
+      if (c0 + i >= nv) break;
+      const float wgt = ml[i].x == -INFINITY ? 0.f : exp2f(ml[i].x - mb);
       Lsum += wgt * ml[i].y;
+      const float* v = reinterpret_cast<const float*>(&ov[i]);
 #pragma unroll
-      for (int e = 0; e < PER; ++e) acc[e] += wgt * ov[i][e];
+      for (int e = 0; e < PER; ++e) acc[e] += wgt * v[e];
     }
+    M = mb;
   }
   const float inv = 1.0f / Lsum;
   const int64_t r = m_abs / G;

@@ -26,6 +26,32 @@ int selected_attention(const void* q, const void* k_cache, const void* v_cache, 
                        int64_t max_position, float scale, int precision, void* workspace, size_t workspace_bytes,
                        int dtype, void* stream, bool status_zeroed);
 
+// kvr_add_rmsnorm whose delta may instead be a deferred projection: nparts
+// fp32 slices (row stride part_stride, slice stride part_slice floats),
+// summed in order and rounded before the residual add.
+int add_rmsnorm_ex(void* hidden, const void* delta, const float* parts, int nparts, int64_t part_stride,
+                   int64_t part_slice, const void* weight, void* out, int64_t rows, int hidden_size,
+                   int64_t hidden_stride, int64_t delta_stride, int64_t out_stride, float eps, int dtype,
+                   void* stream);
+
+// Deferred q/k/v projection for qkv_rope_scatter_ex: `count` fp32 slices of
+// [rows][row_stride] (slice stride `slice` floats), q/k/v at columns
+// q_col/k_col/v_col.
+struct QkvParts {
+  const float* data;
+  int count;
+  int64_t row_stride, slice, q_col, k_col, v_col;
+};
+
+// kvr_qkv_rope_scatter reading q/k/v from `parts` when given (q_in/k_in/v_in
+// are then unused).
+int qkv_rope_scatter_ex(const void* q_in, const void* k_in, const void* v_in, int64_t q_row_stride,
+                        int64_t k_row_stride, int64_t v_row_stride, const void* q_norm_w, const void* k_norm_w,
+                        float eps, const void* cos_tab, const void* sin_tab, const int64_t* positions,
+                        int64_t rows, int q_heads, int kv_heads, int head_dim, void* q_out, void* k_cache,
+                        void* v_cache, int64_t cache_rows, int64_t cache_head_stride, int64_t cache_row_stride,
+                        int* error_count, int dtype, void* stream, const QkvParts* parts);
+
 // Call right after each kernel launch.
 inline int check_launch() {
   cudaError_t e = cudaGetLastError();

@@ -101,6 +101,7 @@ struct Layout {
 struct Segment {
   uint16_t* out;
   int64_t out_stride;
+  float* part;  // deferred mode: this segment's fp32 partial buffer (slice 0, row 0, column 0)
   int64_t n;
   int tile_begin;  // first global tile of this segment
   int paired;      // 64 rows of gate + 64 rows of up per tile; out = silu(gate) * up
@@ -117,6 +118,7 @@ struct Args {
   int dp_tiles;  // stream-K mode: tiles [0, dp_tiles) are streamed whole, after the stream-K part
   int sk_grid;   // stream-K mode: CTAs that share the stream-K part (<= grid, <= sk_units)
   int64_t sk_units;  // stream-K mode: (tiles - dp_tiles) * kchunks
+  int64_t part_stride, part_slice;  // deferred mode (part_slice > 0): partial layout, floats
   int* status;
   int* counters;    // [tiles - dp_tiles]
   float* partials;  // [sk_grid][2 slots][BN / 4][128][4]
@@ -416,6 +418,25 @@ __global__ void __launch_bounds__(THREADS, 1) linear_kernel(const __grid_constan
       const Segment sg = seg_at(a, seg_index(a, t));
       const int lt = t - sg.tile_begin;
       const uint32_t acc = tmem + lane_base + static_cast<uint32_t>(buf * BN);
+      if (a.part_slice) {
+        // Deferred reduction: this CTA's fp32 partial (k range b % split) of
+        // weight row n for every x row; the consumer sums the slices.
+        const int64_t n = static_cast<int64_t>(lt) * BM + row;
+        float* dst = sg.part + (b % a.split) * a.part_slice + n;
+        for (int q = wg; q < qn; q += 2) {
+          uint32_t r[32];
+          sm100::tmem_ld32(acc + q * 32, r);
+          sm100::tmem_wait_ld();
+          if (n < sg.n) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (q * 32 + e < a.rows) dst[static_cast<int64_t>(q * 32 + e) * a.part_stride] = __uint_as_float(r[e]);
+          }
+        }
+        sm100::tc_fence_before();
+        sm100::mbar_arrive(acc_empty(buf));
+        continue;
+      }
       if (a.split > 1) {
         // Split-K: the fp32 partial goes to this CTA's ring ([x row][weight
         // row]), free now that every MMA has read its stage; the cluster sums
@@ -521,7 +542,7 @@ __global__ void __launch_bounds__(THREADS, 1) linear_kernel(const __grid_constan
     }
   }
 
-  if (a.split > 1) {
+  if (a.split > 1 && !a.part_slice) {
     // Split-K reduction. Once the whole cluster is here, every CTA's partial
     // is in its shared memory and every ring is idle. x rows [rows*r/S,
     // rows*(r+1)/S) belong to rank r: each rank pushes each peer's rows of its
@@ -733,7 +754,7 @@ int choose_split(int dev, int tiles, int kchunks, int rows) {
 }
 
 template <class T, int BN>
-int launch(const Maps& maps, Args a, const Plan& p, cudaStream_t s) {
+int launch(const Maps& maps, Args a, const Plan& p, cudaStream_t s, int deferred) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -743,22 +764,27 @@ int launch(const Maps& maps, Args a, const Plan& p, cudaStream_t s) {
   const int st = configure<T, BN>(dev);
   if (st != KVR_OK) return st;
   unsigned grid = static_cast<unsigned>(p.grid);
-  if (p.stream_k) {
+  int cluster = 1;
+  if (deferred > 0) {  // one wave of independent CTAs, no cluster
+    a.split = deferred;
+    grid = static_cast<unsigned>(p.tiles * a.split);
+  } else if (p.stream_k) {
     a.split = 0;
   } else {
     a.split = choose_split<T, BN>(dev, p.tiles, p.kchunks, a.rows);
+    cluster = a.split;
     grid = static_cast<unsigned>(p.tiles * a.split);
   }
-  return launch_pdl<linear_kernel<T, BN>>(dim3(grid), dim3(THREADS), Layout<BN>::BYTES, s, a.split, maps, a);
+  return launch_pdl<linear_kernel<T, BN>>(dim3(grid), dim3(THREADS), Layout<BN>::BYTES, s, cluster, maps, a);
 }
 
 template <class T>
-int launch_bn(const Maps& maps, const Args& a, const Plan& p, cudaStream_t s) {
+int launch_bn(const Maps& maps, const Args& a, const Plan& p, cudaStream_t s, int deferred) {
   switch (p.bn) {
-    case 32: return launch<T, 32>(maps, a, p, s);
-    case 64: return launch<T, 64>(maps, a, p, s);
-    case 128: return launch<T, 128>(maps, a, p, s);
-    default: return launch<T, 256>(maps, a, p, s);
+    case 32: return launch<T, 32>(maps, a, p, s, deferred);
+    case 64: return launch<T, 64>(maps, a, p, s, deferred);
+    case 128: return launch<T, 128>(maps, a, p, s, deferred);
+    default: return launch<T, 256>(maps, a, p, s, deferred);
   }
 }
 
@@ -789,9 +815,17 @@ size_t linear_workspace_size(int64_t rows, int64_t k, const kvr_linear_segment* 
   return lin::workspace_bytes(lin::make_plan(rows, k, segments, count));
 }
 
+int deferred_split(int64_t tiles, int64_t k) {
+  const int64_t kc = (k + lin::BK - 1) / lin::BK;
+  int64_t s = tiles > 0 ? kNumSMs / tiles : 1;
+  if (s > kc) s = kc;
+  if (s > 16) s = 16;
+  return s < 1 ? 1 : static_cast<int>(s);
+}
+
 int linear_forward(const void* x, int64_t x_stride, int64_t rows, int64_t k, const kvr_linear_segment* segments,
                    int count, void* workspace, size_t workspace_bytes, int dtype, bool counters_zeroed,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, Deferred* deferred) {
   if (dtype != KVR_DTYPE_BF16 && dtype != KVR_DTYPE_F16) return KVR_ERR_UNSUPPORTED;
   if (rows < 0 || !lin::valid_segments(k, segments, count)) return KVR_ERR_INVALID_ARG;
   if (rows == 0) return KVR_OK;
@@ -799,8 +833,20 @@ int linear_forward(const void* x, int64_t x_stride, int64_t rows, int64_t k, con
   if (k > 0x7fffffffLL) return KVR_ERR_UNSUPPORTED;
   for (int i = 0; i < count; ++i)
     if (segments[i].n > 0x3fffffffLL) return KVR_ERR_UNSUPPORTED;
-  const lin::Plan p = lin::make_plan(rows, k, segments, count);
+  lin::Plan p = lin::make_plan(rows, k, segments, count);
   if (static_cast<int64_t>(p.tiles) * p.kchunks > 0x7fffffffLL) return KVR_ERR_UNSUPPORTED;
+  int defer = 0;
+  if (deferred) {
+    for (int i = 0; i < count; ++i)
+      if (segments[i].weight_up || !deferred->part[i]) return KVR_ERR_INVALID_ARG;
+    if (rows > kMaxRows) return KVR_ERR_UNSUPPORTED;  // one launch: one set of slices
+    defer = deferred_split(p.tiles, k);
+    if (defer > deferred->max_split) defer = deferred->max_split;
+    deferred->split = defer;
+    p.stream_k = false;  // independent CTAs, no stream-K workspace
+    p.dp_tiles = p.sk_grid = 0;
+    p.sk_units = 0;
+  }
   const size_t need = lin::workspace_bytes(p);
   if (!workspace || workspace_bytes < need || !aligned16(workspace)) return KVR_ERR_INVALID_ARG;
   const bool bf16 = dtype == KVR_DTYPE_BF16;
@@ -820,6 +866,11 @@ int linear_forward(const void* x, int64_t x_stride, int64_t rows, int64_t k, con
     a.seg[i].n = sg.n;
     a.seg[i].tile_begin = p.tile_begin[i];
     a.seg[i].paired = paired ? 1 : 0;
+    a.seg[i].part = deferred ? deferred->part[i] : nullptr;
+  }
+  if (deferred) {
+    a.part_stride = deferred->part_stride;
+    a.part_slice = deferred->part_slice;
   }
   a.nseg = count;
   a.kchunks = p.kchunks;
@@ -847,7 +898,8 @@ int linear_forward(const void* x, int64_t x_stride, int64_t rows, int64_t k, con
     a.rows = static_cast<int>(nr);
     for (int i = 0; i < count; ++i)
       a.seg[i].out = static_cast<uint16_t*>(segments[i].out) + r0 * segments[i].out_stride;
-    const int st = bf16 ? lin::launch_bn<BF16>(maps, a, p, stream) : lin::launch_bn<F16>(maps, a, p, stream);
+    const int st =
+        bf16 ? lin::launch_bn<BF16>(maps, a, p, stream, defer) : lin::launch_bn<F16>(maps, a, p, stream, defer);
     if (st != KVR_OK) return st;
   }
   return KVR_OK;

@@ -39,7 +39,8 @@ inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct Buffers {
   bool lin;  // room for the sm_100a projection kernel (rows <= kMaxRows)
-  size_t hidden, normed, delta, qkv, q_rot, attn, gate, up, act, lin_ws, lin_bytes, lin_zero, attn_ws, total;
+  size_t hidden, normed, delta, qkv, q_rot, attn, gate, up, act, lin_ws, lin_bytes, lin_zero, parts, attn_ws, total;
+  int max_split;  // slices the deferred-projection buffer holds
 };
 
 // Workspace of the projection launches of one layer: the largest of the four
@@ -89,6 +90,29 @@ Buffers layout(const kvr_model* m, int64_t rows, int64_t cache_rows) {
   b.lin_bytes = b.lin_zero = 0;
   if (b.lin) linear_plan(m, rows, &b.lin_bytes, &b.lin_zero);
   b.lin_ws = take(b.lin_bytes);
+  // fp32 partial slices of the deferred projections (q/k/v, o, down), summed
+  // by the kernel that consumes each projection.
+  b.max_split = 0;
+  size_t parts_floats = 0;
+  if (b.lin) {
+    const int64_t H = m->hidden, I = m->intermediate;
+    const int64_t qkv_tiles = (static_cast<int64_t>(qd) + 127) / 128 + 2 * ((static_cast<int64_t>(kd) + 127) / 128);
+    const int64_t kv_tiles = 2 * ((static_cast<int64_t>(kd) + 127) / 128);
+    const int s_qkv = deferred_split(qkv_tiles, H), s_kv = deferred_split(kv_tiles, H);
+    const int s_o = deferred_split((H + 127) / 128, static_cast<int64_t>(qd));
+    const int s_down = deferred_split((H + 127) / 128, I);
+    const size_t w_qkv = qd + 2 * kd;
+    auto need = [&](int sp, size_t width) {
+      const size_t f = static_cast<size_t>(sp) * rows * width;
+      if (f > parts_floats) parts_floats = f;
+      if (sp > b.max_split) b.max_split = sp;
+    };
+    need(s_qkv, w_qkv);
+    need(s_kv, w_qkv);
+    need(s_o, H);
+    need(s_down, H);
+  }
+  b.parts = take(parts_floats * sizeof(float));
   b.attn_ws = take(kvr_attention_workspace_size(rows, m->q_heads, m->kv_heads, m->head_dim, cache_rows));
   b.total = off;
   return b;
@@ -211,10 +235,27 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
   } while (0)
 
   void* lin_ws = ws + b.lin_ws;
+  float* parts = reinterpret_cast<float*>(ws + b.parts);
   const bool lin = b.lin && r.projections == KVR_PROJ_SM100;
+  // Deferred reduction of q/k/v, o and down (their consumers sum the fp32
+  // slices); the tensor-parallel all-reduce needs the rounded sums, so there
+  // the projection kernel reduces in-cluster instead.
+  const bool defer = lin && !r.tp_comm;
+  int down_split = 0;  // slices of the previous layer's down projection
   // Projection on the sm_100a kernel: `count` segments sharing input x.
-  auto project = [&](const void* x, int64_t x_stride, int64_t k, const kvr_linear_segment* segs, int count) {
-    return linear_forward(x, x_stride, rows, k, segs, count, lin_ws, b.lin_bytes, m.dtype, true, s);
+  auto project = [&](const void* x, int64_t x_stride, int64_t k, const kvr_linear_segment* segs, int count,
+                     Deferred* d = nullptr) {
+    return linear_forward(x, x_stride, rows, k, segs, count, lin_ws, b.lin_bytes, m.dtype, true, s, d);
+  };
+  auto deferred = [&](int64_t width, float* p0, float* p1 = nullptr, float* p2 = nullptr) {
+    Deferred d{};
+    d.part[0] = p0;
+    d.part[1] = p1;
+    d.part[2] = p2;
+    d.part_stride = width;
+    d.part_slice = rows * width;
+    d.max_split = b.max_split;
+    return d;
   };
   // Status words (attention, projections) and tile counters start at zero;
   // each launch leaves its counters zero, so the layer loop needs no memset
@@ -233,8 +274,13 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
   for (int l = 0; l < m.num_layers; ++l) {
     const kvr_layer_weights& w = m.layers[l];
     const bool final = l == m.num_layers - 1;
-    KVR_TRY(kvr_add_rmsnorm(hidden, l ? delta : nullptr, w.input_norm, normed, rows, H, H, H, H, m.eps, m.dtype,
-                            stream));
+    if (defer && l)
+      KVR_TRY(add_rmsnorm_ex(hidden, nullptr, parts, down_split, H, rows * H, w.input_norm, normed, rows, H, H, H,
+                             H, m.eps, m.dtype, stream));
+    else
+      KVR_TRY(kvr_add_rmsnorm(hidden, l ? delta : nullptr, w.input_norm, normed, rows, H, H, H, H, m.eps, m.dtype,
+                              stream));
+    QkvParts qkv_parts{};
     if (lin) {
       // q/k/v from separate weights or from row ranges of the stacked matrix.
       const uint8_t* wq = static_cast<const uint8_t*>(w.qkv ? w.qkv : w.q);
@@ -246,7 +292,13 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
           {wv, nullptr, kd, qkv + (qd + kd) * 2, qkv_w},
       };
       // The last layer needs no queries.
-      KVR_TRY(final ? project(normed, H, H, segs + 1, 2) : project(normed, H, H, segs, 3));
+      if (defer) {
+        Deferred d = final ? deferred(qkv_w, parts + qd, parts + qd + kd) : deferred(qkv_w, parts, parts + qd, parts + qd + kd);
+        KVR_TRY(final ? project(normed, H, H, segs + 1, 2, &d) : project(normed, H, H, segs, 3, &d));
+        qkv_parts = QkvParts{parts, d.split, qkv_w, rows * qkv_w, 0, qd, qd + kd};
+      } else {
+        KVR_TRY(final ? project(normed, H, H, segs + 1, 2) : project(normed, H, H, segs, 3));
+      }
     } else if (w.qkv) {
       KVR_TRY(gemm(h, normed, H, w.qkv, qkv, qkv_w, rows, qkv_w, H, t));
     } else {
@@ -254,27 +306,45 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
       KVR_TRY(gemm(h, normed, H, w.k, qkv + qd * 2, qkv_w, rows, kd, H, t));
       KVR_TRY(gemm(h, normed, H, w.v, qkv + (qd + kd) * 2, qkv_w, rows, kd, H, t));
     }
-    KVR_TRY(kvr_qkv_rope_scatter(qkv, qkv + qd * 2, qkv + (qd + kd) * 2, qkv_w, qkv_w, qkv_w, w.q_norm, w.k_norm,
-                                 m.eps, r.cos_tab, r.sin_tab, r.positions, rows, m.q_heads, m.kv_heads, D,
-                                 final ? nullptr : q_rot, r.k_cache[l], r.v_cache[l], r.cache_rows,
-                                 r.cache_head_stride, r.cache_row_stride, nullptr, m.dtype, stream));
+    KVR_TRY(qkv_rope_scatter_ex(qkv, qkv + qd * 2, qkv + (qd + kd) * 2, qkv_w, qkv_w, qkv_w, w.q_norm, w.k_norm,
+                                m.eps, r.cos_tab, r.sin_tab, r.positions, rows, m.q_heads, m.kv_heads, D,
+                                final ? nullptr : q_rot, r.k_cache[l], r.v_cache[l], r.cache_rows,
+                                r.cache_head_stride, r.cache_row_stride, nullptr, m.dtype, stream,
+                                defer ? &qkv_parts : nullptr));
     if (final) break;
     KVR_TRY(selected_attention(q_rot, r.k_cache[l], r.v_cache[l], attn, r.positions, rows, m.q_heads, m.kv_heads,
                                D, r.cache_rows, r.cache_head_stride, r.cache_row_stride, r.max_position, scale,
                                r.attention_precision, attn_ws, attn_ws_bytes, m.dtype, stream, true));
+    int o_split = 0;
     if (lin) {
       const kvr_linear_segment o_seg = {w.o, nullptr, H, delta, H};
-      KVR_TRY(project(attn, qd, qd, &o_seg, 1));
+      if (defer) {
+        Deferred d = deferred(H, parts);
+        KVR_TRY(project(attn, qd, qd, &o_seg, 1, &d));
+        o_split = d.split;
+      } else {
+        KVR_TRY(project(attn, qd, qd, &o_seg, 1));
+      }
     } else {
       KVR_TRY(gemm(h, attn, qd, w.o, delta, H, rows, H, qd, t));
     }
     if (r.tp_comm) KVR_TRY(allreduce(delta, rows * H, m.dtype, r.tp_comm, s));
-    KVR_TRY(kvr_add_rmsnorm(hidden, delta, w.post_norm, normed, rows, H, H, H, H, m.eps, m.dtype, stream));
+    if (defer)
+      KVR_TRY(add_rmsnorm_ex(hidden, nullptr, parts, o_split, H, rows * H, w.post_norm, normed, rows, H, H, H, H,
+                             m.eps, m.dtype, stream));
+    else
+      KVR_TRY(kvr_add_rmsnorm(hidden, delta, w.post_norm, normed, rows, H, H, H, H, m.eps, m.dtype, stream));
     if (lin) {
       const kvr_linear_segment mlp = {w.gate, w.up, I, act, I};
       const kvr_linear_segment down = {w.down, nullptr, H, delta, H};
       KVR_TRY(project(normed, H, H, &mlp, 1));
-      KVR_TRY(project(act, I, I, &down, 1));
+      if (defer) {
+        Deferred d = deferred(H, parts);
+        KVR_TRY(project(act, I, I, &down, 1, &d));
+        down_split = d.split;
+      } else {
+        KVR_TRY(project(act, I, I, &down, 1));
+      }
     } else {
       KVR_TRY(gemm(h, normed, H, w.gate, gate, I, rows, I, H, t));
       KVR_TRY(gemm(h, normed, H, w.up, up, I, rows, I, H, t));

@@ -9,11 +9,45 @@ namespace kvr {
 constexpr int kNormThreads = 256;
 constexpr int kNormMaxVecs = 4;  // hidden_size <= 256 * 4 * 8 = 8192
 
+// Sum of `n` fp32 partial slices of 8 consecutive values, in slice order,
+// rounded to the element type (a deferred projection output).
+// Loads of up to kPartBatch slices are all issued before any add (one memory
+// round trip per batch); the adds keep slice order.
+constexpr int kPartBatch = 8;
+
+template <class T>
+__device__ __forceinline__ Vec8 sum_parts8(const float* p, int n, int64_t slice) {
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int s0 = 0; s0 < n; s0 += kPartBatch) {
+    float4 a[kPartBatch], b[kPartBatch];
+#pragma unroll
+    for (int i = 0; i < kPartBatch; ++i) {
+      if (s0 + i < n) {
+        a[i] = __ldcg(reinterpret_cast<const float4*>(p + (s0 + i) * slice));
+        b[i] = __ldcg(reinterpret_cast<const float4*>(p + (s0 + i) * slice + 4));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kPartBatch; ++i) {
+      if (s0 + i < n) {
+        acc[0] += a[i].x; acc[1] += a[i].y; acc[2] += a[i].z; acc[3] += a[i].w;
+        acc[4] += b[i].x; acc[5] += b[i].y; acc[6] += b[i].z; acc[7] += b[i].w;
+      }
+    }
+  }
+  Vec8 v;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v.h[e] = T::from_f(acc[e]);
+  return v;
+}
+
+// With nparts > 0 the delta is a deferred projection: nparts fp32 slices
+// (row stride p_stride, slice stride p_slice floats), summed and rounded here.
 template <class T>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
     uint16_t* hidden, const uint16_t* __restrict__ delta, const uint16_t* __restrict__ weight,
     uint16_t* out, int vpr, int64_t h_stride, int64_t d_stride, int64_t o_stride, float inv_h,
-    float eps) {
+    float eps, const float* __restrict__ parts, int nparts, int64_t p_stride, int64_t p_slice) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
   pdl_wait();  // every input may come from the previous kernel
   const int64_t r = blockIdx.x;
@@ -25,9 +59,10 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
     const int v = threadIdx.x + k * kNormThreads;
     if (v < vpr) {
       x[k] = ld_vec8(hrow + v * 8);
-      if (delta) {
+      if (delta || nparts) {
         // residual + hidden_states, rounded to the element type.
-        Vec8 dv = ld_vec8(delta + r * d_stride + v * 8);
+        Vec8 dv = nparts ? sum_parts8<T>(parts + r * p_stride + v * 8, nparts, p_slice)
+                         : ld_vec8(delta + r * d_stride + v * 8);
 #pragma unroll
         for (int e = 0; e < 8; ++e) x[k].h[e] = T::from_f(__fadd_rn(T::to_f(x[k].h[e]), T::to_f(dv.h[e])));
         st_vec8(hrow + v * 8, x[k]);
@@ -91,6 +126,11 @@ struct QkvArgs {
   uint16_t* v_cache;
   int64_t cache_rows, c_hs, c_rs;
   int* error_count;
+  // Deferred projection (nparts > 0): q/k/v are nparts fp32 slices of
+  // [rows][p_rs] at columns q_col/k_col/v_col, summed and rounded here.
+  const float* parts;
+  int nparts;
+  int64_t p_rs, p_slice, q_col, k_col, v_col;
 };
 
 template <class T, int D>
@@ -119,7 +159,34 @@ __global__ void __launch_bounds__(256) qkv_rope_scatter_kernel(QkvArgs a) {
                        : (is_v ? a.v_cache : a.k_cache) + head * a.c_hs + p * a.c_rs;
   dst += lane * E;
   uint16_t xb[E];
-  if constexpr (E == 4) {
+  if (a.nparts) {
+    const float* ps =
+        a.parts + r * a.p_rs + (is_q ? a.q_col : (is_v ? a.v_col : a.k_col)) + head * D + lane * E;
+    float acc[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = 0.f;
+    for (int s0 = 0; s0 < a.nparts; s0 += kPartBatch) {
+      float pv[kPartBatch][E];
+#pragma unroll
+      for (int i = 0; i < kPartBatch; ++i)
+        if (s0 + i < a.nparts) {
+          if constexpr (E == 4) {
+            const float4 t = __ldcg(reinterpret_cast<const float4*>(ps + (s0 + i) * a.p_slice));
+            pv[i][0] = t.x; pv[i][1] = t.y; pv[i][2] = t.z; pv[i][3] = t.w;
+          } else {
+            const float2 t = __ldcg(reinterpret_cast<const float2*>(ps + (s0 + i) * a.p_slice));
+            pv[i][0] = t.x; pv[i][1] = t.y;
+          }
+        }
+#pragma unroll
+      for (int i = 0; i < kPartBatch; ++i)
+        if (s0 + i < a.nparts)
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[e] += pv[i][e];
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) xb[e] = T::from_f(acc[e]);
+  } else if constexpr (E == 4) {
     uint2 u = *reinterpret_cast<const uint2*>(src);
     *reinterpret_cast<uint2*>(xb) = u;
   } else {
@@ -193,6 +260,18 @@ extern "C" {
 int kvr_add_rmsnorm(void* hidden, const void* delta, const void* weight, void* out, int64_t rows,
                     int hidden_size, int64_t hidden_stride, int64_t delta_stride,
                     int64_t out_stride, float eps, int dtype, void* stream) {
+  return kvr::add_rmsnorm_ex(hidden, delta, nullptr, 0, 0, 0, weight, out, rows, hidden_size, hidden_stride,
+                             delta_stride, out_stride, eps, dtype, stream);
+}
+
+}  // extern "C"
+
+namespace kvr {
+
+int add_rmsnorm_ex(void* hidden, const void* delta, const float* parts, int nparts, int64_t part_stride,
+                   int64_t part_slice, const void* weight, void* out, int64_t rows, int hidden_size,
+                   int64_t hidden_stride, int64_t delta_stride, int64_t out_stride, float eps, int dtype,
+                   void* stream) {
   if (dtype != KVR_DTYPE_BF16 && dtype != KVR_DTYPE_F16) return KVR_ERR_UNSUPPORTED;
   if (rows < 0 || hidden_size <= 0 || hidden_size % 8) return KVR_ERR_INVALID_ARG;
   if (hidden_size > kNormThreads * kNormMaxVecs * 8) return KVR_ERR_UNSUPPORTED;
@@ -202,6 +281,8 @@ int kvr_add_rmsnorm(void* hidden, const void* delta, const void* weight, void* o
       (delta && !aligned16(delta)) || hidden_stride % 8 || out_stride % 8 ||
       (delta && delta_stride % 8))
     return KVR_ERR_INVALID_ARG;
+  if (nparts < 0 || (nparts && (!parts || !aligned16(parts) || part_stride % 4 || part_slice % 4)))
+    return KVR_ERR_INVALID_ARG;
   auto s = static_cast<cudaStream_t>(stream);
   const int vpr = hidden_size / 8;
   const float inv_h = 1.0f / static_cast<float>(hidden_size);
@@ -210,14 +291,18 @@ int kvr_add_rmsnorm(void* hidden, const void* delta, const void* weight, void* o
     st = launch_pdl<add_rmsnorm_kernel<BF16>>(static_cast<unsigned>(rows), dim3(kNormThreads), 0, s, 1, 
         static_cast<uint16_t*>(hidden), static_cast<const uint16_t*>(delta),
         static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), vpr, hidden_stride,
-        delta_stride, out_stride, inv_h, eps);
+        delta_stride, out_stride, inv_h, eps, parts, nparts, part_stride, part_slice);
   else
     st = launch_pdl<add_rmsnorm_kernel<F16>>(static_cast<unsigned>(rows), dim3(kNormThreads), 0, s, 1, 
         static_cast<uint16_t*>(hidden), static_cast<const uint16_t*>(delta),
         static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), vpr, hidden_stride,
-        delta_stride, out_stride, inv_h, eps);
+        delta_stride, out_stride, inv_h, eps, parts, nparts, part_stride, part_slice);
   return st;
 }
+
+}  // namespace kvr
+
+extern "C" {
 
 int kvr_qkv_rope_scatter(const void* q_in, const void* k_in, const void* v_in,
                          int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride,
@@ -226,12 +311,31 @@ int kvr_qkv_rope_scatter(const void* q_in, const void* k_in, const void* v_in,
                          int kv_heads, int head_dim, void* q_out, void* k_cache, void* v_cache,
                          int64_t cache_rows, int64_t cache_head_stride, int64_t cache_row_stride,
                          int* error_count, int dtype, void* stream) {
+  return kvr::qkv_rope_scatter_ex(q_in, k_in, v_in, q_row_stride, k_row_stride, v_row_stride, q_norm_w, k_norm_w,
+                                  eps, cos_tab, sin_tab, positions, rows, q_heads, kv_heads, head_dim, q_out,
+                                  k_cache, v_cache, cache_rows, cache_head_stride, cache_row_stride, error_count,
+                                  dtype, stream, nullptr);
+}
+
+}  // extern "C"
+
+namespace kvr {
+
+int qkv_rope_scatter_ex(const void* q_in, const void* k_in, const void* v_in, int64_t q_row_stride,
+                        int64_t k_row_stride, int64_t v_row_stride, const void* q_norm_w, const void* k_norm_w,
+                        float eps, const void* cos_tab, const void* sin_tab, const int64_t* positions,
+                        int64_t rows, int q_heads, int kv_heads, int head_dim, void* q_out, void* k_cache,
+                        void* v_cache, int64_t cache_rows, int64_t cache_head_stride, int64_t cache_row_stride,
+                        int* error_count, int dtype, void* stream, const QkvParts* parts) {
   if (dtype != KVR_DTYPE_BF16 && dtype != KVR_DTYPE_F16) return KVR_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return KVR_ERR_UNSUPPORTED;
   if (rows < 0 || q_heads <= 0 || kv_heads <= 0 || cache_rows < 0) return KVR_ERR_INVALID_ARG;
   if (rows == 0) return KVR_OK;
-  if (!k_in || !v_in || !cos_tab || !sin_tab || !positions || !k_cache || !v_cache ||
-      (q_out && !q_in))
+  if (!cos_tab || !sin_tab || !positions || !k_cache || !v_cache) return KVR_ERR_INVALID_ARG;
+  if (!parts && (!k_in || !v_in || (q_out && !q_in))) return KVR_ERR_INVALID_ARG;
+  if (parts && (!parts->data || parts->count < 1 || (reinterpret_cast<uintptr_t>(parts->data) & 15u) ||
+                parts->row_stride % 4 || parts->slice % 4 || parts->q_col % 4 || parts->k_col % 4 ||
+                parts->v_col % 4))
     return KVR_ERR_INVALID_ARG;
   // Lanes move 4/8-byte slices of a head: require 8-byte alignment of every base/stride.
   const void* ptrs[] = {q_in, k_in, v_in, q_out, k_cache, v_cache, cos_tab, sin_tab};
@@ -263,6 +367,13 @@ int kvr_qkv_rope_scatter(const void* q_in, const void* k_in, const void* v_in,
   a.c_hs = cache_head_stride;
   a.c_rs = cache_row_stride;
   a.error_count = error_count;
+  a.parts = parts ? parts->data : nullptr;
+  a.nparts = parts ? parts->count : 0;
+  a.p_rs = parts ? parts->row_stride : 0;
+  a.p_slice = parts ? parts->slice : 0;
+  a.q_col = parts ? parts->q_col : 0;
+  a.k_col = parts ? parts->k_col : 0;
+  a.v_col = parts ? parts->v_col : 0;
   const int slots = (q_out ? q_heads : 0) + 2 * kv_heads;
   const int64_t warps = rows * slots;
   const int64_t blocks = (warps + 7) / 8;
@@ -278,6 +389,10 @@ int kvr_qkv_rope_scatter(const void* q_in, const void* k_in, const void* v_in,
   }
   return st;
 }
+
+}  // namespace kvr
+
+extern "C" {
 
 int kvr_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int64_t width,
                  int64_t gate_stride, int64_t up_stride, int64_t out_stride, int dtype,

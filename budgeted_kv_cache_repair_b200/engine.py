@@ -109,9 +109,11 @@ class ModelView:
 
 _views: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
 
-# Probabilities enter P.V as P_hi + P_lo (close to fp32 P, as the reference's
-# own indexed kernel keeps them); ATTN_P_ROUNDED rounds P once like fused SDPA.
-ATTENTION_PRECISION = _lib.ATTN_P_SPLIT
+# Probabilities enter P.V rounded once to the element type, as the fused SDPA
+# kernels of the reference's packed CUDA path do; refreshed rows agree with the
+# reference's outputs as closely as with ATTN_P_SPLIT (P_hi + P_lo, close to
+# fp32 P), which indexed_causal_attention keeps for its fp32-probability parity.
+ATTENTION_PRECISION = _lib.ATTN_P_ROUNDED
 # Projection GEMMs of the layer loop: cuBLAS, or the sm_100a weight-streaming
 # kernel (kvr_linear) for requests of up to 256 rows.
 PROJECTIONS = _lib.PROJ_CUBLAS
