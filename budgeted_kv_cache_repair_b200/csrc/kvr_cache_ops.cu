@@ -127,6 +127,7 @@ __global__ void __launch_bounds__(256) rope_shift_kernel(LayerPtrs ptrs, RopeArg
 // ---------------------------------------------------------------------------
 struct ShiftArgs {
   int heads;
+  int segments;  // num_layers * heads * 2
   int64_t new_rows, prefix, old_tail, new_tail;
   int64_t old_hs, old_rs, new_hs, new_rs;
   int apply_rope;
@@ -139,85 +140,88 @@ struct ShiftPtrs {
   void* v_new[KVR_MAX_LAYER_TENSORS / 2];
 };
 
+// One persistent grid walks all (layer, head, component) segments as one flat
+// sequence of "pairs" (an 8-element vector of a row's low half and its partner
+// in the high half), so every SM moves the same number of bytes whatever the
+// segment count. The grid stride is a multiple of the pairs per row, so a
+// thread always handles the same pair index j of its rows. cos/sin sit in
+// shared memory as one 16-byte (cos_lo, sin_lo, cos_hi, sin_hi) entry per
+// element, padded to 9 entries per pair index so that the 8 pair indices of a
+// warp read disjoint banks.
 template <class T, int D>
-__device__ __forceinline__ void rope_pair_regs(const Vec8& lo, const Vec8& hi, Vec8& olo, Vec8& ohi, int j,
-                                               const float* cs) {
-  constexpr int H = D / 2;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const int d = j * 8 + e;
-    const float xl = T::to_f(lo.h[e]);
-    const float xh = T::to_f(hi.h[e]);
-    olo.h[e] = rope_elem<T>(xl, -xh, cs[d], cs[D + d]);
-    ohi.h[e] = rope_elem<T>(xh, xl, cs[H + d], cs[D + H + d]);
-  }
-}
-
-template <class T, int D>
-__global__ void __launch_bounds__(256) shift_cache_kernel(ShiftPtrs ptrs, ShiftArgs a,
+__global__ void __launch_bounds__(256, 3) shift_cache_kernel(ShiftPtrs ptrs, ShiftArgs a,
                                                           const uint16_t* __restrict__ cos_sin) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
   pdl_wait();  // every input may come from the previous kernel
-  __shared__ float cs[2 * D];
-  // The table is only passed (non-null) when the tail is rotated.
-  if (a.apply_rope)
-    for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) cs[i] = T::to_f(cos_sin[i]);
-  __syncthreads();
-  const int seg = blockIdx.y;
-  const int comp = seg & 1;
-  const int lh = seg >> 1;
-  const int l = lh / a.heads;
-  const int h = lh - l * a.heads;
-  const uint16_t* src =
-      static_cast<const uint16_t*>(comp ? ptrs.v_old[l] : ptrs.k_old[l]) + h * a.old_hs;
-  uint16_t* dst = static_cast<uint16_t*>(comp ? ptrs.v_new[l] : ptrs.k_new[l]) + h * a.new_hs;
   constexpr int PAIRS = D / 16;
   constexpr int HALF = D / 2;
-  constexpr int U = 4;  // vector pairs in flight per thread
-  const bool rotate = comp == 0 && a.apply_rope;
-  const int64_t n = a.new_rows * PAIRS;
-  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < n; i0 += U * step) {
+  constexpr int U = 4;  // pairs in flight per thread (8 x 16-byte loads)
+  const uint32_t tid0 = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t step = gridDim.x * blockDim.x;  // multiple of PAIRS (host-checked)
+  const int j = static_cast<int>(tid0 % PAIRS);
+  __shared__ float4 cs4[PAIRS * 9];  // [pair index][element (+1 pad)] = (cos_lo, sin_lo, cos_hi, sin_hi)
+  if (a.apply_rope) {  // the table is only non-null when the tail rotates
+    for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
+      cs4[(i >> 3) * 9 + (i & 7)] = make_float4(T::to_f(cos_sin[i]), T::to_f(cos_sin[D + i]),
+                                               T::to_f(cos_sin[HALF + i]), T::to_f(cos_sin[D + HALF + i]));
+    }
+  }
+  __syncthreads();
+  const float4* csj = cs4 + j * 9;
+  const uint32_t per_seg = static_cast<uint32_t>(a.new_rows) * PAIRS;
+  const uint32_t total = per_seg * a.segments;
+  for (uint32_t i0 = tid0; i0 < total; i0 += U * step) {
     Vec8 lo[U], hi[U];
-    int64_t drow[U];
-    int jj[U];
+    uint16_t* dst[U];
     bool live[U], rot[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {  // all loads first
-      const int64_t i = i0 + u * step;
-      const int64_t r = i / PAIRS;
-      jj[u] = static_cast<int>(i & (PAIRS - 1));
-      drow[u] = r;
-      int64_t sr = -1;
-      bool tail = false;
-      if (i < n) {
-        if (r < a.prefix) {
-          sr = r;
-        } else if (r >= a.new_tail) {
-          sr = r - a.new_tail + a.old_tail;
-          tail = true;
+      const uint32_t i = i0 + u * step;
+      live[u] = false;
+      rot[u] = false;
+      dst[u] = nullptr;
+      if (i < total) {
+        const uint32_t seg = i / per_seg;
+        const int64_t r = (i - seg * per_seg) / PAIRS;
+        const int comp = seg & 1;
+        const int lh = seg >> 1;
+        const int l = lh / a.heads;
+        const int h = lh - l * a.heads;
+        int64_t sr = -1;
+        if (r < a.prefix) sr = r;
+        else if (r >= a.new_tail) sr = r - a.new_tail + a.old_tail;
+        // rows in [prefix, new_tail) are recomputed by the caller
+        if (sr >= 0) {
+          live[u] = true;
+          rot[u] = comp == 0 && a.apply_rope && r >= a.new_tail;
+          const uint16_t* s = static_cast<const uint16_t*>(comp ? ptrs.v_old[l] : ptrs.k_old[l]) + h * a.old_hs +
+                              sr * a.old_rs + j * 8;
+          dst[u] = static_cast<uint16_t*>(comp ? ptrs.v_new[l] : ptrs.k_new[l]) + h * a.new_hs + r * a.new_rs +
+                   j * 8;
+          lo[u] = ld_vec8_stream(s);
+          hi[u] = ld_vec8_stream(s + HALF);
         }
-      }
-      live[u] = sr >= 0;  // rows in [prefix, new_tail) are recomputed by the caller
-      rot[u] = tail && rotate;
-      if (live[u]) {
-        const uint16_t* s = src + sr * a.old_rs + jj[u] * 8;
-        lo[u] = ld_vec8_stream(s);
-        hi[u] = ld_vec8_stream(s + HALF);
       }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (!live[u]) continue;
-      uint16_t* d = dst + drow[u] * a.new_rs + jj[u] * 8;
       if (rot[u]) {
         Vec8 olo, ohi;
-        rope_pair_regs<T, D>(lo[u], hi[u], olo, ohi, jj[u], cs);
-        st_vec8_stream(d, olo);
-        st_vec8_stream(d + HALF, ohi);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float xl = T::to_f(lo[u].h[e]);
+          const float xh = T::to_f(hi[u].h[e]);
+          // d < D/2: rotate_half = -x[d + D/2];  d >= D/2: rotate_half = x[d - D/2].
+          const float4 t = csj[e];
+          olo.h[e] = rope_elem_hw<T>(xl, -xh, t.x, t.y);
+          ohi.h[e] = rope_elem_hw<T>(xh, xl, t.z, t.w);
+        }
+        st_vec8_stream(dst[u], olo);
+        st_vec8_stream(dst[u] + HALF, ohi);
       } else {
-        st_vec8_stream(d, lo[u]);
-        st_vec8_stream(d + HALF, hi[u]);
+        st_vec8_stream(dst[u], lo[u]);
+        st_vec8_stream(dst[u] + HALF, hi[u]);
       }
     }
   }
@@ -288,6 +292,29 @@ using namespace kvr;
 namespace {
 
 bool valid_dtype(int dtype) { return dtype == KVR_DTYPE_BF16 || dtype == KVR_DTYPE_F16; }
+
+// CTAs of `kernel` (256 threads, static shared memory only) resident on all
+// SMs at once, queried once per device: the grid of a persistent kernel.
+template <auto kernel>
+int resident_blocks() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return kNumSMs;
+  }
+  int n = __atomic_load_n(&cache[dev], __ATOMIC_ACQUIRE);
+  if (!n) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess || per_sm < 1) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    n = per_sm * kNumSMs;
+    __atomic_store_n(&cache[dev], n, __ATOMIC_RELEASE);
+  }
+  return n;
+}
 
 int blocks_per_segment(int64_t segment_vecs, int segments, int threads) {
   // Enough CTAs in total for ~8 resident per SM, never more than the work.
@@ -415,20 +442,34 @@ int kvr_shift_cache_layers(const void* const* k_old, const void* const* v_old, v
     p.k_new[l] = k_new[l];
     p.v_new[l] = v_new[l];
   }
-  ShiftArgs a{heads, new_rows, prefix, old_tail_start, new_tail_start,
-              old_head_stride, old_row_stride, new_head_stride, new_row_stride, apply_rope};
   const int segs = num_layers * heads * 2;
+  ShiftArgs a{heads, segs, new_rows, prefix, old_tail_start, new_tail_start,
+              old_head_stride, old_row_stride, new_head_stride, new_row_stride, apply_rope};
   const int64_t pairs = new_rows * (head_dim / 16);
-  dim3 grid(blocks_per_segment(pairs / 4, segs, 256), segs);
+  if (pairs * segs + 8LL * kNumSMs * 256 * 4 > 0xffffffffLL) return KVR_ERR_UNSUPPORTED;  // 32-bit pair index
+  // Persistent: as many CTAs of 256 threads as are resident at once (the grid
+  // stride, a multiple of 256, is then a multiple of the pairs per row).
+  const int64_t need = (pairs * segs + 255) / 256;
+  auto grid_for_kernel = [&](int resident) {
+    return dim3(static_cast<unsigned>(need < resident ? need : resident));
+  };
   auto s = static_cast<cudaStream_t>(stream);
   const uint16_t* cs = static_cast<const uint16_t*>(cos_sin);
   int st = KVR_OK;
   if (dtype == KVR_DTYPE_BF16) {
-    if (head_dim == 128) st = launch_pdl<shift_cache_kernel<BF16, 128>>(grid, dim3(256), 0, s, 1, p, a, cs);
-    else st = launch_pdl<shift_cache_kernel<BF16, 64>>(grid, dim3(256), 0, s, 1, p, a, cs);
+    if (head_dim == 128)
+      st = launch_pdl<shift_cache_kernel<BF16, 128>>(grid_for_kernel(resident_blocks<shift_cache_kernel<BF16, 128>>()),
+                                                      dim3(256), 0, s, 1, p, a, cs);
+    else
+      st = launch_pdl<shift_cache_kernel<BF16, 64>>(grid_for_kernel(resident_blocks<shift_cache_kernel<BF16, 64>>()),
+                                                     dim3(256), 0, s, 1, p, a, cs);
   } else {
-    if (head_dim == 128) st = launch_pdl<shift_cache_kernel<F16, 128>>(grid, dim3(256), 0, s, 1, p, a, cs);
-    else st = launch_pdl<shift_cache_kernel<F16, 64>>(grid, dim3(256), 0, s, 1, p, a, cs);
+    if (head_dim == 128)
+      st = launch_pdl<shift_cache_kernel<F16, 128>>(grid_for_kernel(resident_blocks<shift_cache_kernel<F16, 128>>()),
+                                                     dim3(256), 0, s, 1, p, a, cs);
+    else
+      st = launch_pdl<shift_cache_kernel<F16, 64>>(grid_for_kernel(resident_blocks<shift_cache_kernel<F16, 64>>()),
+                                                    dim3(256), 0, s, 1, p, a, cs);
   }
   return st;
 }

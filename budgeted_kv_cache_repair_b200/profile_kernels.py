@@ -1,6 +1,6 @@
 """Run one engine kernel at benchmark geometry, for profilers.
 
-    python -m budgeted_kv_cache_repair_b200.profile_kernels shift     [--reps N]
+    python -m budgeted_kv_cache_repair_b200.profile_kernels shift     [--reps N] [--layers L]
     python -m budgeted_kv_cache_repair_b200.profile_kernels attention [--reps N] [--precision rounded|split]
     python -m budgeted_kv_cache_repair_b200.profile_kernels copy      [--reps N]
     python -m budgeted_kv_cache_repair_b200.profile_kernels linear    [--reps N] [--only NAME]
@@ -47,19 +47,21 @@ def _time(fn, reps: int) -> float:
     return begin.elapsed_time(end) / reps * 1e3
 
 
-def shift(reps: int) -> None:
+def shift(reps: int, layers: int = LAYERS) -> None:
+    """`layers` < 32 runs the same per-layer geometry on fewer layers (a small
+    case for multi-pass profiler captures; traffic scales with the layers)."""
     lib = _lib.load()
-    ko = [torch.randn(1, KV_HEADS, OLD, D, device="cuda").bfloat16() for _ in range(LAYERS)]
-    vo = [torch.randn(1, KV_HEADS, OLD, D, device="cuda").bfloat16() for _ in range(LAYERS)]
-    kn = [torch.empty(1, KV_HEADS, NEW, D, device="cuda", dtype=torch.bfloat16) for _ in range(LAYERS)]
-    vn = [torch.empty(1, KV_HEADS, NEW, D, device="cuda", dtype=torch.bfloat16) for _ in range(LAYERS)]
+    ko = [torch.randn(1, KV_HEADS, OLD, D, device="cuda").bfloat16() for _ in range(layers)]
+    vo = [torch.randn(1, KV_HEADS, OLD, D, device="cuda").bfloat16() for _ in range(layers)]
+    kn = [torch.empty(1, KV_HEADS, NEW, D, device="cuda", dtype=torch.bfloat16) for _ in range(layers)]
+    vn = [torch.empty(1, KV_HEADS, NEW, D, device="cuda", dtype=torch.bfloat16) for _ in range(layers)]
     table = torch.randn(2 * D, device="cuda").bfloat16()
     stream = _lib.stream_handle()
-    args = (_lib.ptr_array(ko), _lib.ptr_array(vo), _lib.ptr_array(kn), _lib.ptr_array(vn), LAYERS, KV_HEADS, D, NEW,
+    args = (_lib.ptr_array(ko), _lib.ptr_array(vo), _lib.ptr_array(kn), _lib.ptr_array(vn), layers, KV_HEADS, D, NEW,
             DELETE_AT, DELETE_AT + DELETED, DELETE_AT, OLD * D, D, NEW * D, D, table.data_ptr(), 1, _lib.DTYPE_BF16,
             stream)
     us = _time(lambda: _lib.check(lib.kvr_shift_cache_layers(*args), "shift"), reps)
-    algo = 2 * 2 * LAYERS * KV_HEADS * NEW * D * 2
+    algo = 2 * 2 * layers * KV_HEADS * NEW * D * 2
     print(f"kvr_shift_cache_layers: {us:.1f} us/launch, {algo / us / 1e3:.0f} GB/s on {algo} algorithmic bytes")
 
 
@@ -173,11 +175,12 @@ def main() -> None:
     parser.add_argument("kernel", choices=["shift", "attention", "copy", "linear"])
     parser.add_argument("--only", default=None, help="linear: one of qkv, o, gate_up, down")
     parser.add_argument("--reps", type=int, default=10)
+    parser.add_argument("--layers", type=int, default=LAYERS, help="shift: layers (fewer for a small capture)")
     parser.add_argument("--precision", choices=["rounded", "split"], default="rounded")
     args = parser.parse_args()
     build.build()
     if args.kernel == "shift":
-        shift(args.reps)
+        shift(args.reps, args.layers)
     elif args.kernel == "copy":
         copy(args.reps)
     elif args.kernel == "linear":

@@ -80,6 +80,47 @@ def test_shift_cache_is_bit_exact_with_reference_fixture(lib, name):
         assert bits_equal(k.cpu(), ek) and bits_equal(v.cpu(), ev)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_shift_cache_special_values_match_torch_ops(lib, dtype):
+    """The rotated tail equals torch's op sequence bit for bit, including NaN,
+    infinities and overflow to infinity (cache.py:47-77: k*cos + rotate_half(k)*sin)."""
+    torch.manual_seed(11)
+    layers, heads, dim, old_rows = 3, 2, 128, 300
+    prefix, old_tail, new_tail = 40, 72, 40
+    new_rows = old_rows - (old_tail - new_tail)
+    k = (torch.randn(layers, heads, old_rows, dim) * 3).to(dtype)
+    v = torch.randn(layers, heads, old_rows, dim).to(dtype)
+    big = torch.finfo(dtype).max
+    special = torch.tensor([float("nan"), float("inf"), -float("inf"), big, -big, 0.0, -0.0], dtype=dtype)
+    k.view(-1)[torch.randint(0, k.numel(), (400,))] = special[torch.randint(0, len(special), (400,))]
+    cos = (torch.rand(dim) * 2 - 1).to(dtype)
+    sin = (torch.rand(dim) * 2 - 1).to(dtype)
+    kd, vd = k.to(DEV), v.to(DEV)
+    k_new = [torch.empty(1, heads, new_rows, dim, dtype=dtype, device=DEV) for _ in range(layers)]
+    v_new = [torch.empty(1, heads, new_rows, dim, dtype=dtype, device=DEV) for _ in range(layers)]
+    L = lib.load()
+    lib.check(L.kvr_shift_cache_layers(lib.ptr_array([kd[i] for i in range(layers)]),
+                                       lib.ptr_array([vd[i] for i in range(layers)]), lib.ptr_array(k_new),
+                                       lib.ptr_array(v_new), layers, heads, dim, new_rows, prefix, old_tail, new_tail,
+                                       old_rows * dim, dim, new_rows * dim, dim, _rope_table(cos, sin).data_ptr(), 1,
+                                       lib.dtype_code(dtype), lib.stream_handle()), "shift")
+    torch.cuda.synchronize()
+    tail = k[:, :, old_tail:]
+    rot = torch.cat((-tail[..., dim // 2:], tail[..., : dim // 2]), dim=-1)
+    expected_tail = tail * cos + rot * sin
+    for i in range(layers):
+        got = k_new[i][0].cpu()
+        assert bits_equal(got[:, :prefix], k[i, :, :prefix])
+        g, e = got[:, new_tail:], expected_tail[i]
+        # A NaN's bit pattern depends on the conversion unit that made it
+        # (torch writes different NaN payloads on CPU and CUDA): compare NaN-ness
+        # there and every bit everywhere else.
+        nan = torch.isnan(e)
+        assert torch.equal(torch.isnan(g), nan)
+        assert bits_equal(g[~nan], e[~nan])
+        assert bits_equal(v_new[i][0].cpu()[:, new_tail:], v[i, :, old_tail:])
+
+
 @pytest.mark.parametrize("dense", [True, False])
 def test_copy_layers_is_bitwise(lib, dense):
     torch.manual_seed(2)
