@@ -341,7 +341,7 @@ def our_arm(args):
     model = build_model(cfg, seed, device)
     shim = OperatorShim(model)
     old_ids, new_ids, old_pairs, intervals = synthetic_request(cfg, seed, device)
-    from budgeted_kv_cache_repair_b200.cache import make_cache
+    from budgeted_kv_cache_repair_b200.cache import copy_layers, make_cache
 
     old_cache = make_cache(old_pairs)
     length = new_ids.shape[1]
@@ -406,18 +406,23 @@ def our_arm(args):
     host_ids = new_ids.cpu().pin_memory()
     pos_dev = torch.tensor([p for a, b in intervals for p in range(a, b)], device=device)
     readback = torch.empty((2, cfg["kv_heads"], rows, cfg["head_dim"]), dtype=torch.bfloat16).pin_memory()
-    for _ in range(max(1, args.warmup)):
+
+    def e2e_step():
         out, _ = packed_interval_repair(shim, shifted, host_ids, intervals)
+        k_last, v_last = cache_layers(out)[-1]
+        sel = torch.stack((k_last[0].index_select(1, pos_dev), v_last[0].index_select(1, pos_dev)))
+        readback.copy_(sel, non_blocking=True)
+
+    # The warm-up runs the whole step, readback included: the first
+    # index_select loads its CUDA module, which must not land in the timing.
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
     torch.cuda.synchronize()
     _barrier(world)
     e_begin = torch.cuda.Event(enable_timing=True)
     e_begin.record(stream)
     for _ in range(args.steps):
-        out, _ = packed_interval_repair(shim, shifted, host_ids, intervals)
-        k_last, v_last = cache_layers(out)[-1]
-        sel = torch.stack((k_last[0].index_select(1, pos_dev), v_last[0].index_select(1, pos_dev)))
-        readback.copy_(sel, non_blocking=True)
-        del out
+        e2e_step()
     e_end = torch.cuda.Event(enable_timing=True)
     e_end.record(stream)
     torch.cuda.synchronize()
@@ -432,13 +437,14 @@ def our_arm(args):
         return
 
     # Kernel attribution in a separate pass (event brackets add host work, so
-    # they stay out of the timed region): the ownership copy inside the API
-    # call, and the attention kernel alone on one layer of this request.
+    # they stay out of the timed region): the ownership copy as one isolated
+    # launch over every layer (inside the API call it runs per layer on a
+    # second stream, overlapped with the refresh), and the attention kernel
+    # alone on one layer of this request.
     timer = engine.KernelTimer()
     engine.set_kernel_timer(timer)
     for _ in range(3):
-        out, _ = packed_interval_repair(shim, shifted, ids_dev, intervals)
-        del out
+        copy_layers(cache_layers(shifted))
     engine.set_kernel_timer(None)
     torch.cuda.synchronize()
     totals = timer.totals_ms()
@@ -451,7 +457,7 @@ def our_arm(args):
         gbs = 2 * cache_bytes / (ms / n / 1e3) / 1e9
         kernels["copy_layers"] = {"launches": n, "avg_us": ms / n * 1e3, "bytes_per_launch": 2 * cache_bytes,
                                   "achieved_gbs": gbs, "frac_hbm": gbs / hbm,
-                                  "est_share_of_step": ms / n / statistics.median(step_ms)}
+                                  "note": "isolated launch; overlapped with the refresh inside the API call"}
     if "selected_attention" in totals:
         n, ms = totals["selected_attention"]
         kv_bytes = 2 * cfg["kv_heads"] * (max(p for a, b in intervals for p in range(a, b)) + 1) * cfg["head_dim"] * 2
@@ -516,7 +522,7 @@ def tp_arm(args):
 
     from budgeted_kv_cache_repair_b200 import _lib
     from budgeted_kv_cache_repair_b200 import build as native_build
-    from budgeted_kv_cache_repair_b200.cache import allocate_layers, copy_layers
+    from budgeted_kv_cache_repair_b200.cache import allocate_layers
     from budgeted_kv_cache_repair_b200.plan import IndexedPlan
     from budgeted_kv_cache_repair_b200.tp import ShardView, TPGroup, refresh_rows_tp
 
@@ -569,9 +575,9 @@ def tp_arm(args):
     group = TPGroup(rank, world, device) if world > 1 else None
 
     def step():
-        owned = copy_layers(base)
+        owned = allocate_layers(cfg["layers"], hk, length, d, torch.bfloat16, device)
         dp = plan.to(device)
-        refresh_rows_tp(view, owned, ids, dp.positions, plan.max_position, length, group)
+        refresh_rows_tp(view, owned, ids, dp.positions, plan.max_position, length, group, sources=base)
         return owned
 
     for _ in range(args.warmup):

@@ -50,7 +50,9 @@ class RefreshRequest(ctypes.Structure):
                 ("cache_row_stride", ctypes.c_int64), ("ids", ctypes.c_void_p), ("id_count", ctypes.c_int64),
                 ("positions", ctypes.c_void_p), ("rows", ctypes.c_int64), ("max_position", ctypes.c_int64),
                 ("cos_tab", ctypes.c_void_p), ("sin_tab", ctypes.c_void_p), ("attention_precision", ctypes.c_int),
-                ("tp_comm", ctypes.c_void_p), ("projections", ctypes.c_int)]
+                ("tp_comm", ctypes.c_void_p), ("projections", ctypes.c_int),
+                ("k_src", ctypes.POINTER(ctypes.c_void_p)), ("v_src", ctypes.POINTER(ctypes.c_void_p)),
+                ("src_head_stride", ctypes.c_int64), ("src_row_stride", ctypes.c_int64)]
 
 
 LINEAR_MAX_SEGMENTS = 4

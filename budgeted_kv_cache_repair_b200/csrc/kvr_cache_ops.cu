@@ -3,8 +3,10 @@
 //
 // All of them move 16-byte vectors (8 bf16/fp16) with consecutive threads on
 // consecutive addresses. A "segment" is one (tensor, head) plane of rows*D
-// elements; blockIdx.y walks segments and blockIdx.x (grid-stride) walks rows
-// inside a segment, so no per-vector integer division is needed.
+// elements. The copy runs one short CTA per 16 KB chunk and the shift a
+// persistent grid (the CTAs resident on all SMs), both over work units that
+// span every segment; the others index segments with blockIdx.y and rows with
+// blockIdx.x.
 #include <stdio.h>
 
 #include "kvr_common.cuh"
@@ -24,45 +26,63 @@ void count_launch() { __atomic_add_fetch(&g_launches, 1ull, __ATOMIC_RELAXED); }
 // ---------------------------------------------------------------------------
 struct CopyArgs {
   int heads;
-  int64_t rows;
   int vecs_per_row;  // head_dim / 8
   int64_t src_hs, src_rs, dst_hs, dst_rs;  // element strides
   bool dense;        // rows of both sides are contiguous inside a head
+  int64_t nvec;      // 16-byte vectors per segment (rows * vecs_per_row)
+  int64_t chunks_per_seg, chunks;
 };
 
-__global__ void __launch_bounds__(256) copy_layers_kernel(LayerPtrs ptrs, CopyArgs a) {
+constexpr int kCopyThreads = 256;
+constexpr int kCopyUnroll = 4;
+constexpr int kCopyChunk = kCopyThreads * kCopyUnroll;  // vectors per chunk (16 KB)
+
+// One short CTA per 16 KB chunk of a segment: one division per chunk maps it
+// to (segment, offset), and each thread has kCopyUnroll coalesced 16-byte loads in flight
+// before its stores. Short CTAs measured faster than a persistent grid here,
+// and a copy running beside higher-priority work gives SM slots back to it
+// within microseconds.
+__global__ void __launch_bounds__(kCopyThreads) copy_layers_kernel(LayerPtrs ptrs, CopyArgs a) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
   pdl_wait();  // every input may come from the previous kernel
-  const int seg = blockIdx.y;                    // tensor * heads + head
-  const int t = seg / a.heads;
-  const int h = seg - t * a.heads;
-  const uint16_t* src = static_cast<const uint16_t*>(ptrs.src[t]) + h * a.src_hs;
-  uint16_t* dst = static_cast<uint16_t*>(ptrs.dst[t]) + h * a.dst_hs;
-  if (a.dense) {
-    // Whole plane is one contiguous span of rows*D elements on both sides.
-    const int64_t nvec = a.rows * a.vecs_per_row;
-    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    for (; i + 3 * step < nvec; i += 4 * step) {
-      Vec8 v0 = ld_vec8_stream(src + i * 8);
-      Vec8 v1 = ld_vec8_stream(src + (i + step) * 8);
-      Vec8 v2 = ld_vec8_stream(src + (i + 2 * step) * 8);
-      Vec8 v3 = ld_vec8_stream(src + (i + 3 * step) * 8);
-      st_vec8_stream(dst + i * 8, v0);
-      st_vec8_stream(dst + (i + step) * 8, v1);
-      st_vec8_stream(dst + (i + 2 * step) * 8, v2);
-      st_vec8_stream(dst + (i + 3 * step) * 8, v3);
+  for (int64_t c = blockIdx.x; c < a.chunks; c += gridDim.x) {
+    const int64_t seg = c / a.chunks_per_seg;
+    const int64_t base = (c - seg * a.chunks_per_seg) * kCopyChunk + threadIdx.x;
+    const int t = static_cast<int>(seg / a.heads);
+    const int h = static_cast<int>(seg - static_cast<int64_t>(t) * a.heads);
+    const uint16_t* src = static_cast<const uint16_t*>(ptrs.src[t]) + h * a.src_hs;
+    uint16_t* dst = static_cast<uint16_t*>(ptrs.dst[t]) + h * a.dst_hs;
+    Vec8 v[kCopyUnroll];
+    if (a.dense) {
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t i = base + u * kCopyThreads;
+        if (i < a.nvec) v[u] = ld_vec8_stream(src + i * 8);
+      }
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t i = base + u * kCopyThreads;
+        if (i < a.nvec) st_vec8_stream(dst + i * 8, v[u]);
+      }
+    } else {
+      const int vpr = a.vecs_per_row;
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t i = base + u * kCopyThreads;
+        if (i < a.nvec) {
+          const int64_t r = i / vpr;
+          v[u] = ld_vec8_stream(src + r * a.src_rs + (i - r * vpr) * 8);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t i = base + u * kCopyThreads;
+        if (i < a.nvec) {
+          const int64_t r = i / vpr;
+          st_vec8_stream(dst + r * a.dst_rs + (i - r * vpr) * 8, v[u]);
+        }
+      }
     }
-    for (; i < nvec; i += step) st_vec8_stream(dst + i * 8, ld_vec8_stream(src + i * 8));
-    return;
-  }
-  const int vpr = a.vecs_per_row;
-  const int64_t nvec = a.rows * vpr;
-  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nvec; i += step) {
-    const int64_t r = i / vpr;
-    const int v = static_cast<int>(i - r * vpr);
-    st_vec8_stream(dst + r * a.dst_rs + v * 8, ld_vec8_stream(src + r * a.src_rs + v * 8));
   }
 }
 
@@ -359,7 +379,6 @@ int kvr_copy_layers(const void* const* src, void* const* dst, int num_tensors, i
   if (src_row_stride % 8 || dst_row_stride % 8 || src_head_stride % 8 || dst_head_stride % 8)
     return KVR_ERR_INVALID_ARG;
   if (num_tensors == 0 || rows == 0) return KVR_OK;
-  if (static_cast<int64_t>(num_tensors) * heads > 65535) return KVR_ERR_UNSUPPORTED;
   LayerPtrs p;
   for (int t = 0; t < num_tensors; ++t) {
     if (!src[t] || !dst[t] || !aligned16(src[t]) || !aligned16(dst[t])) return KVR_ERR_INVALID_ARG;
@@ -368,16 +387,18 @@ int kvr_copy_layers(const void* const* src, void* const* dst, int num_tensors, i
   }
   CopyArgs a;
   a.heads = heads;
-  a.rows = rows;
   a.vecs_per_row = head_dim / 8;
   a.src_hs = src_head_stride;
   a.src_rs = src_row_stride;
   a.dst_hs = dst_head_stride;
   a.dst_rs = dst_row_stride;
   a.dense = src_row_stride == head_dim && dst_row_stride == head_dim;
-  const int segs = num_tensors * heads;
-  dim3 grid(blocks_per_segment(rows * a.vecs_per_row / 4, segs, 256), segs);
-  return launch_pdl<copy_layers_kernel>(grid, dim3(256), 0, static_cast<cudaStream_t>(stream), 1, p, a);
+  a.nvec = rows * a.vecs_per_row;
+  a.chunks_per_seg = (a.nvec + kCopyChunk - 1) / kCopyChunk;
+  a.chunks = a.chunks_per_seg * num_tensors * heads;
+  if (a.chunks > 0x7fffffffLL) return KVR_ERR_UNSUPPORTED;
+  dim3 grid(static_cast<unsigned>(a.chunks));
+  return launch_pdl<copy_layers_kernel>(grid, dim3(kCopyThreads), 0, static_cast<cudaStream_t>(stream), 1, p, a);
 }
 
 int kvr_rope_shift_layers(const void* const* src, void* const* dst, int num_layers, int heads,

@@ -1,5 +1,8 @@
 // Native layer loop of the packed refresh: one C-ABI call runs the selected
-// rows through every decoder layer on the caller's stream.
+// rows through every decoder layer on the caller's stream. When the request
+// also asks for the ownership copy of a source cache, the loop runs on an
+// internal high-priority stream beside a low-priority copy stream (layer l is
+// copied before its first write), and the caller's stream waits for both.
 //
 // Per layer: residual add + input RMSNorm, q/k/v projection, fused q/k-norm +
 // RoPE + K/V scatter into the cache, selected-query attention, o projection,
@@ -151,6 +154,61 @@ int gemm(cublasHandle_t h, const void* x, int64_t ldx, const void* w, void* y, i
   return st == CUBLAS_STATUS_SUCCESS ? KVR_OK : KVR_ERR_CUDA;
 }
 
+// Per (thread, device) streams for a refresh that also makes the ownership
+// copy: `work` (the highest stream priority) runs the layer loop, `copy` (the
+// lowest) copies one layer per launch. The block scheduler dispatches pending
+// CTAs of `work` first, so the copy's short CTAs fill the SM slots and HBM time
+// that the layer loop leaves idle instead of delaying it. Events: `start`
+// (both streams wait for the caller's earlier work), one per copied layer, and
+// `done` (the caller's stream waits for `work`).
+struct RefreshStreams {
+  cudaStream_t work = nullptr;
+  cudaStream_t copy = nullptr;
+  cudaEvent_t start = nullptr;
+  cudaEvent_t done = nullptr;
+  cudaEvent_t layer[KVR_MAX_LAYER_TENSORS / 2] = {};
+};
+
+int refresh_streams_for_current_device(RefreshStreams** out) {
+  thread_local std::unordered_map<int, RefreshStreams> pools;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return KVR_ERR_CUDA;
+  }
+  RefreshStreams& c = pools[dev];
+  if (!c.layer[KVR_MAX_LAYER_TENSORS / 2 - 1]) {
+    int least = 0, greatest = 0;
+    e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+    if (e == cudaSuccess && !c.work) e = cudaStreamCreateWithPriority(&c.work, cudaStreamNonBlocking, greatest);
+    if (e == cudaSuccess && !c.copy) e = cudaStreamCreateWithPriority(&c.copy, cudaStreamNonBlocking, least);
+    if (e == cudaSuccess && !c.start) e = cudaEventCreateWithFlags(&c.start, cudaEventDisableTiming);
+    if (e == cudaSuccess && !c.done) e = cudaEventCreateWithFlags(&c.done, cudaEventDisableTiming);
+    for (int l = 0; e == cudaSuccess && l < KVR_MAX_LAYER_TENSORS / 2; ++l)
+      if (!c.layer[l]) e = cudaEventCreateWithFlags(&c.layer[l], cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return KVR_ERR_CUDA;
+    }
+  }
+  *out = &c;
+  return KVR_OK;
+}
+
+// Makes the caller's stream wait for the internal work stream when the
+// refresh returns, on success and on every error path alike.
+struct JoinCaller {
+  cudaStream_t caller = nullptr;
+  const RefreshStreams* streams = nullptr;
+  ~JoinCaller() {
+    if (!streams) return;
+    cudaError_t e = cudaEventRecord(streams->done, streams->work);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(caller, streams->done, 0);
+    if (e != cudaSuccess) set_last_cuda_error(e);
+  }
+};
+
 int allreduce(void* buf, int64_t count, int dtype, void* comm, cudaStream_t s) {
   const ncclResult_t st = ncclAllReduce(buf, buf, static_cast<size_t>(count),
                                         dtype == KVR_DTYPE_BF16 ? ncclBfloat16 : ncclFloat16, ncclSum,
@@ -191,14 +249,31 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
   const kvr_model& m = *model;
   const kvr_refresh_request& r = *req;
   if (r.rows < 0 || r.cache_rows <= 0 || !r.k_cache || !r.v_cache) return KVR_ERR_INVALID_ARG;
-  if (r.rows == 0) return KVR_OK;
+  for (int l = 0; l < m.num_layers; ++l)
+    if (!r.k_cache[l] || !r.v_cache[l]) return KVR_ERR_INVALID_ARG;
+  if ((r.k_src == nullptr) != (r.v_src == nullptr)) return KVR_ERR_INVALID_ARG;
+  if (r.k_src)
+    for (int l = 0; l < m.num_layers; ++l)
+      if (!r.k_src[l] || !r.v_src[l]) return KVR_ERR_INVALID_ARG;
+  if (r.rows == 0) {
+    // Nothing to recompute: the ownership copy is the whole call.
+    if (!r.k_src) return KVR_OK;
+    const void* src[KVR_MAX_LAYER_TENSORS];
+    void* dst[KVR_MAX_LAYER_TENSORS];
+    for (int l = 0; l < m.num_layers; ++l) {
+      src[2 * l] = r.k_src[l];
+      src[2 * l + 1] = r.v_src[l];
+      dst[2 * l] = r.k_cache[l];
+      dst[2 * l + 1] = r.v_cache[l];
+    }
+    return kvr_copy_layers(src, dst, 2 * m.num_layers, m.kv_heads, r.cache_rows, m.head_dim, r.src_head_stride,
+                           r.src_row_stride, r.cache_head_stride, r.cache_row_stride, m.dtype, stream);
+  }
   if (!r.ids || !r.positions || !r.cos_tab || !r.sin_tab || r.id_count <= 0 || r.max_position < 0 ||
       r.max_position >= r.cache_rows)
     return KVR_ERR_INVALID_ARG;
   if (r.rows > 0x7fffffffLL) return KVR_ERR_UNSUPPORTED;
   if (r.projections != KVR_PROJ_CUBLAS && r.projections != KVR_PROJ_SM100) return KVR_ERR_INVALID_ARG;
-  for (int l = 0; l < m.num_layers; ++l)
-    if (!r.k_cache[l] || !r.v_cache[l]) return KVR_ERR_INVALID_ARG;
   const Buffers b = layout(&m, r.rows, r.cache_rows);
   if (!workspace || workspace_bytes < b.total || !aligned16(workspace)) return KVR_ERR_INVALID_ARG;
 
@@ -269,6 +344,48 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
     }
   }
 
+  // Ownership copy of the source layers: from here on the layer loop runs on
+  // the internal high-priority stream and the copy on the low-priority one,
+  // one launch and one event per layer, both after the caller's earlier work.
+  JoinCaller join;
+  RefreshStreams* cp = nullptr;
+  if (r.k_src) {
+    KVR_TRY(refresh_streams_for_current_device(&cp));
+    cudaError_t e = cudaEventRecord(cp->start, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cp->work, cp->start, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cp->copy, cp->start, 0);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return KVR_ERR_CUDA;
+    }
+    join.caller = s;
+    join.streams = cp;
+    s = cp->work;
+    stream = cp->work;
+    if (cublasSetStream(h, s) != CUBLAS_STATUS_SUCCESS) return KVR_ERR_CUDA;
+    for (int l = 0; l < m.num_layers; ++l) {
+      const void* src[2] = {r.k_src[l], r.v_src[l]};
+      void* dst[2] = {r.k_cache[l], r.v_cache[l]};
+      KVR_TRY(kvr_copy_layers(src, dst, 2, m.kv_heads, r.cache_rows, D, r.src_head_stride, r.src_row_stride,
+                              r.cache_head_stride, r.cache_row_stride, m.dtype, cp->copy));
+      e = cudaEventRecord(cp->layer[l], cp->copy);
+      if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return KVR_ERR_CUDA;
+      }
+    }
+  }
+  // Layer l of the owned cache is first written by its K/V scatter.
+  auto copied = [&](int l) -> int {
+    if (!cp) return KVR_OK;
+    const cudaError_t e = cudaStreamWaitEvent(s, cp->layer[l], 0);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return KVR_ERR_CUDA;
+    }
+    return KVR_OK;
+  };
+
   KVR_TRY(kvr_embed_rows(m.embed, m.vocab, H, r.ids, r.id_count, r.positions, rows, hidden, nullptr, m.dtype,
                          stream));
   for (int l = 0; l < m.num_layers; ++l) {
@@ -306,6 +423,7 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
       KVR_TRY(gemm(h, normed, H, w.k, qkv + qd * 2, qkv_w, rows, kd, H, t));
       KVR_TRY(gemm(h, normed, H, w.v, qkv + (qd + kd) * 2, qkv_w, rows, kd, H, t));
     }
+    KVR_TRY(copied(l));
     KVR_TRY(qkv_rope_scatter_ex(qkv, qkv + qd * 2, qkv + (qd + kd) * 2, qkv_w, qkv_w, qkv_w, w.q_norm, w.k_norm,
                                 m.eps, r.cos_tab, r.sin_tab, r.positions, rows, m.q_heads, m.kv_heads, D,
                                 final ? nullptr : q_rot, r.k_cache[l], r.v_cache[l], r.cache_rows,

@@ -227,13 +227,17 @@ def linear(x: torch.Tensor, weights, outs=None) -> list[torch.Tensor]:
 
 
 def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Tensor,
-                 max_position: int, cache_rows: int, tp_comm=None) -> None:
+                 max_position: int, cache_rows: int, tp_comm=None, sources=None) -> None:
     """Recompute the selected rows through every layer, writing K/V in place.
 
     ``layers``: the owned output cache, ``[(K, V)]`` each ``[1, Hkv, N, D]``
     with unit D stride and one (head, row) stride pair; ``ids``: ``[N]`` int64
     on the device; ``positions``: ``[B]`` int64 sorted, on the device. One
     ``kvr_packed_refresh`` call runs every layer on the current stream.
+    ``sources``: optional ``[(K, V)]`` of the same geometry that ``layers``
+    first become a copy of (the ownership copy of clone_cache,
+    kernels/packed_cache.py:287), made inside the same call so that layer l's
+    copy overlaps the work on layers before l.
     """
     lib = _lib.load()
     device = positions.device
@@ -251,8 +255,22 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
         cache_row_stride=row_stride, ids=ids.data_ptr(), id_count=ids.numel(), positions=positions.data_ptr(),
         rows=rows, max_position=max_position, cos_tab=cos.data_ptr(), sin_tab=sin.data_ptr(),
         attention_precision=ATTENTION_PRECISION, tp_comm=tp_comm, projections=PROJECTIONS)
-    need = lib.kvr_packed_refresh_workspace_size(model, rows, cache_rows)
-    if not need:
+    if sources is not None:
+        from .cache import uniform_layout
+
+        if len(sources) != len(layers):
+            raise ValueError("sources must give one (K, V) pair per cache layer")
+        heads, src_rows, dim, dtype, src_device, src_hs, src_rs = uniform_layout(sources, "clone_cache")
+        first = layers[0][0]
+        if (heads, dim, dtype, src_device) != (first.shape[1], first.shape[3], first.dtype, first.device) \
+                or src_rows < cache_rows:
+            raise ValueError("sources must match the cache's heads, head_dim, dtype and device and hold its rows")
+        request.k_src = _lib.ptr_array([k for k, _ in sources])
+        request.v_src = _lib.ptr_array([v for _, v in sources])
+        request.src_head_stride, request.src_row_stride = src_hs, src_rs
+    # No rows: the call only makes the ownership copy and takes no workspace.
+    need = lib.kvr_packed_refresh_workspace_size(model, rows, cache_rows) if rows else 0
+    if rows and not need:
         raise ValueError("model geometry is outside the built kernels")
     workspace = torch.empty(need, dtype=torch.uint8, device=device)
     _lib.check(lib.kvr_packed_refresh(model, request, workspace.data_ptr(), need, _lib.stream_handle(device)),

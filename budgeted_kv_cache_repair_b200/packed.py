@@ -3,8 +3,9 @@
 
 Same signature, validation order, error types, receipt keys and ownership
 contract; the native decoder forward with per-layer ``index_copy_`` and masked
-SDPA is replaced by ``engine.refresh_rows`` over an owned copy made by one
-multi-layer copy kernel.
+SDPA is replaced by one ``engine.refresh_rows`` call that also makes the owned
+copy of the cache, layer by layer, overlapped with the refresh of earlier
+layers.
 """
 
 from __future__ import annotations
@@ -14,7 +15,7 @@ from typing import Any, Sequence
 import torch
 
 from . import _lib
-from .cache import copy_layers, make_cache
+from .cache import allocate_layers, make_cache
 from .engine import model_view, refresh_rows
 from .plan import IndexedPlan
 from .validate import qualify_model, validate_cache, validate_intervals
@@ -143,6 +144,8 @@ def packed_interval_repair(
     with torch.cuda.device(device):
         device_plan = host_plan.to(device)
         ids = _device_ids(edited_ids_t, device)
-        owned = copy_layers(layers)                      # kernels/packed_cache.py:287
-        refresh_rows(view, owned, ids, device_plan.positions, host_plan.max_position, length)
+        # The ownership copy (kernels/packed_cache.py:287) runs inside the
+        # refresh call, each layer's copy overlapping earlier layers' work.
+        owned = allocate_layers(len(layers), view.kv_heads, length, view.head_dim, layers[0][0].dtype, device)
+        refresh_rows(view, owned, ids, device_plan.positions, host_plan.max_position, length, sources=layers)
     return make_cache(owned), receipt

@@ -2,7 +2,7 @@
 
     python -m budgeted_kv_cache_repair_b200.profile_kernels shift     [--reps N] [--layers L]
     python -m budgeted_kv_cache_repair_b200.profile_kernels attention [--reps N] [--precision rounded|split]
-    python -m budgeted_kv_cache_repair_b200.profile_kernels copy      [--reps N]
+    python -m budgeted_kv_cache_repair_b200.profile_kernels copy      [--reps N] [--tensors T]
     python -m budgeted_kv_cache_repair_b200.profile_kernels linear    [--reps N] [--only NAME]
 
 Geometry: Llama-3-8B shape (32 layers, 8 KV heads, head_dim 128, bf16),
@@ -65,15 +65,20 @@ def shift(reps: int, layers: int = LAYERS) -> None:
     print(f"kvr_shift_cache_layers: {us:.1f} us/launch, {algo / us / 1e3:.0f} GB/s on {algo} algorithmic bytes")
 
 
-def copy(reps: int) -> None:
+def copy(reps: int, tensors: int = 2 * LAYERS) -> None:
+    """`tensors` 2 is the per-layer copy the refresh call makes; with fewer
+    than 16 tensors each launch copies a different set of the 64, so the
+    timed launches do not find their source in L2."""
     lib = _lib.load()
     src = [torch.randn(1, KV_HEADS, NEW, D, device="cuda").bfloat16() for _ in range(2 * LAYERS)]
     dst = [torch.empty_like(t) for t in src]
     stream = _lib.stream_handle()
-    args = (_lib.ptr_array(src), _lib.ptr_array(dst), 2 * LAYERS, KV_HEADS, NEW, D, NEW * D, D, NEW * D, D,
-            _lib.DTYPE_BF16, stream)
-    us = _time(lambda: _lib.check(lib.kvr_copy_layers(*args), "copy"), reps)
-    algo = 2 * 2 * LAYERS * KV_HEADS * NEW * D * 2
+    sets = max(1, 2 * LAYERS // tensors)
+    args = [(_lib.ptr_array(src[i * tensors:(i + 1) * tensors]), _lib.ptr_array(dst[i * tensors:(i + 1) * tensors]),
+             tensors, KV_HEADS, NEW, D, NEW * D, D, NEW * D, D, _lib.DTYPE_BF16, stream) for i in range(sets)]
+    calls = iter(range(1 << 30))
+    us = _time(lambda: _lib.check(lib.kvr_copy_layers(*args[next(calls) % sets]), "copy"), reps)
+    algo = 2 * tensors * KV_HEADS * NEW * D * 2
     print(f"kvr_copy_layers: {us:.1f} us/launch, {algo / us / 1e3:.0f} GB/s on {algo} algorithmic bytes")
 
 
@@ -176,13 +181,14 @@ def main() -> None:
     parser.add_argument("--only", default=None, help="linear: one of qkv, o, gate_up, down")
     parser.add_argument("--reps", type=int, default=10)
     parser.add_argument("--layers", type=int, default=LAYERS, help="shift: layers (fewer for a small capture)")
+    parser.add_argument("--tensors", type=int, default=2 * LAYERS, help="copy: K/V tensors per launch (2 to 64)")
     parser.add_argument("--precision", choices=["rounded", "split"], default="rounded")
     args = parser.parse_args()
     build.build()
     if args.kernel == "shift":
         shift(args.reps, args.layers)
     elif args.kernel == "copy":
-        copy(args.reps)
+        copy(args.reps, args.tensors)
     elif args.kernel == "linear":
         linear(args.reps, args.only)
     else:

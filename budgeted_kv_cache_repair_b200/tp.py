@@ -160,8 +160,9 @@ class TPGroup:
 
 
 def refresh_rows_tp(view: ShardView, layers, ids, positions, max_position: int, cache_rows: int,
-                    group: TPGroup) -> None:
-    """``engine.refresh_rows`` on this rank's shard; ``layers`` hold this
-    rank's KV heads. Every rank of the group must call it with the same ids
-    and positions."""
-    refresh_rows(view, layers, ids, positions, max_position, cache_rows, tp_comm=group.comm if group else None)
+                    group: TPGroup, sources=None) -> None:
+    """``engine.refresh_rows`` on this rank's shard; ``layers`` (and the
+    optional ``sources`` they first copy) hold this rank's KV heads. Every rank
+    of the group must call it with the same ids and positions."""
+    refresh_rows(view, layers, ids, positions, max_position, cache_rows, tp_comm=group.comm if group else None,
+                 sources=sources)

@@ -58,7 +58,7 @@ KVR_API uint64_t kvr_kernel_launches(void);
  * Output ownership copy of every layer: dst[t][h, n, :] = src[t][h, n, :] for
  * t < num_tensors (K and V of each layer, any order), h < heads, n < rows.
  * Replaces clone_cache (cache.py:31-44) as used by packed_interval_repair
- * (kernels/packed_cache.py:287). One launch for all layers.
+ * (kernels/packed_cache.py:287). One launch for all given tensors.
  */
 KVR_API int kvr_copy_layers(const void* const* src, void* const* dst, int num_tensors,
                     int heads, int64_t rows, int head_dim,
@@ -285,6 +285,15 @@ typedef struct kvr_refresh_request {
                               all-reduced (sum) across the group after each projection */
   int projections;         /* KVR_PROJ_*: which GEMMs run the q/k/v, o, gate/up and down
                               projections (requests above 256 rows always use cuBLAS) */
+  const void* const* k_src;  /* NULL, or num_layers source layers (same geometry as the cache):
+                              the call first makes k_cache/v_cache an ownership copy of
+                              k_src/v_src (clone_cache, kernels/packed_cache.py:287). The layer
+                              loop then runs on an internal high-priority stream and layer l
+                              is copied on a low-priority one while earlier layers compute
+                              (layer l is first written only after its copy); `stream` waits
+                              for both before any later work on it */
+  const void* const* v_src;
+  int64_t src_head_stride, src_row_stride;
 } kvr_refresh_request;
 #define KVR_PROJ_CUBLAS 0  /* cuBLAS GEMMs, fp32 accumulation */
 #define KVR_PROJ_SM100 1   /* kvr_linear's weight-streaming kernel, gate/up fused with SiLU */

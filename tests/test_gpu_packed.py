@@ -87,6 +87,54 @@ def test_scatter_matches_index_copy_of_the_engines_own_rows(name):
             assert bits_equal(got, expect)
 
 
+@pytest.mark.parametrize("name", CASES[:1])
+@torch.no_grad()
+def test_in_call_ownership_copy_matches_copy_then_refresh(name):
+    """``refresh_rows(..., sources=)`` (the copy made inside the native call,
+    per layer on a second stream) gives the same bits as a separate copy
+    followed by an in-place refresh, for a strided source; with no rows it is
+    exactly the copy."""
+    from budgeted_kv_cache_repair_b200 import OperatorShim
+    from budgeted_kv_cache_repair_b200.cache import allocate_layers, copy_layers
+    from budgeted_kv_cache_repair_b200.engine import model_view, refresh_rows
+    from budgeted_kv_cache_repair_b200.packed import _base_and_dtype
+    from budgeted_kv_cache_repair_b200.plan import IndexedPlan
+
+    record = load_golden(name)
+    model = fixture_model(record, DEV)
+    dense = to_cache(record["shifted_layers"], DEV)
+    from budgeted_kv_cache_repair_b200.validate import cache_layers
+    pairs = cache_layers(dense)
+    length = pairs[0][0].shape[2]
+    # Strided source: each layer is a prefix view of a longer buffer.
+    src = []
+    for k, v in pairs:
+        wide_k = torch.zeros(1, k.shape[1], length + 24, k.shape[3], dtype=k.dtype, device=DEV)
+        wide_v = torch.zeros_like(wide_k)
+        wide_k[:, :, :length] = k
+        wide_v[:, :, :length] = v
+        src.append((wide_k[:, :, :length], wide_v[:, :, :length]))
+    view = model_view(_base_and_dtype(OperatorShim(model), pairs, pairs[0][0].device))
+    ids = record["new_ids"].to(DEV).reshape(-1)
+    plan = IndexedPlan(record["positions"], length)
+    positions = plan.to(DEV).positions
+    heads, dim = pairs[0][0].shape[1], pairs[0][0].shape[3]
+
+    expect = copy_layers(src)
+    refresh_rows(view, expect, ids, positions, plan.max_position, length)
+    got = allocate_layers(len(src), heads, length, dim, pairs[0][0].dtype, DEV)
+    refresh_rows(view, got, ids, positions, plan.max_position, length, sources=src)
+    torch.cuda.synchronize()
+    for (gk, gv), (ek, ev) in zip(got, expect):
+        assert bits_equal(gk, ek) and bits_equal(gv, ev)
+
+    empty = allocate_layers(len(src), heads, length, dim, pairs[0][0].dtype, DEV)
+    refresh_rows(view, empty, ids, positions[:0], plan.max_position, length, sources=src)
+    torch.cuda.synchronize()
+    for (gk, gv), (sk, sv) in zip(empty, src):
+        assert bits_equal(gk, sk) and bits_equal(gv, sv)
+
+
 @pytest.mark.parametrize("name", CASES)
 def test_full_support_matches_clean_prefill(name):
     from budgeted_kv_cache_repair_b200 import OperatorShim, packed_interval_repair

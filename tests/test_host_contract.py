@@ -163,7 +163,7 @@ def test_empty_support_returns_base_and_does_no_work(monkeypatch):
 
     monkeypatch.setattr(packed, "qualify_model", forbidden)
     monkeypatch.setattr(packed, "refresh_rows", forbidden)
-    monkeypatch.setattr(packed, "copy_layers", forbidden)
+    monkeypatch.setattr(packed, "allocate_layers", forbidden)
     monkeypatch.setattr(IndexedPlan, "to", forbidden)
     base = make_cache([(torch.zeros(1, 2, 0, 8), torch.zeros(1, 2, 0, 8)) for _ in range(2)])
     actual, receipt = packed_interval_repair(object(), base, torch.empty((1, 0), dtype=torch.long), [])
