@@ -54,6 +54,7 @@ constexpr int kMmaWarp = 9;
 constexpr int THREADS = 320;
 constexpr int SUB = BM * 128;  // one [128 rows x 128 B] swizzled sub-tile
 constexpr int STATUS_BYTES = 256;
+constexpr int kEpilogueBar = 1;        // named barrier of the softmax warps (0 is __syncthreads)
 constexpr long long WAIT_LIMIT = 4000000000LL;  // SM clocks (~2 s)
 
 enum Err : int { ERR_KV_EMPTY = 1, ERR_Q_FULL, ERR_KV_FULL, ERR_S_FREE, ERR_P_FULL, ERR_S_FULL,
@@ -94,6 +95,10 @@ struct Layout {
   // Swizzled tiles need a 1 KB-aligned base; the allocation carries what slack
   // fits under the per-CTA limit and the kernel checks it at run time.
   static constexpr int BYTES = USED + 1024 <= 232448 ? USED + 1024 : 232448;
+  // Staged output rows (epilogue, in the K ring): D floats plus a 16-byte
+  // shift per row, so a warp's row-per-lane float4 stores hit distinct banks.
+  static constexpr int STAGE_STRIDE = D + 4;
+  static_assert(NS * DS * SUB >= BM * STAGE_STRIDE * 4, "the K ring holds the staged output tile");
   static constexpr uint32_t HALF_TX = DS * SUB;  // one K or one V block
   static_assert(USED <= 232448, "dynamic shared memory above the 227 KB per-CTA limit");
 };
@@ -179,7 +184,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                    const __grid_constant__ CUtensorMap tmap_q, Args a) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
-  pdl_wait();  // every input may come from the previous kernel
   using L = Layout<D, SPLIT>;
   constexpr int DS = L::DS, NS = L::NS, NP = L::NP;
   constexpr int HD = D / 2;  // output columns per softmax thread in the epilogue
@@ -195,12 +199,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int64_t m0 = static_cast<int64_t>(tile) * BM;
   int64_t r_last = (m0 + BM - 1) / G;
   if (r_last > a.rows - 1) r_last = a.rows - 1;
-  const int64_t pmax = a.positions[r_last];
   const int64_t k_begin = static_cast<int64_t>(chunk) * a.chunk;
-  if (k_begin > pmax) return;  // chunk lies past every row of the tile (uniform exit)
-  int64_t k_end = k_begin + a.chunk;
-  if (k_end > pmax + 1) k_end = pmax + 1;
-  const int nblk = static_cast<int>((k_end - k_begin + BN - 1) / BN);
 
   const uint32_t raw = sm100::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -253,19 +252,36 @@ __global__ void __launch_bounds__(THREADS, 1)
     sm100::tmem_alloc(sm100::smem_u32(tmem_slot), 512);
     sm100::tmem_relinquish();
   }
+  if (warp == kTmaWarp && lane == 0) {
+    sm100::prefetch_tmap(&tmap_k);
+    sm100::prefetch_tmap(&tmap_v);
+  }
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  // Everything above (barriers, tensor memory, descriptor prefetch) overlaps
+  // the previous kernel; the positions, queries and cache may come from it.
+  pdl_wait();
+  const int64_t pmax = a.positions[r_last];
+  int64_t k_end = k_begin + a.chunk;
+  if (k_end > pmax + 1) k_end = pmax + 1;
+  // A chunk past every row of the tile has no blocks (uniform): straight to teardown.
+  const int nblk = k_begin > pmax ? 0 : static_cast<int>((k_end - k_begin + BN - 1) / BN);
   // TMEM columns: S buffers [0,128) and [128,256); one O accumulator per key
   // half, [256, 256+D) and [256+D, 256+2D).
   constexpr uint32_t TM_O = 256;
 
-  if (warp == kTmaWarp) {
+  if (nblk == 0) {
+    // No keys for this tile in this chunk: no role has work, but the combine
+    // reads every chunk's (max, sum), so the rows record an empty chunk.
+    if (a.nchunks > 1 && tid < BM) {
+      const int64_t wu = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks + chunk;
+      *reinterpret_cast<float2*>(a.ws_ml + (wu * BM + tid) * 2) = make_float2(-INFINITY, 0.f);
+    }
+  } else if (warp == kTmaWarp) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      sm100::prefetch_tmap(&tmap_k);
-      sm100::prefetch_tmap(&tmap_v);
       if (a.q_by_tma) {
         // The tile's 128 m-entries are 128/G consecutive rows x the G heads of
         // KV head h: one box per 64-column half of head_dim.
@@ -500,47 +516,67 @@ __global__ void __launch_bounds__(THREADS, 1)
         lrow = w_self * lsum + w_other * l_o;
       }
     }
-    if (ok && __all_sync(0xffffffffu, sm100::mbar_wait(pv_done((nblk - 1) & 1), ((nblk - 1) >> 1) & 1, abort,
-                                                       err, ERR_PV_DONE, WAIT_LIMIT))) {
+    bool ready = ok && __all_sync(0xffffffffu, sm100::mbar_wait(pv_done((nblk - 1) & 1), ((nblk - 1) >> 1) & 1,
+                                                                abort, err, ERR_PV_DONE, WAIT_LIMIT));
+    // One decision for all softmax warps (the staging below has a barrier).
+    ready = sm100::bar_and_named(kEpilogueBar, kSoftmaxThreads, ready);
+    if (ready) {
       sm100::tc_fence_after();
-      // O columns [half*HD, half*HD+HD) of this row = w_self*O_self + w_other*O_other.
+      // O columns [half*HD, half*HD+HD) of this row = w_self*O_self + w_other*O_other,
+      // staged row-major in the K ring (idle: every K/V load landed before the
+      // MMAs that read it, and the last P.V is done) so that the global writes
+      // below are whole coalesced rows.
       const float w0 = half == 0 ? w_self : w_other;
       const float w1 = half == 0 ? w_other : w_self;
       const bool final_out = a.nchunks == 1;
       const float inv = final_out ? 1.0f / lrow : 1.0f;
-      const int64_t wu = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks + chunk;
-      uint16_t* dst = a.out + (r * a.hq + static_cast<int64_t>(h) * G + g) * D + half * HD;
-      float* wo = a.ws_o + (wu * BM + row) * D + half * HD;
+      float* stage = reinterpret_cast<float*>(gbase + L::K_OFF);
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o0[32], o1[32];
         sm100::tmem_ld32(tmem + lane_base + TM_O + half * HD + c * 32, o0);
         sm100::tmem_ld32(tmem + lane_base + TM_O + D + half * HD + c * 32, o1);
         sm100::tmem_wait_ld();
-        float v[32];
+        float* srow = stage + row * L::STAGE_STRIDE + half * HD + c * 32;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = (w0 * __uint_as_float(o0[e]) + w1 * __uint_as_float(o1[e])) * inv;
-        if (final_out) {
-          if (valid) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w;
-              w.x = pack2<T>(v[q * 8 + 0], v[q * 8 + 1]);
-              w.y = pack2<T>(v[q * 8 + 2], v[q * 8 + 3]);
-              w.z = pack2<T>(v[q * 8 + 4], v[q * 8 + 5]);
-              w.w = pack2<T>(v[q * 8 + 6], v[q * 8 + 7]);
-              *reinterpret_cast<uint4*>(dst + c * 32 + q * 8) = w;
-            }
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<float4*>(wo + c * 32 + q * 4) = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2],
-                                                                          v[q * 4 + 3]);
+        for (int q = 0; q < 8; ++q) {
+          float4 v;
+          v.x = (w0 * __uint_as_float(o0[q * 4 + 0]) + w1 * __uint_as_float(o1[q * 4 + 0])) * inv;
+          v.y = (w0 * __uint_as_float(o0[q * 4 + 1]) + w1 * __uint_as_float(o1[q * 4 + 1])) * inv;
+          v.z = (w0 * __uint_as_float(o0[q * 4 + 2]) + w1 * __uint_as_float(o1[q * 4 + 2])) * inv;
+          v.w = (w0 * __uint_as_float(o0[q * 4 + 3]) + w1 * __uint_as_float(o1[q * 4 + 3])) * inv;
+          *reinterpret_cast<float4*>(srow + q * 4) = v;
         }
       }
+      const int64_t wu = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks + chunk;
       if (!final_out && half == 0)
         *reinterpret_cast<float2*>(a.ws_ml + (wu * BM + row) * 2) = make_float2(mrow, lrow);
+      sm100::bar_sync_named(kEpilogueBar, kSoftmaxThreads);
+      // Copy-out: each warp writes whole rows, lane l the columns [l*D/32, (l+1)*D/32).
+      constexpr int PER = D / 32;
+      for (int rr = warp; rr < BM; rr += kSoftmaxThreads / 32) {
+        const float* srow = stage + rr * L::STAGE_STRIDE + lane * PER;
+        if (final_out) {
+          const int64_t mr = m0 + rr;
+          if (mr >= total_m) continue;
+          const int64_t rw = mr / G;
+          const int gw = static_cast<int>(mr - rw * G);
+          uint16_t* dst = a.out + (rw * a.hq + static_cast<int64_t>(h) * G + gw) * D + lane * PER;
+          if constexpr (PER == 4) {
+            const float4 v = *reinterpret_cast<const float4*>(srow);
+            *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<T>(v.x, v.y), pack2<T>(v.z, v.w));
+          } else {
+            const float2 v = *reinterpret_cast<const float2*>(srow);
+            *reinterpret_cast<uint32_t*>(dst) = pack2<T>(v.x, v.y);
+          }
+        } else {
+          float* wo = a.ws_o + (wu * BM + rr) * D + lane * PER;
+          if constexpr (PER == 4)
+            *reinterpret_cast<float4*>(wo) = *reinterpret_cast<const float4*>(srow);
+          else
+            *reinterpret_cast<float2*>(wo) = *reinterpret_cast<const float2*>(srow);
+        }
+      }
     }
   }
 
@@ -553,9 +589,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // One warp per m-entry: O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
-// One pass over the chunks in batches of up to 16: every load of a batch is
-// issued before any use (one memory round trip per batch), and batches merge
-// with a running max. The chunk order is fixed, so the result is too.
+// Every chunk of the tile has a (max, sum) record (an empty chunk: max -inf,
+// and no O, whose weight 0 skips it), so nothing here waits on the positions:
+// lane c loads (m_c, l_c) of chunk c while the O rows of the first chunks are
+// already in flight (lane l owns columns [l*D/32, (l+1)*D/32)); the warp
+// reduces M and L with shuffles and takes each chunk's weight by shuffle. The
+// chunk order of the sum is fixed, so the result is too.
 template <class T, int D>
 __global__ void __launch_bounds__(256) attn_combine_kernel(Args a) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
@@ -571,40 +610,47 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(Args a) {
   if (m_abs >= total_m) return;
   const int tile = static_cast<int>(m_abs / BM);
   const int row = static_cast<int>(m_abs - static_cast<int64_t>(tile) * BM);
-  int64_t r_last = (static_cast<int64_t>(tile) * BM + BM - 1) / G;
-  if (r_last > a.rows - 1) r_last = a.rows - 1;
-  const int64_t pmax = a.positions[r_last];
-  int nv = static_cast<int>(pmax / a.chunk) + 1;
-  if (nv > a.nchunks) nv = a.nchunks;
-  const int64_t w0 = (static_cast<int64_t>(h) * a.tiles + tile) * a.nchunks;
+  const int nc = a.nchunks;
+  const int64_t w0 = (static_cast<int64_t>(h) * a.tiles + tile) * nc;
   float M = -INFINITY, Lsum = 0.f, acc[PER];
 #pragma unroll
   for (int e = 0; e < PER; ++e) acc[e] = 0.f;
-  for (int c0 = 0; c0 < nv; c0 += BATCH) {
-    float2 ml[BATCH];
+  for (int c0 = 0; c0 < nc; c0 += 32) {
+    const int cn = nc - c0 < 32 ? nc - c0 : 32;
+    const float* o_base = a.ws_o + ((w0 + c0) * BM + row) * D + lane * PER;
     Vec ov[BATCH];
 #pragma unroll
-    for (int i = 0; i < BATCH; ++i) {
-      const bool in = c0 + i < nv;
-      const int64_t w = w0 + (in ? c0 + i : 0);
-      ml[i] = in ? *reinterpret_cast<const float2*>(a.ws_ml + (w * BM + row) * 2) : make_float2(-INFINITY, 0.f);
-      if (in) ov[i] = *reinterpret_cast<const Vec*>(a.ws_o + (w * BM + row) * D + lane * PER);
-    }
-    float mb = M;
+    for (int i = 0; i < BATCH; ++i)
+      if (i < cn) ov[i] = *reinterpret_cast<const Vec*>(o_base + static_cast<int64_t>(i) * BM * D);
+    const float2 ml = lane < cn ? *reinterpret_cast<const float2*>(a.ws_ml + ((w0 + c0 + lane) * BM + row) * 2)
+                                : make_float2(-INFINITY, 0.f);
+    float mb = ml.x;
 #pragma unroll
-    for (int i = 0; i < BATCH; ++i) mb = fmaxf(mb, ml[i].x);
-    const float keep = (M == -INFINITY) ? 0.f : exp2f(M - mb);  // rescale what earlier batches summed
-    Lsum *= keep;
+    for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+    mb = fmaxf(mb, M);
+    const float keep = M == -INFINITY ? 0.f : exp2f(M - mb);  // rescale what earlier groups summed
+    const float wgt = ml.x == -INFINITY ? 0.f : exp2f(ml.x - mb);
+    float lw = wgt * ml.y;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+    Lsum = Lsum * keep + lw;
 #pragma unroll
     for (int e = 0; e < PER; ++e) acc[e] *= keep;
+    for (int b = 0; b < cn; b += BATCH) {
+      if (b > 0) {
 #pragma unroll
-    for (int i = 0; i < BATCH; ++i) {
-      if (c0 + i >= nv) break;
-      const float wgt = ml[i].x == -INFINITY ? 0.f : exp2f(ml[i].x - mb);
-      Lsum += wgt * ml[i].y;
-      const float* v = reinterpret_cast<const float*>(&ov[i]);
+        for (int i = 0; i < BATCH; ++i)
+          if (b + i < cn) ov[i] = *reinterpret_cast<const Vec*>(o_base + static_cast<int64_t>(b + i) * BM * D);
+      }
 #pragma unroll
-      for (int e = 0; e < PER; ++e) acc[e] += wgt * v[e];
+      for (int i = 0; i < BATCH; ++i) {
+        const float wi = __shfl_sync(0xffffffffu, wgt, (b + i) & 31);
+        if (b + i < cn && wi != 0.f) {  // an empty chunk's O was never written
+          const float* v = reinterpret_cast<const float*>(&ov[i]);
+#pragma unroll
+          for (int e = 0; e < PER; ++e) acc[e] += wi * v[e];
+        }
+      }
     }
     M = mb;
   }

@@ -13,7 +13,9 @@ enough weight copies in rotation that no launch finds its weights in L2, and
 replayed from a CUDA graph so that host launch cost is not measured).
 Inputs are seeded random tensors. After two
 warm-up launches the command times `--reps` launches with CUDA events and
-prints the average; under ncu, capture with `-s 2`.
+prints the average (`attention` and `linear`: replayed from a CUDA graph,
+after a capture pass and one replay); under ncu, capture with `-s 2`
+(`attention`: two kernels per call).
 """
 
 from __future__ import annotations
@@ -94,10 +96,11 @@ def attention(reps: int, precision: str) -> None:
     need = lib.kvr_attention_workspace_size(rows, HEADS, KV_HEADS, D, NEW)
     ws = torch.empty(need, dtype=torch.uint8, device="cuda")
     mode = _lib.ATTN_P_SPLIT if precision == "split" else _lib.ATTN_P_ROUNDED
-    stream = _lib.stream_handle()
     args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), pos.data_ptr(), rows, HEADS, KV_HEADS, D, NEW,
-            NEW * D, D, positions[-1], D ** -0.5, mode, ws.data_ptr(), need, _lib.DTYPE_BF16, stream)
-    us = _time(lambda: _lib.check(lib.kvr_selected_attention(*args), "attention"), reps)
+            NEW * D, D, positions[-1], D ** -0.5, mode, ws.data_ptr(), need, _lib.DTYPE_BF16)
+    # Device time per call from a CUDA graph of back-to-back calls: a call's
+    # host work (tensor maps, two launches) is longer than its kernels.
+    us = _graph_time(lambda i: _lib.check(lib.kvr_selected_attention(*args, _lib.stream_handle()), "attention"), reps)
     kv = 2 * KV_HEADS * (positions[-1] + 1) * D * 2
     flops = 4.0 * HEADS * D * sum(p + 1 for p in positions)
     print(f"kvr_selected_attention ({precision}): {us:.1f} us/call, {kv / us / 1e3:.0f} GB/s of K/V, "
