@@ -20,6 +20,12 @@ flush is needed between steps. Times are CUDA events on the launching stream,
 max over ranks. With N GPUs each rank repairs its own request (different seed,
 no collective on the data path): weak scaling.
 
+``--workload config3`` runs BASELINE configs[3] instead: Qwen3-8B shape (36
+layers, per-head q/k RMSNorm, MLP 12288, vocab 151936, rope_theta 1e6),
+32768-token context, 1024 tokens deleted at 4096 (N=31744), 1383 rows (5 % of
+the retained suffix) in 32 intervals; with N GPUs each rank repairs its own
+request (data parallel, weak scaling).
+
 ``--impl reference`` times the reference's packed path restated on the same
 transformers modules (oracle/hf_packed.py; the reference package itself cannot
 be installed on the GPU box) on all host cores, on a bounded sample of the same
@@ -44,10 +50,21 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-CONFIG = dict(name="llama3-8b-shape", layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128,
-              intermediate=14336, vocab=128256, theta=500000.0, context=8192, delete_at=1024, delete=256,
-              intervals=16, rows=64)
-METRIC = "repaired rows/s (packed refresh stage, Llama-3-8B shape, 8192 ctx, 16 intervals, 64 rows)"
+CONFIG = dict(name="llama3-8b-shape", arch="llama", layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128,
+              intermediate=14336, vocab=128256, theta=500000.0, eps=1e-5, context=8192, delete_at=1024, delete=256,
+              intervals=16, rows=64,
+              metric="repaired rows/s (packed refresh stage, Llama-3-8B shape, 8192 ctx, 16 intervals, 64 rows)",
+              workload="config2: Llama-3-8B shape, 8192 ctx, delete 256@1024 (N=7936), 16 intervals x 4 rows")
+METRIC = CONFIG["metric"]
+# Qwen3-8B shape (per-head q/k RMSNorm), 32k context,
+# 5 % of the 27,648-row retained suffix (1,383 rows) over 32 intervals; the
+# data-parallel configuration (independent requests, one per GPU).
+CONFIG3 = dict(name="qwen3-8b-shape", arch="qwen3", layers=36, hidden=4096, heads=32, kv_heads=8, head_dim=128,
+               intermediate=12288, vocab=151936, theta=1000000.0, eps=1e-6, context=32768, delete_at=4096,
+               delete=1024, intervals=32, rows=1383,
+               metric="repaired rows/s (packed refresh stage, Qwen3-8B shape, 32768 ctx, 32 intervals, 1383 rows)",
+               workload="config3: Qwen3-8B shape, 32768 ctx, delete 1024@4096 (N=31744), 1383 rows in 32 intervals")
+WORKLOADS = {"config2": CONFIG, "config3": CONFIG3}
 
 
 def _peaks():
@@ -67,19 +84,36 @@ def make_intervals(seed: int, suffix_start: int, length: int, count: int, width:
     return [(suffix_start + s * (width + 1), suffix_start + s * (width + 1) + width) for s in picks]
 
 
-def build_model(cfg, seed, device):
-    from transformers import LlamaConfig, LlamaForCausalLM
+def budget_intervals(seed: int, suffix_start: int, length: int, count: int, rows: int):
+    """``count`` intervals holding ``rows`` rows in total: width rows // count,
+    the first rows % count of them one row wider (slots one row longer, so the
+    intervals stay non-adjacent); equal to ``make_intervals`` when count
+    divides rows."""
+    width, extra = divmod(rows, count)
+    if not extra:
+        return make_intervals(seed, suffix_start, length, count, width)
+    gen = torch.Generator().manual_seed(seed)
+    slot = width + 2
+    picks = sorted(torch.randperm((length - suffix_start) // slot, generator=gen)[:count].tolist())
+    return [(suffix_start + s * slot, suffix_start + s * slot + width + (1 if i < extra else 0))
+            for i, s in enumerate(picks)]
 
-    config = LlamaConfig(vocab_size=cfg["vocab"], hidden_size=cfg["hidden"], intermediate_size=cfg["intermediate"],
-                         num_hidden_layers=cfg["layers"], num_attention_heads=cfg["heads"],
-                         num_key_value_heads=cfg["kv_heads"], head_dim=cfg["head_dim"], rope_theta=cfg["theta"],
-                         max_position_embeddings=131072, initializer_range=0.02, rms_norm_eps=1e-5)
+
+def build_model(cfg, seed, device):
+    from transformers import LlamaConfig, LlamaForCausalLM, Qwen3Config, Qwen3ForCausalLM
+
+    qwen3 = cfg.get("arch") == "qwen3"
+    config = (Qwen3Config if qwen3 else LlamaConfig)(
+        vocab_size=cfg["vocab"], hidden_size=cfg["hidden"], intermediate_size=cfg["intermediate"],
+        num_hidden_layers=cfg["layers"], num_attention_heads=cfg["heads"], num_key_value_heads=cfg["kv_heads"],
+        head_dim=cfg["head_dim"], rope_theta=cfg["theta"], max_position_embeddings=131072, initializer_range=0.02,
+        rms_norm_eps=cfg.get("eps", 1e-5))
     torch.manual_seed(seed)
     previous = torch.get_default_dtype()
     torch.set_default_dtype(torch.bfloat16)
     try:
         with torch.device(device):
-            model = LlamaForCausalLM(config)
+            model = (Qwen3ForCausalLM if qwen3 else LlamaForCausalLM)(config)
     finally:
         torch.set_default_dtype(previous)
     return model.eval()
@@ -98,8 +132,7 @@ def synthetic_request(cfg, seed, device):
         k = torch.randn(shape, device=device, generator=gen, dtype=torch.float32).to(torch.bfloat16)
         v = (0.5 * torch.randn(shape, device=device, generator=gen, dtype=torch.float32)).to(torch.bfloat16)
         pairs.append((k, v))
-    width = cfg["rows"] // cfg["intervals"]
-    intervals = make_intervals(seed, a, new_ids.shape[1], cfg["intervals"], width)
+    intervals = budget_intervals(seed, a, new_ids.shape[1], cfg["intervals"], cfg["rows"])
     return old_ids, new_ids, pairs, intervals
 
 
@@ -247,8 +280,7 @@ def _sample_request(cfg, seed, device, layers):
     shape = (1, cfg["kv_heads"], length, cfg["head_dim"])
     base = [(torch.randn(shape, device=device, generator=gen).to(torch.bfloat16),
              (0.5 * torch.randn(shape, device=device, generator=gen)).to(torch.bfloat16)) for _ in range(layers)]
-    width = cfg["rows"] // cfg["intervals"]
-    intervals = make_intervals(seed, cfg["delete_at"], length, cfg["intervals"], width)
+    intervals = budget_intervals(seed, cfg["delete_at"], length, cfg["intervals"], cfg["rows"])
     return ids, base, [p for a, b in intervals for p in range(a, b)]
 
 
@@ -284,7 +316,7 @@ def gpu_comparator(args):
     full depth: the "reference CUDA SDPA path" the north star compares with.
     Same workload as our arm; CUDA events around each call, median."""
     device = torch.device("cuda", 0)
-    cfg = dict(CONFIG)
+    cfg = dict(WORKLOADS[args.workload])
     from oracle.hf_packed import packed_refresh_hf
 
     model = build_model(cfg, 1, device)
@@ -301,7 +333,7 @@ def gpu_comparator(args):
         e.synchronize()
         times.append(b.elapsed_time(e))
     ms = statistics.median(times)
-    print(json.dumps({"impl": "reference-cuda-comparator", "metric": METRIC, "value": len(positions) / (ms / 1e3),
+    print(json.dumps({"impl": "reference-cuda-comparator", "metric": cfg["metric"], "value": len(positions) / (ms / 1e3),
                       "unit": "rows/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
                       "n_gpus": 1, "note": "reference packed SDPA path restated on transformers (oracle/hf_packed.py)"}),
           flush=True)
@@ -312,14 +344,14 @@ def reference_arm(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    cfg = dict(CONFIG)
+    cfg = dict(WORKLOADS[args.workload])
     base = run_cpu_baseline(cfg, sample_layers=2, threads=threads)
-    line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "rows/s", "n_gpus": world,
+    line = {"impl": "reference", "metric": cfg["metric"], "value": base["value"], "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["ms_per_request"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random weights N(0,0.02), ids, stale cache)",
-            "config": {"workload": "config2: Llama-3-8B shape, 8192 ctx, delete 256@1024, 16x4 rows",
-                       "parallelism": f"dp{world} (rank 0 only)", "l2": "weights 14 GB >> L2"},
+            "config": {"workload": cfg["workload"], "parallelism": f"dp{world} (rank 0 only)",
+                       "l2": "weights >= 14 GB >> L2"},
             "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": base["value"], "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -344,8 +376,8 @@ def our_arm(args):
     torch.cuda.set_device(device)
     native_build.build()
     _lib.load()
-    cfg = dict(CONFIG)
-    seed = 1 + rank
+    cfg = dict(WORKLOADS[args.workload])
+    seed = (3 if args.workload == "config3" else 1) + rank
     model = build_model(cfg, seed, device)
     shim = OperatorShim(model)
     old_ids, new_ids, old_pairs, intervals = synthetic_request(cfg, seed, device)
@@ -459,6 +491,9 @@ def our_arm(args):
     totals.update(_time_attention(shifted, intervals, cfg, device))
     kernels = {}
     algo_bytes, params = refresh_bytes(cfg, length)
+    selected = [p for a, b in intervals for p in range(a, b)]
+    step_flops = 2.0 * params * len(selected) * cfg["layers"] + \
+        4.0 * cfg["heads"] * cfg["head_dim"] * sum(p + 1 for p in selected) * cfg["layers"]
     cache_bytes = 2 * cfg["layers"] * cfg["kv_heads"] * length * cfg["head_dim"] * 2
     if "copy_layers" in totals:
         n, ms = totals["copy_layers"]
@@ -480,21 +515,24 @@ def our_arm(args):
     clocks = sampler.summary()
     cpu = run_cpu_baseline(cfg, sample_layers=2, threads=os.cpu_count() or 1) if world == 1 and not args.no_cpu else None
     line = {
-        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+        "metric": cfg["metric"], "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random weights N(0,0.02), ids, stale cache)",
-        "config": {"workload": "config2: Llama-3-8B shape, 8192 ctx, delete 256@1024 (N=7936), 16 intervals x 4 rows",
+        "config": {"workload": cfg["workload"],
                    "rows": rows, "logical_length": length, "intervals": intervals[:4] + ["..."],
-                   "parallelism": f"dp{world}", "l2": "no flush: 14 GB of weights stream per step (>> 126 MB L2)"},
+                   "parallelism": f"dp{world}", "l2": "no flush: >= 14 GB of weights stream per step (>> 126 MB L2)"},
         "refresh_ms": {"median": statistics.median(step_ms), "min": min(step_ms), "max": max(step_ms)},
-        "roofline": {"bound": "hbm", "kernel": "kvr_shift_cache_layers (RoPE fix + shift, 32 layers, 1 launch)",
+        "roofline": {"bound": "hbm",
+                     "kernel": f"kvr_shift_cache_layers (RoPE fix + shift, {cfg['layers']} layers, 1 launch)",
                      "achieved": rope_gbs, "peak": hbm, "unit": "GB/s", "frac": rope_gbs / hbm,
                      "traffic": None, "algorithmic_bytes": fused_bytes, "rope_only_bytes": rope_bytes,
                      "avg_us": rope_t * 1e6, "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"},
-        "step_roofline": {"bound": "hbm", "algorithmic_bytes": algo_bytes,
+        "step_roofline": {"bound": "hbm" if algo_bytes / hbm / 1e6 >= step_flops / tflops / 1e9 else "tensor",
+                          "algorithmic_bytes": algo_bytes, "flops": step_flops,
                           "achieved_gbs": algo_bytes / (ms_per_step / 1e3) / 1e9,
-                          "frac": algo_bytes / (ms_per_step / 1e3) / 1e9 / hbm,
-                          "floor_ms": algo_bytes / hbm / 1e6},
+                          "achieved_tflops": step_flops / (ms_per_step / 1e3) / 1e12,
+                          "floor_ms": max(algo_bytes / hbm / 1e6, step_flops / tflops / 1e9),
+                          "frac": max(algo_bytes / hbm / 1e6, step_flops / tflops / 1e9) / ms_per_step},
         "kernels": kernels,
         "e2e": {"value": e2e_value, "unit": "rows/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": int(host_ids.numel() * 8),
@@ -631,8 +669,9 @@ def main():
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     parser.add_argument("--device", choices=["cpu", "cuda"], default="cpu",
                         help="with --impl reference: cpu (the reference arm) or cuda (the GPU comparator)")
-    parser.add_argument("--workload", choices=["config2", "70b-tp"], default="config2",
-                        help="config2: Llama-3-8B refresh (DP replicas when N>1); 70b-tp: configs[4], head-sharded")
+    parser.add_argument("--workload", choices=["config2", "config3", "70b-tp"], default="config2",
+                        help="config2: Llama-3-8B refresh, 64 rows (DP replicas when N>1); config3: Qwen3-8B, 32k "
+                             "context, 1383 rows (DP replicas); 70b-tp: configs[4], head-sharded")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")

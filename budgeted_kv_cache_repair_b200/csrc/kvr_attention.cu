@@ -8,20 +8,23 @@
 // repeat_kv). Rows are sorted by absolute position; a tile's causal span is
 // [0, pos(last row)].
 //
-// One CTA per SM, 10 warps:
+// One CTA per SM, 11 warps:
 //   warp 8  TMA producer: K and V blocks of 128 keys, 128B-swizzled, into
 //           rings of NS stages with separate K and V barriers, so a K stage is
 //           refilled as soon as its Q.K^T is done (bounded waits, no multicast)
-//   warp 9  MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S
-//           buffers, then O += P_j V_j into the TMEM O accumulators
+//   warp 10 Q.K^T issuer (one thread): S_j = Q K_j^T into TMEM S buffer j & 1
+//   warp 9  P.V issuer (one thread): O += P_j V_j into the TMEM O accumulators,
+//           with P_j read from tensor memory; it also owns the TMEM allocation.
+//           Two issuing threads, because tcgen05.mma issue blocks while the
+//           tensor pipe is busy: S_{j+2} must not queue behind P.V of block j+1.
 //   warps 0-7  softmax: two threads per m-entry row (TMEM lane = row), each
 //           owning 64 keys of every block with its own running max, sum and
 //           TMEM O accumulator. A thread loads its S half-row, applies the
-//           causal/chunk mask, keeps a running max, writes P = 2^(s - m) to
-//           shared memory as the A operand of the PV MMA, and rescales its O
-//           half in TMEM only when the max grew by more than 2^8 (exact: the
-//           final normalisation uses the same stale max). The two halves merge
-//           once, in the epilogue.
+//           causal/chunk mask, keeps a running max, writes P = 2^(s - m) over
+//           its own S columns in tensor memory (the A operand of P.V), and
+//           rescales its O half in TMEM only when the max grew by more than 2^8
+//           (exact: the final normalisation uses the same stale max). The two
+//           halves merge once, in the epilogue.
 // QK^T of block j+1 overlaps the softmax of block j.
 //
 // Precision: QK^T and PV run on bf16/fp16 operands with fp32 accumulation.
@@ -50,8 +53,9 @@ constexpr int BM = 128;  // m-entries per CTA (MMA M, TMEM lanes)
 constexpr int BN = 128;  // keys per block (MMA N of QK^T, K of PV)
 constexpr int kSoftmaxThreads = 256;  // warps 0-7: two threads per m-entry row
 constexpr int kTmaWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int THREADS = 320;
+constexpr int kMmaWarp = 9;   // P.V issuer; also allocates and frees tensor memory
+constexpr int kQkWarp = 10;   // Q.K^T issuer
+constexpr int THREADS = 352;
 constexpr int SUB = BM * 128;  // one [128 rows x 128 B] swizzled sub-tile
 constexpr int STATUS_BYTES = 256;
 constexpr int kEpilogueBar = 1;        // named barrier of the softmax warps (0 is __syncthreads)
@@ -87,8 +91,8 @@ struct Layout {
   static constexpr int NP = 2;  // P buffers = the two S buffers
   static constexpr int BAR_OFF = V_OFF + NS * DS * SUB;
   // q_full, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS], s_full[2], s_free[2], p_full[NP],
-  // pv_done[NP], drain, red_bar
-  static constexpr int NBAR = 1 + 4 * NS + 4 + 2 * NP + 1 + 1;
+  // pv_done[NP], drain, red_bar, drain_qk
+  static constexpr int NBAR = 1 + 4 * NS + 4 + 2 * NP + 1 + 1 + 1;
   static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;
   static constexpr int RED_OFF = MISC_OFF + 16;  // float [2 halves][128 rows][max, sum]
   static constexpr int USED = RED_OFF + 2 * BM * 2 * 4;
@@ -222,6 +226,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto pv_done = [&](int pb) { return bar0 + 8u * (5 + 4 * NS + NP + pb); };
   const uint32_t drain = bar0 + 8u * (5 + 4 * NS + 2 * NP);
   const uint32_t red_bar = bar0 + 8u * (6 + 4 * NS + 2 * NP);
+  const uint32_t drain_qk = bar0 + 8u * (7 + 4 * NS + 2 * NP);
   volatile int* abort = reinterpret_cast<volatile int*>(gbase + L::MISC_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L::MISC_OFF + 4);
   float* red = reinterpret_cast<float*>(gbase + L::RED_OFF);  // [2 halves][128 rows][max, sum]
@@ -245,6 +250,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       sm100::mbar_init(pv_done(pb), 1);
     }
     sm100::mbar_init(drain, 1);
+    sm100::mbar_init(drain_qk, 1);
     sm100::mbar_init(red_bar, kSoftmaxThreads);
     sm100::fence_barrier_init();
   }
@@ -320,17 +326,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           sm100::mbar_wait(v_full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kQkWarp) {
     if (lane == 0) {
-      // ---------------- MMA issuer ----------------
+      // ---------------- Q.K^T issuer ----------------
+      // Its own thread, so that S of block j+2 is issued the moment P.V of
+      // block j has freed the buffer, never behind a P.V issue (tcgen05.mma
+      // issue blocks while the tensor pipe is busy).
       constexpr uint32_t IQK = sm100::idesc_f16(kBF16, BM, BN, false);
-      constexpr uint32_t IPV = sm100::idesc_f16(kBF16, BM, D, true);
       bool ok = sm100::mbar_wait(q_full, 0, abort, err, ERR_Q_FULL, WAIT_LIMIT);
-      auto issue_qk = [&](int j) -> bool {
+      for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % NS, b = j & 1;
-        if (!sm100::mbar_wait(k_full(s), (j / NS) & 1, abort, err, ERR_KV_FULL, WAIT_LIMIT)) return false;
-        if (j >= 2 && !sm100::mbar_wait(s_free(b), ((j >> 1) - 1) & 1, abort, err, ERR_S_FREE, WAIT_LIMIT))
-          return false;
+        if (!sm100::mbar_wait(k_full(s), (j / NS) & 1, abort, err, ERR_KV_FULL, WAIT_LIMIT)) break;
+        if (j >= 2 && !sm100::mbar_wait(s_free(b), ((j >> 1) - 1) & 1, abort, err, ERR_S_FREE, WAIT_LIMIT)) break;
         sm100::tc_fence_after();
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
@@ -341,11 +348,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         sm100::mma_commit(s_full(b));
         sm100::mma_commit(k_empty(s));  // K block free once Q.K^T is done
-        return true;
-      };
-      if (ok) ok = issue_qk(0);
-      for (int j = 0; ok && j < nblk; ++j) {
-        if (j + 1 < nblk && !issue_qk(j + 1)) break;
+      }
+      // Nothing of ours may still be writing TMEM when it is freed.
+      sm100::mma_commit(drain_qk);
+      volatile int keep_waiting = 0;
+      sm100::mbar_wait(drain_qk, 0, &keep_waiting, err, ERR_DRAIN, WAIT_LIMIT);
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      // ---------------- P.V issuer ----------------
+      constexpr uint32_t IPV = sm100::idesc_f16(kBF16, BM, D, true);
+      for (int j = 0; j < nblk; ++j) {
         const int pb = j & 1;  // P of block j sits in S buffer j & 1
         if (!sm100::mbar_wait(p_full(pb), (j >> 1) & 1, abort, err, ERR_P_FULL, WAIT_LIMIT)) break;
         if (!sm100::mbar_wait(v_full(j % NS), (j / NS) & 1, abort, err, ERR_KV_FULL, WAIT_LIMIT)) break;
