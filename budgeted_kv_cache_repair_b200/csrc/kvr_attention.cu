@@ -195,9 +195,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = blockIdx.y;
-  const int tile = blockIdx.x % a.tiles;  // tiles of one chunk launch together (shared K/V in L2)
-  const int chunk = blockIdx.x / a.tiles;
+  // Launch order (1-D grid): key chunk, then KV head, then tiles from the last
+  // (latest positions, longest causal span) down, so that the block scheduler
+  // starts the longest work first and the tiles sharing a K/V chunk run
+  // together (the chunk stays in L2).
+  const int tile = a.tiles - 1 - static_cast<int>(blockIdx.x % a.tiles);
+  const int h = static_cast<int>((blockIdx.x / a.tiles) % a.hkv);
+  const int chunk = static_cast<int>(blockIdx.x / a.tiles / a.hkv);
   const int G = a.group;
   const int64_t total_m = a.rows * G;
   const int64_t m0 = static_cast<int64_t>(tile) * BM;
@@ -796,7 +800,7 @@ int launch(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, 
       return KVR_ERR_CUDA;
     }
   }
-  dim3 grid(a.tiles * a.nchunks, a.hkv);
+  dim3 grid(static_cast<unsigned>(a.tiles) * a.nchunks * a.hkv);
   int st = launch_pdl<attn_tc_kernel<T, D, SPLIT>>(grid, dim3(THREADS), smem, s, 1, mk, mv, mq, a);
   if (st != KVR_OK || a.nchunks == 1) return st;
   const int64_t total_m = a.rows * a.group;
@@ -851,7 +855,7 @@ int selected_attention(const void* q, const void* k_cache, const void* v_cache, 
   if (max_position < 0 || max_position >= cache_rows || !(scale == scale)) return KVR_ERR_INVALID_ARG;
   if (cache_rows > 0x7fffffffLL || kv_heads > 65535) return KVR_ERR_UNSUPPORTED;
   attn::Plan p = attn::make_plan(rows, q_heads, kv_heads, max_position);
-  if (static_cast<int64_t>(p.tiles) * p.nchunks > 0x7fffffff) return KVR_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(p.tiles) * p.nchunks * kv_heads > 0x7fffffff) return KVR_ERR_UNSUPPORTED;
   const size_t need = attn::workspace_bytes(p.tiles, p.nchunks, kv_heads, head_dim);
   if (!workspace || workspace_bytes < need || !aligned16(workspace)) return KVR_ERR_INVALID_ARG;
   const bool bf16 = dtype == KVR_DTYPE_BF16;

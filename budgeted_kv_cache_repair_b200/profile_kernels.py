@@ -2,6 +2,7 @@
 
     python -m budgeted_kv_cache_repair_b200.profile_kernels shift     [--reps N] [--layers L]
     python -m budgeted_kv_cache_repair_b200.profile_kernels attention [--reps N] [--precision rounded|split]
+                                                                      [--geometry config2|config3]
     python -m budgeted_kv_cache_repair_b200.profile_kernels copy      [--reps N] [--tensors T]
     python -m budgeted_kv_cache_repair_b200.profile_kernels linear    [--reps N] [--only NAME]
 
@@ -11,7 +12,9 @@ rows in 16 intervals of 4 (`linear`: the per-layer projections of that model
 at 64 rows, each timed beside torch's cuBLAS GEMMs for the same products, with
 enough weight copies in rotation that no launch finds its weights in L2, and
 replayed from a CUDA graph so that host launch cost is not measured).
-Inputs are seeded random tensors. After two
+`attention --geometry config3`: one layer of the Qwen3-8B shape at 32k context
+(31744 cached rows, 1383 rows in 32 intervals from 4096). Inputs are seeded
+random tensors. After two
 warm-up launches the command times `--reps` launches with CUDA events and
 prints the average (`attention` and `linear`: replayed from a CUDA graph,
 after a capture pass and one replay); under ncu, capture with `-s 2`
@@ -34,6 +37,17 @@ def _positions():
     slots = (NEW - DELETE_AT) // 5
     starts = sorted(DELETE_AT + s * 5 for s in torch.randperm(slots, generator=gen)[:16].tolist())
     return sorted(p + i for p in starts for i in range(4))
+
+
+NEW3, DELETE_AT3, ROWS3, INTERVALS3 = 31744, 4096, 1383, 32
+
+
+def _positions3():
+    """1383 rows in 32 non-adjacent intervals (widths 43 and 44) from 4096."""
+    width, extra = divmod(ROWS3, INTERVALS3)
+    gen = torch.Generator().manual_seed(3)
+    picks = sorted(torch.randperm((NEW3 - DELETE_AT3) // (width + 2), generator=gen)[:INTERVALS3].tolist())
+    return [DELETE_AT3 + s * (width + 2) + i for n, s in enumerate(picks) for i in range(width + (n < extra))]
 
 
 def _time(fn, reps: int) -> float:
@@ -84,26 +98,26 @@ def copy(reps: int, tensors: int = 2 * LAYERS) -> None:
     print(f"kvr_copy_layers: {us:.1f} us/launch, {algo / us / 1e3:.0f} GB/s on {algo} algorithmic bytes")
 
 
-def attention(reps: int, precision: str) -> None:
+def attention(reps: int, precision: str, geometry: str = "config2") -> None:
     lib = _lib.load()
-    positions = _positions()
+    positions, new = (_positions3(), NEW3) if geometry == "config3" else (_positions(), NEW)
     rows = len(positions)
     pos = torch.tensor(positions, device="cuda")
     q = (torch.randn(rows, HEADS, D, device="cuda") * 0.5).bfloat16()
-    k = torch.randn(1, KV_HEADS, NEW, D, device="cuda").bfloat16()
-    v = torch.randn(1, KV_HEADS, NEW, D, device="cuda").bfloat16()
+    k = torch.randn(1, KV_HEADS, new, D, device="cuda").bfloat16()
+    v = torch.randn(1, KV_HEADS, new, D, device="cuda").bfloat16()
     out = torch.empty_like(q)
-    need = lib.kvr_attention_workspace_size(rows, HEADS, KV_HEADS, D, NEW)
+    need = lib.kvr_attention_workspace_size(rows, HEADS, KV_HEADS, D, new)
     ws = torch.empty(need, dtype=torch.uint8, device="cuda")
     mode = _lib.ATTN_P_SPLIT if precision == "split" else _lib.ATTN_P_ROUNDED
-    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), pos.data_ptr(), rows, HEADS, KV_HEADS, D, NEW,
-            NEW * D, D, positions[-1], D ** -0.5, mode, ws.data_ptr(), need, _lib.DTYPE_BF16)
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), pos.data_ptr(), rows, HEADS, KV_HEADS, D, new,
+            new * D, D, positions[-1], D ** -0.5, mode, ws.data_ptr(), need, _lib.DTYPE_BF16)
     # Device time per call from a CUDA graph of back-to-back calls: a call's
     # host work (tensor maps, two launches) is longer than its kernels.
     us = _graph_time(lambda i: _lib.check(lib.kvr_selected_attention(*args, _lib.stream_handle()), "attention"), reps)
     kv = 2 * KV_HEADS * (positions[-1] + 1) * D * 2
     flops = 4.0 * HEADS * D * sum(p + 1 for p in positions)
-    print(f"kvr_selected_attention ({precision}): {us:.1f} us/call, {kv / us / 1e3:.0f} GB/s of K/V, "
+    print(f"kvr_selected_attention ({precision}, {geometry}): {us:.1f} us/call, {kv / us / 1e3:.0f} GB/s of K/V, "
           f"{flops / us / 1e6:.1f} TFLOP/s; status {int(ws[:4].view(torch.int32).item())}")
 
 
@@ -186,6 +200,7 @@ def main() -> None:
     parser.add_argument("--layers", type=int, default=LAYERS, help="shift: layers (fewer for a small capture)")
     parser.add_argument("--tensors", type=int, default=2 * LAYERS, help="copy: K/V tensors per launch (2 to 64)")
     parser.add_argument("--precision", choices=["rounded", "split"], default="rounded")
+    parser.add_argument("--geometry", choices=["config2", "config3"], default="config2", help="attention geometry")
     args = parser.parse_args()
     build.build()
     if args.kernel == "shift":
@@ -195,7 +210,7 @@ def main() -> None:
     elif args.kernel == "linear":
         linear(args.reps, args.only)
     else:
-        attention(args.reps, args.precision)
+        attention(args.reps, args.precision, args.geometry)
 
 
 if __name__ == "__main__":
