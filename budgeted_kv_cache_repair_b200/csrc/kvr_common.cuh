@@ -28,11 +28,13 @@ int selected_attention(const void* q, const void* k_cache, const void* v_cache, 
 
 // kvr_add_rmsnorm whose delta may instead be a deferred projection: nparts
 // fp32 slices (row stride part_stride, slice stride part_slice floats),
-// summed in order and rounded before the residual add.
+// summed in order and rounded before the residual add. weight_early: the norm
+// weight is not written by any kernel of the programmatic launch chain, so it
+// is loaded before the wait on the previous kernel.
 int add_rmsnorm_ex(void* hidden, const void* delta, const float* parts, int nparts, int64_t part_stride,
                    int64_t part_slice, const void* weight, void* out, int64_t rows, int hidden_size,
                    int64_t hidden_stride, int64_t delta_stride, int64_t out_stride, float eps, int dtype,
-                   void* stream);
+                   void* stream, bool weight_early);
 
 // Deferred q/k/v projection for qkv_rope_scatter_ex: `count` fp32 slices of
 // [rows][row_stride] (slice stride `slice` floats), q/k/v at columns
@@ -44,13 +46,15 @@ struct QkvParts {
 };
 
 // kvr_qkv_rope_scatter reading q/k/v from `parts` when given (q_in/k_in/v_in
-// are then unused).
+// are then unused). consts_early: positions, cos/sin and norm weights are
+// written by no kernel of the programmatic launch chain, so they are loaded
+// before the wait on the previous kernel.
 int qkv_rope_scatter_ex(const void* q_in, const void* k_in, const void* v_in, int64_t q_row_stride,
                         int64_t k_row_stride, int64_t v_row_stride, const void* q_norm_w, const void* k_norm_w,
                         float eps, const void* cos_tab, const void* sin_tab, const int64_t* positions,
                         int64_t rows, int q_heads, int kv_heads, int head_dim, void* q_out, void* k_cache,
                         void* v_cache, int64_t cache_rows, int64_t cache_head_stride, int64_t cache_row_stride,
-                        int* error_count, int dtype, void* stream, const QkvParts* parts);
+                        int* error_count, int dtype, void* stream, const QkvParts* parts, bool consts_early);
 
 // Call right after each kernel launch.
 inline int check_launch() {

@@ -393,10 +393,10 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
     const bool final = l == m.num_layers - 1;
     if (defer && l)
       KVR_TRY(add_rmsnorm_ex(hidden, nullptr, parts, down_split, H, rows * H, w.input_norm, normed, rows, H, H, H,
-                             H, m.eps, m.dtype, stream));
+                             H, m.eps, m.dtype, stream, true));
     else
-      KVR_TRY(kvr_add_rmsnorm(hidden, l ? delta : nullptr, w.input_norm, normed, rows, H, H, H, H, m.eps, m.dtype,
-                              stream));
+      KVR_TRY(add_rmsnorm_ex(hidden, l ? delta : nullptr, nullptr, 0, 0, 0, w.input_norm, normed, rows, H, H, H, H,
+                             m.eps, m.dtype, stream, true));
     QkvParts qkv_parts{};
     if (lin) {
       // q/k/v from separate weights or from row ranges of the stacked matrix.
@@ -428,7 +428,7 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
                                 m.eps, r.cos_tab, r.sin_tab, r.positions, rows, m.q_heads, m.kv_heads, D,
                                 final ? nullptr : q_rot, r.k_cache[l], r.v_cache[l], r.cache_rows,
                                 r.cache_head_stride, r.cache_row_stride, nullptr, m.dtype, stream,
-                                defer ? &qkv_parts : nullptr));
+                                defer ? &qkv_parts : nullptr, true));
     if (final) break;
     KVR_TRY(selected_attention(q_rot, r.k_cache[l], r.v_cache[l], attn, r.positions, rows, m.q_heads, m.kv_heads,
                                D, r.cache_rows, r.cache_head_stride, r.cache_row_stride, r.max_position, scale,
@@ -449,9 +449,10 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
     if (r.tp_comm) KVR_TRY(allreduce(delta, rows * H, m.dtype, r.tp_comm, s));
     if (defer)
       KVR_TRY(add_rmsnorm_ex(hidden, nullptr, parts, o_split, H, rows * H, w.post_norm, normed, rows, H, H, H, H,
-                             m.eps, m.dtype, stream));
+                             m.eps, m.dtype, stream, true));
     else
-      KVR_TRY(kvr_add_rmsnorm(hidden, delta, w.post_norm, normed, rows, H, H, H, H, m.eps, m.dtype, stream));
+      KVR_TRY(add_rmsnorm_ex(hidden, delta, nullptr, 0, 0, 0, w.post_norm, normed, rows, H, H, H, H, m.eps, m.dtype,
+                             stream, true));
     if (lin) {
       const kvr_linear_segment mlp = {w.gate, w.up, I, act, I};
       const kvr_linear_segment down = {w.down, nullptr, H, delta, H};

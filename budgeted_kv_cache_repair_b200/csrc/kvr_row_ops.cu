@@ -47,24 +47,52 @@ template <class T>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
     uint16_t* hidden, const uint16_t* __restrict__ delta, const uint16_t* __restrict__ weight,
     uint16_t* out, int vpr, int64_t h_stride, int64_t d_stride, int64_t o_stride, float inv_h,
-    float eps, const float* __restrict__ parts, int nparts, int64_t p_stride, int64_t p_slice) {
+    float eps, const float* __restrict__ parts, int nparts, int64_t p_stride, int64_t p_slice, int weight_early) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
-  pdl_wait();  // every input may come from the previous kernel
+  // With weight_early (the layer loop: the norm weight is a model constant)
+  // the weight is fetched before the wait, so its load overlaps the previous
+  // kernel instead of following the reduction.
+  Vec8 w[kNormMaxVecs];
+  if (weight_early) {
+#pragma unroll
+    for (int k = 0; k < kNormMaxVecs; ++k) {
+      const int v = threadIdx.x + k * kNormThreads;
+      if (v < vpr) w[k] = ld_vec8(weight + v * 8);
+    }
+  }
+  pdl_wait();  // every other input may come from the previous kernel
+  if (!weight_early) {
+#pragma unroll
+    for (int k = 0; k < kNormMaxVecs; ++k) {
+      const int v = threadIdx.x + k * kNormThreads;
+      if (v < vpr) w[k] = ld_vec8(weight + v * 8);
+    }
+  }
   const int64_t r = blockIdx.x;
   uint16_t* hrow = hidden + r * h_stride;
-  Vec8 x[kNormMaxVecs];
-  float ss = 0.f;
+  // Every load of the row (hidden, then the delta or its partial slices) is
+  // issued before the first store back to `hidden`: one memory round trip.
+  Vec8 x[kNormMaxVecs], dv[kNormMaxVecs];
 #pragma unroll
   for (int k = 0; k < kNormMaxVecs; ++k) {
     const int v = threadIdx.x + k * kNormThreads;
     if (v < vpr) {
       x[k] = ld_vec8(hrow + v * 8);
+      if (nparts)
+        dv[k] = sum_parts8<T>(parts + r * p_stride + v * 8, nparts, p_slice);
+      else if (delta)
+        dv[k] = ld_vec8(delta + r * d_stride + v * 8);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormMaxVecs; ++k) {
+    const int v = threadIdx.x + k * kNormThreads;
+    if (v < vpr) {
       if (delta || nparts) {
         // residual + hidden_states, rounded to the element type.
-        Vec8 dv = nparts ? sum_parts8<T>(parts + r * p_stride + v * 8, nparts, p_slice)
-                         : ld_vec8(delta + r * d_stride + v * 8);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[k].h[e] = T::from_f(__fadd_rn(T::to_f(x[k].h[e]), T::to_f(dv.h[e])));
+        for (int e = 0; e < 8; ++e) x[k].h[e] = T::from_f(__fadd_rn(T::to_f(x[k].h[e]), T::to_f(dv[k].h[e])));
         st_vec8(hrow + v * 8, x[k]);
       }
 #pragma unroll
@@ -92,12 +120,11 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   for (int k = 0; k < kNormMaxVecs; ++k) {
     const int v = threadIdx.x + k * kNormThreads;
     if (v < vpr) {
-      Vec8 w = ld_vec8(weight + v * 8);
       Vec8 y;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const float normed = rnd<T>(__fmul_rn(T::to_f(x[k].h[e]), inv));
-        y.h[e] = T::from_f(__fmul_rn(T::to_f(w.h[e]), normed));
+        y.h[e] = T::from_f(__fmul_rn(T::to_f(w[k].h[e]), normed));
       }
       st_vec8(out + r * o_stride + v * 8, y);
     }
@@ -131,24 +158,45 @@ struct QkvArgs {
   const float* parts;
   int nparts;
   int64_t p_rs, p_slice, q_col, k_col, v_col;
+  // Positions, cos/sin tables and norm weights are written by no kernel of the
+  // programmatic launch chain (the layer loop): load them before the wait.
+  int consts_early;
 };
 
 template <class T, int D>
 __global__ void __launch_bounds__(256) qkv_rope_scatter_kernel(QkvArgs a) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
-  pdl_wait();  // every input may come from the previous kernel
   constexpr int E = D / 32;  // 4 for D=128, 2 for D=64
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int qh = a.q_out ? a.q_heads : 0;
   const int slots = qh + 2 * a.kv_heads;
   const int64_t r = warp / slots;
-  if (r >= a.rows) return;
+  if (r >= a.rows) {
+    pdl_wait();
+    return;
+  }
   const int slot = static_cast<int>(warp - r * slots);
-  const int64_t p = a.positions[r];
   const bool is_q = slot < qh;
   const bool is_v = slot >= qh + a.kv_heads;
   const int head = is_q ? slot : (is_v ? slot - qh - a.kv_heads : slot - qh);
+  const uint16_t* nw = is_q ? a.q_norm : a.k_norm;
+  // Row constants: position, cos/sin of this lane's elements, norm weights.
+  int64_t p = 0;
+  uint16_t cb[E], sb[E], wb[E];
+  auto load_consts = [&]() {
+    p = a.positions[r];
+    if (is_v) return;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      cb[e] = a.cos_tab[r * D + lane * E + e];
+      sb[e] = a.sin_tab[r * D + lane * E + e];
+      wb[e] = nw ? nw[lane * E + e] : 0;
+    }
+  };
+  if (a.consts_early) load_consts();
+  pdl_wait();  // q/k/v (or their partial slices) come from the previous kernel
+  if (!a.consts_early) load_consts();
   if (!is_q && (p < 0 || p >= a.cache_rows)) {
     if (lane == 0 && head == 0 && !is_v && a.error_count) atomicAdd(a.error_count, 1);
     return;
@@ -201,7 +249,6 @@ __global__ void __launch_bounds__(256) qkv_rope_scatter_kernel(QkvArgs a) {
   float x[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) x[e] = T::to_f(xb[e]);
-  const uint16_t* nw = is_q ? a.q_norm : a.k_norm;
   if (nw) {  // Qwen3 per-head RMSNorm over head_dim
     float ss = 0.f;
 #pragma unroll
@@ -212,19 +259,17 @@ __global__ void __launch_bounds__(256) qkv_rope_scatter_kernel(QkvArgs a) {
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       const float normed = rnd<T>(__fmul_rn(x[e], inv));
-      x[e] = rnd<T>(__fmul_rn(T::to_f(nw[lane * E + e]), normed));
+      x[e] = rnd<T>(__fmul_rn(T::to_f(wb[e]), normed));
     }
   }
   // RoPE at the row's absolute position: out = x*cos + rotate_half(x)*sin.
-  const uint16_t* ct = a.cos_tab + r * D + lane * E;
-  const uint16_t* st = a.sin_tab + r * D + lane * E;
   const bool low = lane < 16;
   uint16_t ob[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) {
     const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
     const float rot = low ? -partner : partner;
-    ob[e] = rope_elem<T>(x[e], rot, T::to_f(ct[e]), T::to_f(st[e]));
+    ob[e] = rope_elem<T>(x[e], rot, T::to_f(cb[e]), T::to_f(sb[e]));
   }
   if constexpr (E == 4) *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(ob);
   else *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(ob);
@@ -261,7 +306,7 @@ int kvr_add_rmsnorm(void* hidden, const void* delta, const void* weight, void* o
                     int hidden_size, int64_t hidden_stride, int64_t delta_stride,
                     int64_t out_stride, float eps, int dtype, void* stream) {
   return kvr::add_rmsnorm_ex(hidden, delta, nullptr, 0, 0, 0, weight, out, rows, hidden_size, hidden_stride,
-                             delta_stride, out_stride, eps, dtype, stream);
+                             delta_stride, out_stride, eps, dtype, stream, false);
 }
 
 }  // extern "C"
@@ -271,7 +316,7 @@ namespace kvr {
 int add_rmsnorm_ex(void* hidden, const void* delta, const float* parts, int nparts, int64_t part_stride,
                    int64_t part_slice, const void* weight, void* out, int64_t rows, int hidden_size,
                    int64_t hidden_stride, int64_t delta_stride, int64_t out_stride, float eps, int dtype,
-                   void* stream) {
+                   void* stream, bool weight_early) {
   if (dtype != KVR_DTYPE_BF16 && dtype != KVR_DTYPE_F16) return KVR_ERR_UNSUPPORTED;
   if (rows < 0 || hidden_size <= 0 || hidden_size % 8) return KVR_ERR_INVALID_ARG;
   if (hidden_size > kNormThreads * kNormMaxVecs * 8) return KVR_ERR_UNSUPPORTED;
@@ -291,12 +336,12 @@ int add_rmsnorm_ex(void* hidden, const void* delta, const float* parts, int npar
     st = launch_pdl<add_rmsnorm_kernel<BF16>>(static_cast<unsigned>(rows), dim3(kNormThreads), 0, s, 1, 
         static_cast<uint16_t*>(hidden), static_cast<const uint16_t*>(delta),
         static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), vpr, hidden_stride,
-        delta_stride, out_stride, inv_h, eps, parts, nparts, part_stride, part_slice);
+        delta_stride, out_stride, inv_h, eps, parts, nparts, part_stride, part_slice, weight_early ? 1 : 0);
   else
     st = launch_pdl<add_rmsnorm_kernel<F16>>(static_cast<unsigned>(rows), dim3(kNormThreads), 0, s, 1, 
         static_cast<uint16_t*>(hidden), static_cast<const uint16_t*>(delta),
         static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), vpr, hidden_stride,
-        delta_stride, out_stride, inv_h, eps, parts, nparts, part_stride, part_slice);
+        delta_stride, out_stride, inv_h, eps, parts, nparts, part_stride, part_slice, weight_early ? 1 : 0);
   return st;
 }
 
@@ -314,7 +359,7 @@ int kvr_qkv_rope_scatter(const void* q_in, const void* k_in, const void* v_in,
   return kvr::qkv_rope_scatter_ex(q_in, k_in, v_in, q_row_stride, k_row_stride, v_row_stride, q_norm_w, k_norm_w,
                                   eps, cos_tab, sin_tab, positions, rows, q_heads, kv_heads, head_dim, q_out,
                                   k_cache, v_cache, cache_rows, cache_head_stride, cache_row_stride, error_count,
-                                  dtype, stream, nullptr);
+                                  dtype, stream, nullptr, false);
 }
 
 }  // extern "C"
@@ -326,7 +371,7 @@ int qkv_rope_scatter_ex(const void* q_in, const void* k_in, const void* v_in, in
                         float eps, const void* cos_tab, const void* sin_tab, const int64_t* positions,
                         int64_t rows, int q_heads, int kv_heads, int head_dim, void* q_out, void* k_cache,
                         void* v_cache, int64_t cache_rows, int64_t cache_head_stride, int64_t cache_row_stride,
-                        int* error_count, int dtype, void* stream, const QkvParts* parts) {
+                        int* error_count, int dtype, void* stream, const QkvParts* parts, bool consts_early) {
   if (dtype != KVR_DTYPE_BF16 && dtype != KVR_DTYPE_F16) return KVR_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return KVR_ERR_UNSUPPORTED;
   if (rows < 0 || q_heads <= 0 || kv_heads <= 0 || cache_rows < 0) return KVR_ERR_INVALID_ARG;
@@ -374,6 +419,7 @@ int qkv_rope_scatter_ex(const void* q_in, const void* k_in, const void* v_in, in
   a.q_col = parts ? parts->q_col : 0;
   a.k_col = parts ? parts->k_col : 0;
   a.v_col = parts ? parts->v_col : 0;
+  a.consts_early = consts_early ? 1 : 0;
   const int slots = (q_out ? q_heads : 0) + 2 * kv_heads;
   const int64_t warps = rows * slots;
   const int64_t blocks = (warps + 7) / 8;

@@ -66,6 +66,35 @@ def test_native_argument_checks_run_without_a_gpu(built):
     assert lib.kvr_attention_workspace_size(20000, 32, 8, 128, 7936) == 256  # enough tiles: status word only
 
 
+def test_refresh_request_source_cache_checks_run_without_a_gpu(built):
+    """The ownership-copy fields of the refresh request: K and V sources come
+    together, one per layer, or the call fails before any launch."""
+    from budgeted_kv_cache_repair_b200 import _lib
+
+    lib = _lib.load()
+    fake = 1 << 20  # never dereferenced: every case fails host-side validation
+    layers = (_lib.LayerWeights * 2)(*[_lib.LayerWeights(input_norm=fake, qkv=fake, o=fake, post_norm=fake,
+                                                        gate=fake, up=fake, down=fake) for _ in range(2)])
+    model = _lib.Model(num_layers=2, hidden=64, q_heads=4, kv_heads=2, head_dim=64, intermediate=128, vocab=256,
+                       eps=1e-5, dtype=_lib.DTYPE_BF16, embed=fake, layers=layers)
+    ptrs = _lib.ptr_array([fake, fake])
+
+    def request(**kw):
+        base = dict(k_cache=ptrs, v_cache=ptrs, cache_rows=16, cache_head_stride=16 * 64, cache_row_stride=64,
+                    rows=0, projections=_lib.PROJ_CUBLAS)
+        base.update(kw)
+        return _lib.RefreshRequest(**base)
+
+    def call(req):
+        return lib.kvr_packed_refresh(ctypes.byref(model), ctypes.byref(req), None, 0, None)
+
+    assert call(request()) == _lib.OK  # no rows and no sources: nothing to do
+    assert call(request(k_src=ptrs)) == _lib.ERR_INVALID_ARG  # V sources missing
+    assert call(request(v_src=ptrs)) == _lib.ERR_INVALID_ARG  # K sources missing
+    holes = _lib.ptr_array([fake, 0])
+    assert call(request(k_src=ptrs, v_src=holes)) == _lib.ERR_INVALID_ARG  # a layer without a source
+
+
 def test_alignment_matches_reference():
     from budgeted_kv_cache_repair_b200 import token_alignment
 
