@@ -3,9 +3,9 @@
 ``repair_after_deletion`` keeps the reference's signature, validation, budget
 rule and result type; positional correction and the packed refresh run on the
 B200 kernels. Support selection (semantic units + frozen-embedding relevance,
-semantic_units.py / scoring.py) is outside this engine: ``select_support``
-delegates to the reference's own allocator when ``kv_cache_repair`` is
-importable, and callers may pass any ``selector`` with the same signature.
+semantic_units.py / scoring.py) is ``selection.sur_selector``: host-side units
+and allocation, relevance scores from one CUDA kernel; callers may pass any
+``selector`` with the same signature instead.
 
 When the API owns the shifted cache (it does: the caller never sees it), the
 packed refresh writes into that cache in place instead of cloning it, which
@@ -23,6 +23,7 @@ import torch
 
 from .cache import OperatorShim, build_halo_cache
 from .packed import make_receipt, refresh_owned_layers
+from .selection import sur_selector
 from .validate import cache_layers
 
 
@@ -82,14 +83,6 @@ def budget_tokens(suffix_tokens: int, budget_percent: float) -> int:
     return min(suffix_tokens, math.ceil(suffix_tokens * budget_percent / 100.0))
 
 
-def _reference_selector():
-    try:
-        from kv_cache_repair.api import _select_encoded  # the reference's allocator
-    except ImportError:
-        return None
-    return _select_encoded
-
-
 def _select_encoded(model, tokenizer, text, query, ids, suffix_start, budget_percent,
                     selector: Callable | None = None) -> Selection:
     if isinstance(suffix_start, bool) or not isinstance(suffix_start, int):
@@ -107,11 +100,7 @@ def _select_encoded(model, tokenizer, text, query, ids, suffix_start, budget_per
         positions = list(range(suffix_start, length))
         metadata["selection"] = "full_suffix"
     else:
-        chosen = selector or _reference_selector()
-        if chosen is None:
-            raise RuntimeError(
-                "partial-budget selection needs an allocator: install the reference package "
-                "(kv_cache_repair) for SUR selection or pass selector=")
+        chosen = selector or sur_selector
         picked = chosen(model, tokenizer, text, query, ids, suffix_start, budget_percent)
         positions = list(picked.positions if hasattr(picked, "positions") else picked)
         metadata.update(dict(getattr(picked, "metadata", {}) or {}))

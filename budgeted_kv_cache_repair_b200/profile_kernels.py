@@ -5,6 +5,7 @@
                                                                       [--geometry config2|config3]
     python -m budgeted_kv_cache_repair_b200.profile_kernels copy      [--reps N] [--tensors T]
     python -m budgeted_kv_cache_repair_b200.profile_kernels linear    [--reps N] [--only NAME]
+    python -m budgeted_kv_cache_repair_b200.profile_kernels relevance [--reps N]
 
 Geometry: Llama-3-8B shape (32 layers, 8 KV heads, head_dim 128, bf16),
 8192-token context with 256 tokens deleted at 1024 (7936 rows), 64 selected
@@ -12,6 +13,8 @@ rows in 16 intervals of 4 (`linear`: the per-layer projections of that model
 at 64 rows, each timed beside torch's cuBLAS GEMMs for the same products, with
 enough weight copies in rotation that no launch finds its weights in L2, and
 replayed from a CUDA graph so that host launch cost is not measured).
+`relevance`: select_support's query relevance at config 3 (Qwen3-8B
+embedding table, 151936 x 4096 bf16; 31744 prompt tokens; 8 query tokens).
 `attention --geometry config3`: one layer of the Qwen3-8B shape at 32k context
 (31744 cached rows, 1383 rows in 32 intervals from 4096). Inputs are seeded
 random tensors. After two
@@ -192,9 +195,26 @@ def linear(reps: int, only: str | None) -> None:
               f"status {int(workspace[:4].view(torch.int32).item())}")
 
 
+def relevance(reps: int) -> None:
+    lib = _lib.load()
+    vocab, hidden, n, nq = 151936, 4096, 31744, 8
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    table = (torch.randn(vocab, hidden, device="cuda", generator=gen) * 0.02).bfloat16()
+    prompt = torch.randint(0, vocab, (n,), device="cuda", generator=gen)
+    query = torch.randint(0, vocab, (nq,), device="cuda", generator=gen)
+    scores = torch.empty(n, device="cuda")
+    need = lib.kvr_query_relevance_workspace_size(hidden, nq)
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    us = _graph_time(lambda i: _lib.check(lib.kvr_query_relevance(
+        table.data_ptr(), vocab, hidden, _lib.DTYPE_BF16, prompt.data_ptr(), n, query.data_ptr(), nq, 0.25,
+        scores.data_ptr(), ws.data_ptr(), need, _lib.stream_handle()), "relevance"), reps)
+    algo = n * hidden * 2
+    print(f"kvr_query_relevance: {us:.1f} us/call, {algo / us / 1e3:.0f} GB/s of embedding rows ({algo} bytes)")
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("kernel", choices=["shift", "attention", "copy", "linear"])
+    parser.add_argument("kernel", choices=["shift", "attention", "copy", "linear", "relevance"])
     parser.add_argument("--only", default=None, help="linear: one of qkv, o, gate_up, down")
     parser.add_argument("--reps", type=int, default=10)
     parser.add_argument("--layers", type=int, default=LAYERS, help="shift: layers (fewer for a small capture)")
@@ -209,6 +229,8 @@ def main() -> None:
         copy(args.reps, args.tensors)
     elif args.kernel == "linear":
         linear(args.reps, args.only)
+    elif args.kernel == "relevance":
+        relevance(args.reps)
     else:
         attention(args.reps, args.precision, args.geometry)
 

@@ -40,6 +40,7 @@ extern "C" {
 
 #define KVR_DTYPE_BF16 0
 #define KVR_DTYPE_F16 1
+#define KVR_DTYPE_F32 2  /* kvr_query_relevance's embedding table only */
 
 /* Largest number of per-layer tensors one multi-layer launch takes (K and V of
  * 128 layers). */
@@ -341,6 +342,23 @@ KVR_API int kvr_selected_attention_static(const void* q, const void* k_cache, co
                                           int64_t cache_head_stride, int64_t cache_row_stride,
                                           int64_t max_position, float scale, int precision,
                                           int dtype, void* stream);
+
+/*
+ * Query relevance of prompt tokens from the frozen input embeddings
+ * (dense_query_relevance_scores, scoring.py:11-72), the scoring step of
+ * select_support's SUR allocation (api.py:83-96):
+ *   scores[t] = max_q cos(E[prompt_ids[t]], E[query_ids[q]])
+ *               + exact_boost * [prompt_ids[t] in query_ids]
+ * with E the [vocab, hidden] table (dtype KVR_DTYPE_BF16/F16/F32, rows
+ * contiguous), cosine through x / max(||x||, 1e-12) in fp32. scores: fp32
+ * [prompt_count] on the device. The workspace (kvr_query_relevance_workspace_size
+ * bytes) holds the normalised query rows; its first 4 bytes count ids outside
+ * [0, vocab) (those scores are NaN): read it with the scores.
+ */
+KVR_API size_t kvr_query_relevance_workspace_size(int hidden, int query_count);
+KVR_API int kvr_query_relevance(const void* embed, int64_t vocab, int hidden, int dtype, const int64_t* prompt_ids,
+                                int64_t prompt_count, const int64_t* query_ids, int query_count, float exact_boost,
+                                float* scores, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }
