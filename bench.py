@@ -64,7 +64,24 @@ CONFIG3 = dict(name="qwen3-8b-shape", arch="qwen3", layers=36, hidden=4096, head
                delete=1024, intervals=32, rows=1383,
                metric="repaired rows/s (packed refresh stage, Qwen3-8B shape, 32768 ctx, 32 intervals, 1383 rows)",
                workload="config3: Qwen3-8B shape, 32768 ctx, delete 1024@4096 (N=31744), 1383 rows in 32 intervals")
-WORKLOADS = {"config2": CONFIG, "config3": CONFIG3}
+# the same model at 2048-token context, 128 tokens
+# deleted at 512, 64 rows in one interval.
+CONFIG1 = dict(CONFIG, context=2048, delete_at=512, delete=128, intervals=1, rows=64,
+               metric="repaired rows/s (packed refresh stage, Llama-3-8B shape, 2048 ctx, 1 interval, 64 rows)",
+               workload="config1: Llama-3-8B shape, 2048 ctx, delete 128@512 (N=1920), 1 interval x 64 rows")
+WORKLOADS = {"config1": CONFIG1, "config2": CONFIG, "config3": CONFIG3}
+
+
+def workload_config(args):
+    """The workload's config; ``--intervals`` re-splits its rows (the
+    1/4/16-interval sweep of config 2)."""
+    cfg = dict(WORKLOADS[args.workload])
+    if getattr(args, "intervals", None):
+        cfg["intervals"] = args.intervals
+        cfg["metric"] = cfg["metric"].replace(f"{WORKLOADS[args.workload]['intervals']} interval",
+                                              f"{args.intervals} interval")
+        cfg["workload"] += f" (re-split into {args.intervals} intervals)"
+    return cfg
 
 
 def _peaks():
@@ -316,7 +333,7 @@ def gpu_comparator(args):
     full depth: the "reference CUDA SDPA path" the north star compares with.
     Same workload as our arm; CUDA events around each call, median."""
     device = torch.device("cuda", 0)
-    cfg = dict(WORKLOADS[args.workload])
+    cfg = workload_config(args)
     from oracle.hf_packed import packed_refresh_hf
 
     model = build_model(cfg, 1, device)
@@ -344,7 +361,7 @@ def reference_arm(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    cfg = dict(WORKLOADS[args.workload])
+    cfg = workload_config(args)
     base = run_cpu_baseline(cfg, sample_layers=2, threads=threads)
     line = {"impl": "reference", "metric": cfg["metric"], "value": base["value"], "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["ms_per_request"],
@@ -376,7 +393,7 @@ def our_arm(args):
     torch.cuda.set_device(device)
     native_build.build()
     _lib.load()
-    cfg = dict(WORKLOADS[args.workload])
+    cfg = workload_config(args)
     seed = (3 if args.workload == "config3" else 1) + rank
     model = build_model(cfg, seed, device)
     shim = OperatorShim(model)
@@ -669,9 +686,12 @@ def main():
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     parser.add_argument("--device", choices=["cpu", "cuda"], default="cpu",
                         help="with --impl reference: cpu (the reference arm) or cuda (the GPU comparator)")
-    parser.add_argument("--workload", choices=["config2", "config3", "70b-tp"], default="config2",
-                        help="config2: Llama-3-8B refresh, 64 rows (DP replicas when N>1); config3: Qwen3-8B, 32k "
-                             "context, 1383 rows (DP replicas); 70b-tp: configs[4], head-sharded")
+    parser.add_argument("--workload", choices=["config1", "config2", "config3", "70b-tp"], default="config2",
+                        help="config2: Llama-3-8B refresh, 8k context, 64 rows (DP replicas when N>1); config1: the "
+                             "same at 2k context, one interval; config3: Qwen3-8B, 32k context, 1383 rows (DP "
+                             "replicas); 70b-tp: configs[4], head-sharded")
+    parser.add_argument("--intervals", type=int, default=None,
+                        help="re-split the workload's rows into this many intervals (config 2 sweep: 1, 4, 16)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
