@@ -70,6 +70,10 @@ CONFIG1 = dict(CONFIG, context=2048, delete_at=512, delete=128, intervals=1, row
                metric="repaired rows/s (packed refresh stage, Llama-3-8B shape, 2048 ctx, 1 interval, 64 rows)",
                workload="config1: Llama-3-8B shape, 2048 ctx, delete 128@512 (N=1920), 1 interval x 64 rows")
 WORKLOADS = {"config1": CONFIG1, "config2": CONFIG, "config3": CONFIG3}
+# DRAM bytes of one RoPE-fix launch at config 2, from one ncu capture of a
+# 4-layer case of the same kernel scaled to 32 layers: reads 130.1 MB + writes
+# 79.9 MB, x8 (profiles/shift_cache_config2_traffic.md).
+ROPE_TRAFFIC = int((130.1e6 + 79.9e6) * 8)
 
 
 def workload_config(args):
@@ -542,7 +546,12 @@ def our_arm(args):
         "roofline": {"bound": "hbm",
                      "kernel": f"kvr_shift_cache_layers (RoPE fix + shift, {cfg['layers']} layers, 1 launch)",
                      "achieved": rope_gbs, "peak": hbm, "unit": "GB/s", "frac": rope_gbs / hbm,
-                     "traffic": None, "algorithmic_bytes": fused_bytes, "rope_only_bytes": rope_bytes,
+                     "traffic": ROPE_TRAFFIC if args.workload == "config2" and not args.intervals else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the same kernel on 4 of "
+                                       "the 32 layers (260 MB algorithmic, > L2), scaled x8 "
+                                       "(profiles/shift_cache_config2_traffic.md); writes still in L2 at the end "
+                                       "of the launch are not counted",
+                     "algorithmic_bytes": fused_bytes, "rope_only_bytes": rope_bytes,
                      "avg_us": rope_t * 1e6, "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"},
         "step_roofline": {"bound": "hbm" if algo_bytes / hbm / 1e6 >= step_flops / tflops / 1e9 else "tensor",
                           "algorithmic_bytes": algo_bytes, "flops": step_flops,
