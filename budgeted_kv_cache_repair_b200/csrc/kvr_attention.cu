@@ -587,12 +587,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 // already in flight (lane l owns columns [l*D/32, (l+1)*D/32)); the warp
 // reduces M and L with shuffles and takes each chunk's weight by shuffle. The
 // chunk order of the sum is fixed, so the result is too.
-template <class T, int D>
+// BATCH (chunks whose O rows are loaded together) is a template parameter:
+// the launch picks the smallest of 4 and 16 that holds every chunk, so that
+// few-chunk plans keep the registers, and the warps resident per SM, of a
+// small batch.
+template <class T, int D, int BATCH>
 __global__ void __launch_bounds__(256) attn_combine_kernel(Args a) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
   pdl_wait();  // every input may come from the previous kernel
   constexpr int PER = D / 32;  // values per lane: 4 (D=128) or 2 (D=64)
-  constexpr int BATCH = 16;
   using Vec = typename std::conditional<PER == 4, float4, float2>::type;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
@@ -779,8 +782,9 @@ int launch(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, 
   int st = launch_pdl<attn_tc_kernel<T, D, SPLIT>>(grid, dim3(THREADS), smem, s, 1, mk, mv, mq, a);
   if (st != KVR_OK || a.nchunks == 1) return st;
   const int64_t total_m = a.rows * a.group;
-  return launch_pdl<attn_combine_kernel<T, D>>(dim3(static_cast<unsigned>((total_m + 7) / 8), a.hkv), dim3(256), 0,
-                                               s, 1, a);
+  const dim3 cgrid(static_cast<unsigned>((total_m + 7) / 8), a.hkv);
+  if (a.nchunks <= 4) return launch_pdl<attn_combine_kernel<T, D, 4>>(cgrid, dim3(256), 0, s, 1, a);
+  return launch_pdl<attn_combine_kernel<T, D, 16>>(cgrid, dim3(256), 0, s, 1, a);
 }
 
 }  // namespace attn

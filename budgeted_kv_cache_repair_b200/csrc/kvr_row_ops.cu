@@ -9,6 +9,12 @@ namespace kvr {
 constexpr int kNormThreads = 256;
 constexpr int kNormMaxVecs = 4;  // hidden_size <= 256 * 4 * 8 = 8192
 
+// A kernel as a type, for generic launch helpers.
+template <auto K>
+struct KernelRef {
+  static constexpr auto value = K;
+};
+
 // Sum of `n` fp32 partial slices of 8 consecutive values, in slice order,
 // rounded to the element type (a deferred projection output).
 // Loads of up to kPartBatch slices are all issued before any add (one memory
@@ -43,7 +49,11 @@ __device__ __forceinline__ Vec8 sum_parts8(const float* p, int n, int64_t slice)
 
 // With nparts > 0 the delta is a deferred projection: nparts fp32 slices
 // (row stride p_stride, slice stride p_slice floats), summed and rounded here.
-template <class T>
+// VPT: 16-byte vectors per thread (ceil(hidden / 8 / kNormThreads)) and
+// PARTS (the delta is deferred fp32 slices) are template parameters so that
+// registers, and with them the CTAs resident per SM, follow the work
+// (hundreds of rows run in many waves).
+template <class T, int VPT, bool PARTS>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
     uint16_t* hidden, const uint16_t* __restrict__ delta, const uint16_t* __restrict__ weight,
     uint16_t* out, int vpr, int64_t h_stride, int64_t d_stride, int64_t o_stride, float inv_h,
@@ -52,10 +62,10 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   // With weight_early (the layer loop: the norm weight is a model constant)
   // the weight is fetched before the wait, so its load overlaps the previous
   // kernel instead of following the reduction.
-  Vec8 w[kNormMaxVecs];
+  Vec8 w[VPT];
   if (weight_early) {
 #pragma unroll
-    for (int k = 0; k < kNormMaxVecs; ++k) {
+    for (int k = 0; k < VPT; ++k) {
       const int v = threadIdx.x + k * kNormThreads;
       if (v < vpr) w[k] = ld_vec8(weight + v * 8);
     }
@@ -63,7 +73,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   pdl_wait();  // every other input may come from the previous kernel
   if (!weight_early) {
 #pragma unroll
-    for (int k = 0; k < kNormMaxVecs; ++k) {
+    for (int k = 0; k < VPT; ++k) {
       const int v = threadIdx.x + k * kNormThreads;
       if (v < vpr) w[k] = ld_vec8(weight + v * 8);
     }
@@ -72,13 +82,13 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   uint16_t* hrow = hidden + r * h_stride;
   // Every load of the row (hidden, then the delta or its partial slices) is
   // issued before the first store back to `hidden`: one memory round trip.
-  Vec8 x[kNormMaxVecs], dv[kNormMaxVecs];
+  Vec8 x[VPT], dv[VPT];
 #pragma unroll
-  for (int k = 0; k < kNormMaxVecs; ++k) {
+  for (int k = 0; k < VPT; ++k) {
     const int v = threadIdx.x + k * kNormThreads;
     if (v < vpr) {
       x[k] = ld_vec8(hrow + v * 8);
-      if (nparts)
+      if constexpr (PARTS)
         dv[k] = sum_parts8<T>(parts + r * p_stride + v * 8, nparts, p_slice);
       else if (delta)
         dv[k] = ld_vec8(delta + r * d_stride + v * 8);
@@ -86,10 +96,10 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   }
   float ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kNormMaxVecs; ++k) {
+  for (int k = 0; k < VPT; ++k) {
     const int v = threadIdx.x + k * kNormThreads;
     if (v < vpr) {
-      if (delta || nparts) {
+      if (PARTS || delta) {
         // residual + hidden_states, rounded to the element type.
 #pragma unroll
         for (int e = 0; e < 8; ++e) x[k].h[e] = T::from_f(__fadd_rn(T::to_f(x[k].h[e]), T::to_f(dv[k].h[e])));
@@ -117,7 +127,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   __syncthreads();
   const float inv = rsqrtf(__fadd_rn(red[0] * inv_h, eps));
 #pragma unroll
-  for (int k = 0; k < kNormMaxVecs; ++k) {
+  for (int k = 0; k < VPT; ++k) {
     const int v = threadIdx.x + k * kNormThreads;
     if (v < vpr) {
       Vec8 y;
@@ -163,7 +173,9 @@ struct QkvArgs {
   int consts_early;
 };
 
-template <class T, int D>
+// PARTS: q/k/v come as deferred fp32 slices (a.nparts > 0); a template
+// parameter so the direct path keeps the registers of the slice sums free.
+template <class T, int D, bool PARTS>
 __global__ void __launch_bounds__(256) qkv_rope_scatter_kernel(QkvArgs a) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
   constexpr int E = D / 32;  // 4 for D=128, 2 for D=64
@@ -207,7 +219,7 @@ __global__ void __launch_bounds__(256) qkv_rope_scatter_kernel(QkvArgs a) {
                        : (is_v ? a.v_cache : a.k_cache) + head * a.c_hs + p * a.c_rs;
   dst += lane * E;
   uint16_t xb[E];
-  if (a.nparts) {
+  if constexpr (PARTS) {
     const float* ps =
         a.parts + r * a.p_rs + (is_q ? a.q_col : (is_v ? a.v_col : a.k_col)) + head * D + lane * E;
     float acc[E];
@@ -332,16 +344,25 @@ int add_rmsnorm_ex(void* hidden, const void* delta, const float* parts, int npar
   const int vpr = hidden_size / 8;
   const float inv_h = 1.0f / static_cast<float>(hidden_size);
   int st = KVR_OK;
-  if (dtype == KVR_DTYPE_BF16)
-    st = launch_pdl<add_rmsnorm_kernel<BF16>>(static_cast<unsigned>(rows), dim3(kNormThreads), 0, s, 1, 
+  auto go = [&](auto kernel) {
+    return launch_pdl<decltype(kernel)::value>(static_cast<unsigned>(rows), dim3(kNormThreads), 0, s, 1,
         static_cast<uint16_t*>(hidden), static_cast<const uint16_t*>(delta),
         static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), vpr, hidden_stride,
         delta_stride, out_stride, inv_h, eps, parts, nparts, part_stride, part_slice, weight_early ? 1 : 0);
-  else
-    st = launch_pdl<add_rmsnorm_kernel<F16>>(static_cast<unsigned>(rows), dim3(kNormThreads), 0, s, 1, 
-        static_cast<uint16_t*>(hidden), static_cast<const uint16_t*>(delta),
-        static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), vpr, hidden_stride,
-        delta_stride, out_stride, inv_h, eps, parts, nparts, part_stride, part_slice, weight_early ? 1 : 0);
+  };
+  const int vpt = (vpr + kNormThreads - 1) / kNormThreads;
+  auto pick = [&](auto elem) {
+    using T = decltype(elem);
+    if (nparts) {
+      if (vpt <= 1) return go(KernelRef<add_rmsnorm_kernel<T, 1, true>>{});
+      if (vpt == 2) return go(KernelRef<add_rmsnorm_kernel<T, 2, true>>{});
+      return go(KernelRef<add_rmsnorm_kernel<T, 4, true>>{});
+    }
+    if (vpt <= 1) return go(KernelRef<add_rmsnorm_kernel<T, 1, false>>{});
+    if (vpt == 2) return go(KernelRef<add_rmsnorm_kernel<T, 2, false>>{});
+    return go(KernelRef<add_rmsnorm_kernel<T, 4, false>>{});
+  };
+  st = dtype == KVR_DTYPE_BF16 ? pick(BF16{}) : pick(F16{});
   return st;
 }
 
@@ -426,12 +447,23 @@ int qkv_rope_scatter_ex(const void* q_in, const void* k_in, const void* v_in, in
   if (blocks > 0x7fffffff) return KVR_ERR_UNSUPPORTED;
   auto s = static_cast<cudaStream_t>(stream);
   int st = KVR_OK;
+  const unsigned grid = static_cast<unsigned>(blocks);
+  auto go = [&](auto kernel) { return launch_pdl<decltype(kernel)::value>(grid, dim3(256), 0, s, 1, a); };
+  const bool with_parts = a.nparts > 0;
   if (dtype == KVR_DTYPE_BF16) {
-    if (head_dim == 128) st = launch_pdl<qkv_rope_scatter_kernel<BF16, 128>>(static_cast<unsigned>(blocks), dim3(256), 0, s, 1, a);
-    else st = launch_pdl<qkv_rope_scatter_kernel<BF16, 64>>(static_cast<unsigned>(blocks), dim3(256), 0, s, 1, a);
+    if (head_dim == 128)
+      st = with_parts ? go(KernelRef<qkv_rope_scatter_kernel<BF16, 128, true>>{})
+                      : go(KernelRef<qkv_rope_scatter_kernel<BF16, 128, false>>{});
+    else
+      st = with_parts ? go(KernelRef<qkv_rope_scatter_kernel<BF16, 64, true>>{})
+                      : go(KernelRef<qkv_rope_scatter_kernel<BF16, 64, false>>{});
   } else {
-    if (head_dim == 128) st = launch_pdl<qkv_rope_scatter_kernel<F16, 128>>(static_cast<unsigned>(blocks), dim3(256), 0, s, 1, a);
-    else st = launch_pdl<qkv_rope_scatter_kernel<F16, 64>>(static_cast<unsigned>(blocks), dim3(256), 0, s, 1, a);
+    if (head_dim == 128)
+      st = with_parts ? go(KernelRef<qkv_rope_scatter_kernel<F16, 128, true>>{})
+                      : go(KernelRef<qkv_rope_scatter_kernel<F16, 128, false>>{});
+    else
+      st = with_parts ? go(KernelRef<qkv_rope_scatter_kernel<F16, 64, true>>{})
+                      : go(KernelRef<qkv_rope_scatter_kernel<F16, 64, false>>{});
   }
   return st;
 }
