@@ -52,7 +52,8 @@ class RefreshRequest(ctypes.Structure):
                 ("cos_tab", ctypes.c_void_p), ("sin_tab", ctypes.c_void_p), ("attention_precision", ctypes.c_int),
                 ("tp_comm", ctypes.c_void_p), ("projections", ctypes.c_int),
                 ("k_src", ctypes.POINTER(ctypes.c_void_p)), ("v_src", ctypes.POINTER(ctypes.c_void_p)),
-                ("src_head_stride", ctypes.c_int64), ("src_row_stride", ctypes.c_int64)]
+                ("src_head_stride", ctypes.c_int64), ("src_row_stride", ctypes.c_int64),
+                ("graph_replay", ctypes.c_int)]
 
 
 LINEAR_MAX_SEGMENTS = 4
@@ -71,6 +72,7 @@ SIGNATURES = {
     "kvr_status_string": (ctypes.c_char_p, [_I]),
     "kvr_last_cuda_error": (_I, []),
     "kvr_kernel_launches": (ctypes.c_uint64, []),
+    "kvr_graph_replays": (ctypes.c_uint64, []),
     "kvr_copy_layers": (_I, [_PP, _PP, _I, _I, _L, _I, _L, _L, _L, _L, _I, _P]),
     "kvr_rope_shift_layers": (_I, [_PP, _PP, _I, _I, _L, _I, _L, _L, _L, _L, _P, _I, _P]),
     "kvr_shift_cache_layers": (_I, [_PP, _PP, _PP, _PP, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L,

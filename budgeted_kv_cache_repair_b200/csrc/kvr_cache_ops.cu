@@ -16,10 +16,18 @@ namespace kvr {
 namespace {
 thread_local int g_last_cuda_error = 0;
 unsigned long long g_launches = 0;
+thread_local uint64_t* g_captured = nullptr;  // set while this thread captures a graph
 }
 
 void set_last_cuda_error(cudaError_t e) { g_last_cuda_error = static_cast<int>(e); }
-void count_launch() { __atomic_add_fetch(&g_launches, 1ull, __ATOMIC_RELAXED); }
+void count_launch() {
+  if (g_captured)
+    ++*g_captured;
+  else
+    __atomic_add_fetch(&g_launches, 1ull, __ATOMIC_RELAXED);
+}
+void count_launches(uint64_t n) { __atomic_add_fetch(&g_launches, static_cast<unsigned long long>(n), __ATOMIC_RELAXED); }
+void count_captured_launches(uint64_t* sink) { g_captured = sink; }
 
 // ---------------------------------------------------------------------------
 // Ownership copy (clone_cache, cache.py:31-44).

@@ -17,6 +17,11 @@ constexpr int kNumSMs = 148;  // B200: 2 dies x 74 SMs
 void set_last_cuda_error(cudaError_t e);
 // Adds to the process-wide launch counter behind kvr_kernel_launches().
 void count_launch();
+// Adds n launches at once (the kernels of a replayed CUDA graph).
+void count_launches(uint64_t n);
+// While `sink` is set, this thread's launches are being captured into a graph
+// (recorded, not run): count_launch() adds to *sink instead. NULL ends it.
+void count_captured_launches(uint64_t* sink);
 
 // kvr_selected_attention; with status_zeroed the caller has zeroed the status
 // word at the start of `workspace` and no memset is issued.

@@ -27,8 +27,10 @@
 
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
+#include <vector>
 
 #include "kvr_common.cuh"
 #include "kvr_linear.h"
@@ -164,6 +166,7 @@ int gemm(cublasHandle_t h, const void* x, int64_t ldx, const void* w, void* y, i
 struct RefreshStreams {
   cudaStream_t work = nullptr;
   cudaStream_t copy = nullptr;
+  cudaStream_t capture = nullptr;  // only ever captured into a graph, never run
   cudaEvent_t start = nullptr;
   cudaEvent_t done = nullptr;
   cudaEvent_t layer[KVR_MAX_LAYER_TENSORS / 2] = {};
@@ -183,6 +186,7 @@ int refresh_streams_for_current_device(RefreshStreams** out) {
     e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
     if (e == cudaSuccess && !c.work) e = cudaStreamCreateWithPriority(&c.work, cudaStreamNonBlocking, greatest);
     if (e == cudaSuccess && !c.copy) e = cudaStreamCreateWithPriority(&c.copy, cudaStreamNonBlocking, least);
+    if (e == cudaSuccess && !c.capture) e = cudaStreamCreateWithFlags(&c.capture, cudaStreamNonBlocking);
     if (e == cudaSuccess && !c.start) e = cudaEventCreateWithFlags(&c.start, cudaEventDisableTiming);
     if (e == cudaSuccess && !c.done) e = cudaEventCreateWithFlags(&c.done, cudaEventDisableTiming);
     for (int l = 0; e == cudaSuccess && l < KVR_MAX_LAYER_TENSORS / 2; ++l)
@@ -243,8 +247,8 @@ size_t kvr_packed_refresh_workspace_size(const kvr_model* model, int64_t rows, i
   return layout(model, rows, cache_rows).total;
 }
 
-int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, void* workspace,
-                       size_t workspace_bytes, void* stream) {
+static int refresh_direct(const kvr_model* model, const kvr_refresh_request* req, void* workspace,
+                          size_t workspace_bytes, void* stream) {
   if (!valid_model(model) || !req) return KVR_ERR_INVALID_ARG;
   const kvr_model& m = *model;
   const kvr_refresh_request& r = *req;
@@ -475,6 +479,190 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
 #undef KVR_TRY
   return KVR_OK;
 }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Replay of repeated requests as CUDA graphs (request.graph_replay).
+//
+// The layer loop issues ~14 launches per layer; the cuBLAS kernels among them
+// cannot start before their predecessor has drained (no programmatic launch),
+// which costs ~2.5 us of idle GPU per boundary when launched into a stream and
+// less inside a graph. A request that repeats an earlier call's launch key (the
+// same model weights, geometry, options and every device pointer: cache,
+// sources, ids, positions, rotary tables, workspace) issues exactly the same
+// launches, so its second occurrence is captured once and later ones replay
+// the graph. Positions and ids are read by the kernels at run time: a caller
+// that stages each request's values into the same buffers (and drops or reuses
+// its output cache) hits the cache with new data.
+// ---------------------------------------------------------------------------
+namespace kvr {
+namespace {
+
+constexpr size_t kGraphs = 4;  // executable graphs kept per (thread, device)
+constexpr size_t kSeen = 8;    // keys run once, remembered for a capture on the next
+unsigned long long g_replays = 0;
+
+std::vector<uint64_t> graph_key(int dev, const kvr_model& m, const kvr_refresh_request& r, const void* ws,
+                                size_t bytes) {
+  std::vector<uint64_t> k;
+  k.reserve(40 + 16 * static_cast<size_t>(m.num_layers));
+  auto p = [&](const void* x) { k.push_back(static_cast<uint64_t>(reinterpret_cast<uintptr_t>(x))); };
+  auto v = [&](int64_t x) { k.push_back(static_cast<uint64_t>(x)); };
+  uint32_t eps_bits = 0;
+  memcpy(&eps_bits, &m.eps, sizeof(eps_bits));
+  v(dev), v(m.num_layers), v(m.hidden), v(m.q_heads), v(m.kv_heads), v(m.head_dim), v(m.intermediate);
+  v(m.vocab), v(eps_bits), v(m.dtype), p(m.embed);
+  for (int l = 0; l < m.num_layers; ++l) {
+    const kvr_layer_weights& w = m.layers[l];
+    for (const void* x : {w.input_norm, w.qkv, w.q, w.k, w.v, w.q_norm, w.k_norm, w.o, w.post_norm, w.gate, w.up,
+                          w.down})
+      p(x);
+    p(r.k_cache[l]), p(r.v_cache[l]);
+    if (r.k_src) p(r.k_src[l]), p(r.v_src[l]);
+  }
+  v(r.cache_rows), v(r.cache_head_stride), v(r.cache_row_stride), p(r.ids), v(r.id_count), p(r.positions);
+  v(r.rows), v(r.max_position), p(r.cos_tab), p(r.sin_tab), v(r.attention_precision), p(r.tp_comm);
+  v(r.projections), v(r.k_src != nullptr), v(r.src_head_stride), v(r.src_row_stride), p(ws), v(bytes);
+  return k;
+}
+
+struct GraphEntry {
+  std::vector<uint64_t> key;
+  cudaGraphExec_t exec = nullptr;
+  cudaEvent_t last = nullptr;  // recorded after each launch; eviction waits for it
+  uint64_t launches = 0;       // library kernels in the graph
+  uint64_t used = 0;
+};
+
+struct GraphCache {
+  std::vector<GraphEntry> entries;
+  std::vector<std::vector<uint64_t>> seen;  // oldest first
+  uint64_t clock = 0;
+};
+
+GraphCache& graph_cache_for(int dev) {
+  thread_local std::unordered_map<int, GraphCache> caches;
+  return caches[dev];
+}
+
+int launch_entry(GraphEntry& e, cudaStream_t s) {
+  cudaError_t err = cudaGraphLaunch(e.exec, s);
+  if (err == cudaSuccess) err = cudaEventRecord(e.last, s);
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return KVR_ERR_CUDA;
+  }
+  count_launches(e.launches);
+  __atomic_add_fetch(&g_replays, 1ull, __ATOMIC_RELAXED);
+  return KVR_OK;
+}
+
+// Drops the least recently used graph once its latest launch has finished.
+int evict_oldest(GraphCache& c) {
+  size_t at = 0;
+  for (size_t i = 1; i < c.entries.size(); ++i)
+    if (c.entries[i].used < c.entries[at].used) at = i;
+  GraphEntry& e = c.entries[at];
+  cudaError_t err = cudaEventSynchronize(e.last);
+  if (err == cudaSuccess) err = cudaGraphExecDestroy(e.exec);
+  cudaEventDestroy(e.last);
+  c.entries.erase(c.entries.begin() + static_cast<std::ptrdiff_t>(at));
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return KVR_ERR_CUDA;
+  }
+  return KVR_OK;
+}
+
+int refresh_graphed(const kvr_model* model, const kvr_refresh_request* req, void* ws, size_t bytes, void* stream) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return KVR_ERR_CUDA;
+  }
+  GraphCache& c = graph_cache_for(dev);
+  std::vector<uint64_t> key = graph_key(dev, *model, *req, ws, bytes);
+  const auto s = static_cast<cudaStream_t>(stream);
+  for (GraphEntry& e : c.entries)
+    if (e.key == key) {
+      e.used = ++c.clock;
+      return launch_entry(e, s);
+    }
+  auto seen = std::find(c.seen.begin(), c.seen.end(), key);
+  if (seen == c.seen.end()) {
+    // First occurrence: run directly and remember the key.
+    const int st = refresh_direct(model, req, ws, bytes, stream);
+    if (st == KVR_OK) {
+      if (c.seen.size() >= kSeen) c.seen.erase(c.seen.begin());
+      c.seen.push_back(std::move(key));
+    }
+    return st;
+  }
+  c.seen.erase(seen);
+  // Second occurrence: capture the same launches on the idle capture stream,
+  // then run the graph on the caller's stream. Anything that fails during the
+  // capture leaves nothing behind and the call runs directly instead.
+  RefreshStreams* cp = nullptr;
+  int st = refresh_streams_for_current_device(&cp);
+  if (st != KVR_OK) return st;
+  err = cudaStreamBeginCapture(cp->capture, cudaStreamCaptureModeThreadLocal);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return refresh_direct(model, req, ws, bytes, stream);
+  }
+  uint64_t captured = 0;
+  count_captured_launches(&captured);
+  st = refresh_direct(model, req, ws, bytes, cp->capture);
+  count_captured_launches(nullptr);
+  cudaGraph_t graph = nullptr;
+  err = cudaStreamEndCapture(cp->capture, &graph);
+  cudaGraphExec_t exec = nullptr;
+  if (st == KVR_OK && err == cudaSuccess && graph) err = cudaGraphInstantiate(&exec, graph, 0);
+  if (graph) cudaGraphDestroy(graph);
+  if (st != KVR_OK || err != cudaSuccess || !exec) {
+    if (exec) cudaGraphExecDestroy(exec);
+    (void)cudaGetLastError();
+    return refresh_direct(model, req, ws, bytes, stream);
+  }
+  GraphEntry e;
+  e.key = std::move(key);
+  e.exec = exec;
+  e.launches = captured;
+  e.used = ++c.clock;
+  err = cudaEventCreateWithFlags(&e.last, cudaEventDisableTiming);
+  if (err != cudaSuccess) {
+    cudaGraphExecDestroy(exec);
+    set_last_cuda_error(err);
+    return KVR_ERR_CUDA;
+  }
+  if (c.entries.size() >= kGraphs) {
+    st = evict_oldest(c);
+    if (st != KVR_OK) {
+      cudaGraphExecDestroy(exec);
+      cudaEventDestroy(e.last);
+      return st;
+    }
+  }
+  c.entries.push_back(std::move(e));
+  return launch_entry(c.entries.back(), s);
+}
+
+}  // namespace
+}  // namespace kvr
+
+extern "C" {
+
+int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if (req && req->graph_replay && req->rows > 0 && !req->tp_comm && valid_model(model) && req->k_cache &&
+      req->v_cache)
+    return refresh_graphed(model, req, workspace, workspace_bytes, stream);
+  return refresh_direct(model, req, workspace, workspace_bytes, stream);
+}
+
+uint64_t kvr_graph_replays(void) { return __atomic_load_n(&g_replays, __ATOMIC_RELAXED); }
 
 int kvr_tp_unique_id(void* out) {
   if (!out) return KVR_ERR_INVALID_ARG;

@@ -26,11 +26,19 @@ separate GEMMs whose k/v weights are only 8 MB each.
 The last layer stops after its K/V scatter: its attention output, MLP and the
 final norm feed nothing in the returned cache (the reference computes and
 discards them).
+
+Repeated requests replay a CUDA graph (``GRAPH_REPLAY``): each request's ids,
+positions and rotary tables are staged into buffers kept per (device, stream,
+geometry), with one workspace there, so a request with the geometry and the
+cache buffers of an earlier one (for example, the caller released the last
+output before asking again) makes the same launches and the library replays
+them from a graph captured on the second such call.
 """
 
 from __future__ import annotations
 
 import weakref
+from collections import OrderedDict
 from dataclasses import dataclass
 
 import torch
@@ -117,6 +125,42 @@ ATTENTION_PRECISION = _lib.ATTN_P_ROUNDED
 # Projection GEMMs of the layer loop: cuBLAS, or the sm_100a weight-streaming
 # kernel (kvr_linear) for requests of up to 256 rows.
 PROJECTIONS = _lib.PROJ_CUBLAS
+# Stage request inputs into stable buffers and let the library replay graphs of
+# repeated requests (kvr_refresh_request.graph_replay).
+GRAPH_REPLAY = True
+_STAGING_KEEP = 4
+
+
+class _Staging:
+    """Per (device, stream, geometry) input buffers and workspace of a refresh."""
+
+    def __init__(self, device, id_count: int, rows: int, dim: int, dtype, workspace_bytes: int):
+        self.ids = torch.empty(id_count, dtype=torch.int64, device=device)
+        self.positions = torch.empty(rows, dtype=torch.int64, device=device)
+        self.cos = torch.empty(rows, dim, dtype=dtype, device=device)
+        self.sin = torch.empty(rows, dim, dtype=dtype, device=device)
+        self.workspace = torch.empty(workspace_bytes, dtype=torch.uint8, device=device)
+
+
+_staging: "OrderedDict[tuple, _Staging]" = OrderedDict()
+
+
+def _staged(device, ids, positions, cos, sin, need) -> _Staging:
+    """The staging buffers for this request's geometry on the current stream,
+    filled with its values (stream-ordered copies)."""
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream, ids.numel(), positions.numel(), cos.shape[1], cos.dtype, need)
+    st = _staging.pop(key, None)
+    if st is None:
+        st = _Staging(device, ids.numel(), positions.numel(), cos.shape[1], cos.dtype, need)
+        while len(_staging) >= _STAGING_KEEP:
+            _staging.popitem(last=False)
+    _staging[key] = st
+    st.ids.copy_(ids)
+    st.positions.copy_(positions)
+    st.cos.copy_(cos)
+    st.sin.copy_(sin)
+    return st
 
 
 class KernelTimer:
@@ -272,6 +316,13 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
     need = lib.kvr_packed_refresh_workspace_size(model, rows, cache_rows) if rows else 0
     if rows and not need:
         raise ValueError("model geometry is outside the built kernels")
-    workspace = torch.empty(need, dtype=torch.uint8, device=device)
+    if GRAPH_REPLAY and rows and tp_comm is None:
+        st = _staged(device, ids, positions, cos, sin, need)
+        request.ids, request.positions = st.ids.data_ptr(), st.positions.data_ptr()
+        request.cos_tab, request.sin_tab = st.cos.data_ptr(), st.sin.data_ptr()
+        request.graph_replay = 1
+        workspace = st.workspace
+    else:
+        workspace = torch.empty(need, dtype=torch.uint8, device=device)
     _lib.check(lib.kvr_packed_refresh(model, request, workspace.data_ptr(), need, _lib.stream_handle(device)),
                "packed_refresh")

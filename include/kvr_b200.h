@@ -52,8 +52,12 @@ KVR_API const char* kvr_status_string(int status);
 /* cudaError_t of the last failing CUDA call in this thread (0 if none). */
 KVR_API int kvr_last_cuda_error(void);
 /* Kernels this library has launched in this process (all threads, all
- * devices); a diagnostic counter for benchmarks and tests. */
+ * devices), those run by replayed graphs included; a diagnostic counter for
+ * benchmarks and tests. */
 KVR_API uint64_t kvr_kernel_launches(void);
+/* Packed refreshes this process ran as a CUDA graph (request.graph_replay):
+ * the graph launches of captured keys, the capturing call's own included. */
+KVR_API uint64_t kvr_graph_replays(void);
 
 /*
  * Output ownership copy of every layer: dst[t][h, n, :] = src[t][h, n, :] for
@@ -295,6 +299,15 @@ typedef struct kvr_refresh_request {
                               for both before any later work on it */
   const void* const* v_src;
   int64_t src_head_stride, src_row_stride;
+  int graph_replay;        /* 0: launch every kernel into `stream`. 1: key the call on the model's
+                              weights, the geometry and options and every pointer of the request
+                              and the workspace; a key's second call is captured into a CUDA graph
+                              (on an internal stream, nothing runs during the capture) and that and
+                              later calls with the key launch the graph into `stream` (same kernels
+                              and results; the cuBLAS boundaries drain faster inside a graph).
+                              Kernels read ids, positions, tables, weights and sources at run time,
+                              so staging new values into the same buffers replays with them. Up to 4
+                              graphs per (thread, device); tensor-parallel calls run directly. */
 } kvr_refresh_request;
 #define KVR_PROJ_CUBLAS 0  /* cuBLAS GEMMs, fp32 accumulation */
 #define KVR_PROJ_SM100 1   /* kvr_linear's weight-streaming kernel, gate/up fused with SiLU */

@@ -1,0 +1,130 @@
+"""CUDA-graph replay of repeated refresh requests (``graph_replay``): a
+request that repeats an earlier one's geometry and buffers is captured once
+and replayed, with the bytes of direct launches, with each request's own ids
+and positions, and with its kernels counted."""
+
+import pytest
+import torch
+
+from conftest import load_golden
+from helpers import bits_equal, fixture_model, layers_cpu, to_cache
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+CASES = ["case_qwen3_bf16_d128.pt", "case_llama_bf16_d64.pt"]
+
+
+@pytest.fixture(params=["cublas", "sm100"])
+def projections(request, monkeypatch):
+    from budgeted_kv_cache_repair_b200 import _lib, engine
+
+    monkeypatch.setattr(engine, "PROJECTIONS", {"cublas": _lib.PROJ_CUBLAS, "sm100": _lib.PROJ_SM100}[request.param])
+    return request.param
+
+
+def _setup(name):
+    from budgeted_kv_cache_repair_b200 import OperatorShim
+
+    record = load_golden(name)
+    model = fixture_model(record, DEV)
+    return record, OperatorShim(model), to_cache(record["shifted_layers"], DEV)
+
+
+def _direct(monkeypatch, shim, base, ids, intervals):
+    from budgeted_kv_cache_repair_b200 import engine, packed_interval_repair
+
+    monkeypatch.setattr(engine, "GRAPH_REPLAY", False)
+    out, _ = packed_interval_repair(shim, base, ids, intervals)
+    got = layers_cpu(out)
+    monkeypatch.setattr(engine, "GRAPH_REPLAY", True)
+    return got
+
+
+def _same(a, b):
+    return all(bits_equal(x, y) for pa, pb in zip(a, b) for x, y in zip(pa, pb))
+
+
+def _counters():
+    from budgeted_kv_cache_repair_b200 import _lib
+
+    lib = _lib.load()
+    torch.cuda.synchronize()
+    return lib.kvr_graph_replays(), lib.kvr_kernel_launches()
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_replay_gives_the_bytes_of_direct_launches(name, projections, monkeypatch):
+    from budgeted_kv_cache_repair_b200 import packed_interval_repair
+
+    record, shim, base = _setup(name)
+    ids = record["new_ids"].to(DEV)
+    expect = _direct(monkeypatch, shim, base, ids, record["intervals"])
+    replays0, launches0 = _counters()
+    per_call = []
+    for _ in range(5):
+        before = _counters()[1]
+        out, _ = packed_interval_repair(shim, base, ids, record["intervals"])
+        assert _same(layers_cpu(out), expect)
+        del out  # the next call gets the same output buffers back: same launch key
+        per_call.append(_counters()[1] - before)
+    replays, _ = _counters()
+    # Call 1 runs directly (first sight of the key), call 2 captures and
+    # launches the graph, calls 3-5 replay it.
+    assert replays - replays0 == 4
+    assert len(set(per_call)) == 1 and per_call[0] > 0  # a replay counts the kernels it runs
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_replay_reads_each_requests_ids_and_positions(name, monkeypatch):
+    """Same geometry (rows, last position), other positions and ids: the
+    staged values reach the replayed kernels."""
+    from budgeted_kv_cache_repair_b200 import packed_interval_repair
+
+    record, shim, base = _setup(name)
+    ids_a = record["new_ids"].to(DEV)
+    intervals_a = [tuple(i) for i in record["intervals"]]
+    # Move an inner interval one row earlier (still sorted, disjoint and
+    # non-adjacent; the last row stays) and change the token ids it covers.
+    i = next(j for j in range(1, len(intervals_a) - 1) if intervals_a[j][0] - 1 > intervals_a[j - 1][1])
+    s0, e0 = intervals_a[i]
+    intervals_b = intervals_a[:i] + [(s0 - 1, e0 - 1)] + intervals_a[i + 1:]
+    ids_b = ids_a.clone()
+    ids_b[0, s0 - 1:e0 - 1] = (ids_b[0, s0 - 1:e0 - 1] + 7) % int(shim.generator.config.vocab_size)
+    expect_a = _direct(monkeypatch, shim, base, ids_a, intervals_a)
+    expect_b = _direct(monkeypatch, shim, base, ids_b, intervals_b)
+    assert not _same(expect_a, expect_b)
+    replays0, _ = _counters()
+    for ids, intervals, expect in [(ids_a, intervals_a, expect_a), (ids_a, intervals_a, expect_a),
+                                   (ids_b, intervals_b, expect_b), (ids_a, intervals_a, expect_a),
+                                   (ids_b, intervals_b, expect_b)]:
+        out, _ = packed_interval_repair(shim, base, ids, intervals)
+        assert _same(layers_cpu(out), expect)
+        del out
+    assert _counters()[0] - replays0 == 4
+
+
+def test_held_outputs_are_never_captured(monkeypatch):
+    """Outputs the caller keeps are new buffers each call: every call runs
+    directly and no graph is made."""
+    from budgeted_kv_cache_repair_b200 import packed_interval_repair
+
+    record, shim, base = _setup(CASES[0])
+    ids = record["new_ids"].to(DEV)
+    expect = _direct(monkeypatch, shim, base, ids, record["intervals"])
+    replays0, _ = _counters()
+    kept = [packed_interval_repair(shim, base, ids, record["intervals"])[0] for _ in range(3)]
+    assert _counters()[0] == replays0
+    for out in kept:
+        assert _same(layers_cpu(out), expect)
+
+
+def test_replay_leaves_the_base_cache_untouched(monkeypatch):
+    from budgeted_kv_cache_repair_b200 import packed_interval_repair
+
+    record, shim, base = _setup(CASES[0])
+    snapshot = layers_cpu(base)
+    ids = record["new_ids"].to(DEV)
+    for _ in range(4):
+        out, _ = packed_interval_repair(shim, base, ids, record["intervals"])
+        del out
+    assert _same(layers_cpu(base), snapshot)
