@@ -619,7 +619,11 @@ int refresh_graphed(const kvr_model* model, const kvr_refresh_request* req, void
   cudaGraph_t graph = nullptr;
   err = cudaStreamEndCapture(cp->capture, &graph);
   cudaGraphExec_t exec = nullptr;
-  if (st == KVR_OK && err == cudaSuccess && graph) err = cudaGraphInstantiate(&exec, graph, 0);
+  // Kernel nodes keep the priority of the stream they were captured from (the
+  // layer loop's high one, the copy's low one); without this flag the whole
+  // graph would run at the priority of the stream it is launched into.
+  if (st == KVR_OK && err == cudaSuccess && graph)
+    err = cudaGraphInstantiate(&exec, graph, cudaGraphInstantiateFlagUseNodePriority);
   if (graph) cudaGraphDestroy(graph);
   if (st != KVR_OK || err != cudaSuccess || !exec) {
     if (exec) cudaGraphExecDestroy(exec);
