@@ -402,6 +402,13 @@ static int refresh_direct(const kvr_model* model, const kvr_refresh_request* req
       KVR_TRY(add_rmsnorm_ex(hidden, l ? delta : nullptr, nullptr, 0, 0, 0, w.input_norm, normed, rows, H, H, H, H,
                              m.eps, m.dtype, stream, true));
     QkvParts qkv_parts{};
+    // Layer l of the owned cache must be copied before its K/V scatter. The
+    // wait is a full dependency: on the cuBLAS path it goes on the q/k/v GEMM,
+    // which waits for its predecessor anyway, so that the scatter keeps its
+    // programmatic launch; on the kvr_linear path every kernel is in the
+    // programmatic chain and it stays on the scatter, so that the projection
+    // can start streaming its weights early.
+    if (!lin) KVR_TRY(copied(l));
     if (lin) {
       // q/k/v from separate weights or from row ranges of the stacked matrix.
       const uint8_t* wq = static_cast<const uint8_t*>(w.qkv ? w.qkv : w.q);
@@ -427,7 +434,7 @@ static int refresh_direct(const kvr_model* model, const kvr_refresh_request* req
       KVR_TRY(gemm(h, normed, H, w.k, qkv + qd * 2, qkv_w, rows, kd, H, t));
       KVR_TRY(gemm(h, normed, H, w.v, qkv + (qd + kd) * 2, qkv_w, rows, kd, H, t));
     }
-    KVR_TRY(copied(l));
+    if (lin) KVR_TRY(copied(l));
     KVR_TRY(qkv_rope_scatter_ex(qkv, qkv + qd * 2, qkv + (qd + kd) * 2, qkv_w, qkv_w, qkv_w, w.q_norm, w.k_norm,
                                 m.eps, r.cos_tab, r.sin_tab, r.positions, rows, m.q_heads, m.kv_heads, D,
                                 final ? nullptr : q_rot, r.k_cache[l], r.v_cache[l], r.cache_rows,
