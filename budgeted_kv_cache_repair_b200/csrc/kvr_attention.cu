@@ -672,9 +672,11 @@ inline Plan make_plan(int64_t rows, int hq, int hkv, int64_t max_position) {
   const int64_t base = static_cast<int64_t>(p.tiles) * hkv;
   // One CTA per SM and a per-CTA prologue/epilogue of a few microseconds: with
   // few (head, tile) units, cut the key range into about one wave of chunks;
-  // with many, use ~4 waves so that short and long causal spans balance out.
-  // Chunks hold >= 4 key blocks.
-  const int64_t waves = base >= kNumSMs ? 4 : 1;
+  // with many, use ~6 waves so that short and long causal spans balance out
+  // (config-3 geometry, 352 units: 4/5/6/7/8/12/16 waves measured
+  // 504-516/516/471-476/497/491/518/524 us per call). Chunks hold >= 4 key
+  // blocks.
+  const int64_t waves = base >= kNumSMs ? 6 : 1;
   int64_t cb = (base * blocks + waves * kNumSMs - 1) / (waves * kNumSMs);
   if (cb < 4) cb = 4;
   if (cb > blocks) cb = blocks;
