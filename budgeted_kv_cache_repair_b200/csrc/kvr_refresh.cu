@@ -546,12 +546,35 @@ struct GraphCache {
   std::vector<GraphEntry> entries;
   std::vector<std::vector<uint64_t>> seen;  // oldest first
   uint64_t clock = 0;
+  // Destroys every graph once its latest launch has finished and forgets the
+  // keys; a thread that exits does this for its caches (at process exit the
+  // runtime may already be gone, and its errors are ignored).
+  int release() {
+    cudaError_t first = cudaSuccess;
+    for (GraphEntry& e : entries) {
+      cudaError_t err = cudaEventSynchronize(e.last);
+      if (err == cudaSuccess) err = cudaGraphExecDestroy(e.exec);
+      cudaEventDestroy(e.last);
+      if (first == cudaSuccess) first = err;
+    }
+    entries.clear();
+    seen.clear();
+    (void)cudaGetLastError();
+    if (first != cudaSuccess) {
+      set_last_cuda_error(first);
+      return KVR_ERR_CUDA;
+    }
+    return KVR_OK;
+  }
+  ~GraphCache() { release(); }
 };
 
-GraphCache& graph_cache_for(int dev) {
+std::unordered_map<int, GraphCache>& graph_caches() {
   thread_local std::unordered_map<int, GraphCache> caches;
-  return caches[dev];
+  return caches;
 }
+
+GraphCache& graph_cache_for(int dev) { return graph_caches()[dev]; }
 
 int launch_entry(GraphEntry& e, cudaStream_t s) {
   cudaError_t err = cudaGraphLaunch(e.exec, s);
@@ -674,6 +697,15 @@ int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, v
 }
 
 uint64_t kvr_graph_replays(void) { return __atomic_load_n(&g_replays, __ATOMIC_RELAXED); }
+
+int kvr_release_graphs(void) {
+  int st = KVR_OK;
+  for (auto& entry : graph_caches()) {
+    const int s = entry.second.release();
+    if (st == KVR_OK) st = s;
+  }
+  return st;
+}
 
 int kvr_tp_unique_id(void* out) {
   if (!out) return KVR_ERR_INVALID_ARG;

@@ -145,6 +145,13 @@ class _Staging:
 _staging: "OrderedDict[tuple, _Staging]" = OrderedDict()
 
 
+def release_graphs() -> None:
+    """Drop this thread's cached refresh graphs and the staged request
+    buffers (their device memory returns to torch's allocator)."""
+    _lib.check(_lib.load().kvr_release_graphs(), "release_graphs")
+    _staging.clear()
+
+
 def _staged(device, ids, positions, cos, sin, need) -> _Staging:
     """The staging buffers for this request's geometry on the current stream,
     filled with its values (stream-ordered copies)."""

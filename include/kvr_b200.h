@@ -58,6 +58,10 @@ KVR_API uint64_t kvr_kernel_launches(void);
 /* Packed refreshes this process ran as a CUDA graph (request.graph_replay):
  * the graph launches of captured keys, the capturing call's own included. */
 KVR_API uint64_t kvr_graph_replays(void);
+/* Destroys the calling thread's cached refresh graphs (on every device, each
+ * after its latest launch has finished) and forgets the keys seen once, e.g.
+ * when a model is unloaded; later calls start over (direct, then capture). */
+KVR_API int kvr_release_graphs(void);
 
 /*
  * Output ownership copy of every layer: dst[t][h, n, :] = src[t][h, n, :] for

@@ -14,6 +14,17 @@ DEV = "cuda"
 CASES = ["case_qwen3_bf16_d128.pt", "case_llama_bf16_d64.pt"]
 
 
+@pytest.fixture(autouse=True)
+def _fresh_graph_cache():
+    """Each test starts with no cached graph, so that a graph captured by an
+    earlier test at the same addresses cannot shift the replay counts."""
+    from budgeted_kv_cache_repair_b200 import engine
+
+    engine.release_graphs()
+    yield
+    engine.release_graphs()
+
+
 @pytest.fixture(params=["cublas", "sm100"])
 def projections(request, monkeypatch):
     from budgeted_kv_cache_repair_b200 import _lib, engine
@@ -128,3 +139,55 @@ def test_replay_leaves_the_base_cache_untouched(monkeypatch):
         out, _ = packed_interval_repair(shim, base, ids, record["intervals"])
         del out
     assert _same(layers_cpu(base), snapshot)
+
+
+def test_graphs_of_an_exited_thread_are_released(monkeypatch):
+    """A worker thread captures and replays, then exits (its graphs are
+    destroyed with it); the main thread's next calls are unaffected."""
+    import threading
+
+    from budgeted_kv_cache_repair_b200 import packed_interval_repair
+
+    record, shim, base = _setup(CASES[0])
+    ids = record["new_ids"].to(DEV)
+    expect = _direct(monkeypatch, shim, base, ids, record["intervals"])
+    results = []
+
+    def worker():
+        torch.cuda.set_device(0)
+        for _ in range(3):
+            out, _ = packed_interval_repair(shim, base, ids, record["intervals"])
+            results.append(layers_cpu(out))
+            del out
+
+    replays0, _ = _counters()
+    thread = threading.Thread(target=worker)
+    thread.start()
+    thread.join()
+    assert len(results) == 3 and all(_same(r, expect) for r in results)
+    assert _counters()[0] - replays0 == 2
+    for _ in range(3):
+        out, _ = packed_interval_repair(shim, base, ids, record["intervals"])
+        assert _same(layers_cpu(out), expect)
+        del out
+
+
+def test_release_starts_over(monkeypatch):
+    from budgeted_kv_cache_repair_b200 import engine, packed_interval_repair
+
+    record, shim, base = _setup(CASES[0])
+    ids = record["new_ids"].to(DEV)
+    expect = _direct(monkeypatch, shim, base, ids, record["intervals"])
+
+    def calls(n):
+        start = _counters()[0]
+        for _ in range(n):
+            out, _ = packed_interval_repair(shim, base, ids, record["intervals"])
+            assert _same(layers_cpu(out), expect)
+            del out
+        return _counters()[0] - start
+
+    assert calls(3) == 2  # direct, capture + launch, replay
+    engine.release_graphs()
+    assert calls(1) == 0  # the key is new again: direct
+    assert calls(1) == 1  # captured again
