@@ -37,6 +37,7 @@ them from a graph captured on the second such call.
 
 from __future__ import annotations
 
+import threading
 import weakref
 from collections import OrderedDict
 from dataclasses import dataclass
@@ -128,7 +129,7 @@ PROJECTIONS = _lib.PROJ_CUBLAS
 # Stage request inputs into stable buffers and let the library replay graphs of
 # repeated requests (kvr_refresh_request.graph_replay).
 GRAPH_REPLAY = True
-_STAGING_KEEP = 4
+_STAGING_KEEP = 8
 
 
 class _Staging:
@@ -142,27 +143,36 @@ class _Staging:
         self.workspace = torch.empty(workspace_bytes, dtype=torch.uint8, device=device)
 
 
+# Keyed by (thread, device, stream, geometry): two threads issuing requests on
+# one stream must not stage into the same buffers (the second thread's copies
+# could land between the first thread's copies and its refresh).
 _staging: "OrderedDict[tuple, _Staging]" = OrderedDict()
+_staging_lock = threading.Lock()
 
 
 def release_graphs() -> None:
-    """Drop this thread's cached refresh graphs and the staged request
+    """Drop this thread's cached refresh graphs and its staged request
     buffers (their device memory returns to torch's allocator)."""
     _lib.check(_lib.load().kvr_release_graphs(), "release_graphs")
-    _staging.clear()
+    me = threading.get_ident()
+    with _staging_lock:
+        for key in [k for k in _staging if k[0] == me]:
+            del _staging[key]
 
 
 def _staged(device, ids, positions, cos, sin, need) -> _Staging:
-    """The staging buffers for this request's geometry on the current stream,
-    filled with its values (stream-ordered copies)."""
+    """This thread's staging buffers for the request's geometry on the current
+    stream, filled with its values (stream-ordered copies)."""
     stream = torch.cuda.current_stream(device)
-    key = (device.index, stream.cuda_stream, ids.numel(), positions.numel(), cos.shape[1], cos.dtype, need)
-    st = _staging.pop(key, None)
-    if st is None:
-        st = _Staging(device, ids.numel(), positions.numel(), cos.shape[1], cos.dtype, need)
-        while len(_staging) >= _STAGING_KEEP:
-            _staging.popitem(last=False)
-    _staging[key] = st
+    key = (threading.get_ident(), device.index, stream.cuda_stream, ids.numel(), positions.numel(), cos.shape[1],
+           cos.dtype, need)
+    with _staging_lock:
+        st = _staging.pop(key, None)
+        if st is None:
+            st = _Staging(device, ids.numel(), positions.numel(), cos.shape[1], cos.dtype, need)
+            while len(_staging) >= _STAGING_KEEP:
+                _staging.popitem(last=False)
+        _staging[key] = st
     st.ids.copy_(ids)
     st.positions.copy_(positions)
     st.cos.copy_(cos)

@@ -191,3 +191,43 @@ def test_release_starts_over(monkeypatch):
     engine.release_graphs()
     assert calls(1) == 0  # the key is new again: direct
     assert calls(1) == 1  # captured again
+
+
+def test_threads_on_one_stream_keep_their_own_requests(monkeypatch):
+    """Two threads issue requests of one geometry with different ids and
+    positions on the same stream, interleaved: each gets its own result (the
+    staged inputs are per thread)."""
+    import threading
+
+    from budgeted_kv_cache_repair_b200 import packed_interval_repair
+
+    record, shim, base = _setup(CASES[0])
+    ids_a = record["new_ids"].to(DEV)
+    intervals_a = [tuple(i) for i in record["intervals"]]
+    i = next(j for j in range(1, len(intervals_a) - 1) if intervals_a[j][0] - 1 > intervals_a[j - 1][1])
+    s0, e0 = intervals_a[i]
+    intervals_b = intervals_a[:i] + [(s0 - 1, e0 - 1)] + intervals_a[i + 1:]
+    ids_b = ids_a.clone()
+    ids_b[0, s0 - 1:e0 - 1] = (ids_b[0, s0 - 1:e0 - 1] + 11) % int(shim.generator.config.vocab_size)
+    expect = {"a": _direct(monkeypatch, shim, base, ids_a, intervals_a),
+              "b": _direct(monkeypatch, shim, base, ids_b, intervals_b)}
+    request = {"a": (ids_a, intervals_a), "b": (ids_b, intervals_b)}
+    barrier = threading.Barrier(2)
+    failures = []
+
+    def worker(name):
+        torch.cuda.set_device(0)
+        ids, intervals = request[name]
+        barrier.wait()
+        for _ in range(4):
+            out, _ = packed_interval_repair(shim, base, ids, intervals)
+            if not _same(layers_cpu(out), expect[name]):
+                failures.append(name)
+            del out
+
+    threads = [threading.Thread(target=worker, args=(n,)) for n in ("a", "b")]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not failures, failures
