@@ -691,8 +691,16 @@ extern "C" {
 int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, void* workspace,
                        size_t workspace_bytes, void* stream) {
   if (req && req->graph_replay && req->rows > 0 && !req->tp_comm && valid_model(model) && req->k_cache &&
-      req->v_cache)
-    return refresh_graphed(model, req, workspace, workspace_bytes, stream);
+      req->v_cache) {
+    // The key and cache bookkeeping allocate host memory: no exception may
+    // cross the C ABI.
+    try {
+      return refresh_graphed(model, req, workspace, workspace_bytes, stream);
+    } catch (...) {
+      count_captured_launches(nullptr);
+      return KVR_ERR_CUDA;
+    }
+  }
   return refresh_direct(model, req, workspace, workspace_bytes, stream);
 }
 
