@@ -158,7 +158,9 @@ def synthetic_request(cfg, seed, device):
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons while a region runs."""
+    """nvidia-smi samples of SM clock and throttle reasons while a region runs:
+    one `nvidia-smi -lms 50` process, started (and its first line awaited)
+    before the region; only lines that arrive inside the region are kept."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -167,30 +169,48 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.samples = []
-        self._stop = threading.Event()
+        self._lines = []
+        self._first = threading.Event()
+        self._proc = None
         self._thread = None
+        self._window = (0.0, 0.0)
 
     def __enter__(self):
-        def run():
-            while not self._stop.is_set():
-                try:
-                    out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                         timeout=5).stdout.strip()
-                    if out:
-                        self.samples.append([x.strip() for x in out.split(",")])
-                except (OSError, subprocess.SubprocessError):
-                    return
-                self._stop.wait(0.2)
+        try:
+            self._proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                           "--format=csv,noheader,nounits", "-lms", "50"],
+                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self._proc = None
+            return self
 
-        self._thread = threading.Thread(target=run, daemon=True)
+        def read():
+            for line in self._proc.stdout:
+                line = line.strip()
+                if line:
+                    self._lines.append((time.monotonic(), [x.strip() for x in line.split(",")]))
+                    self._first.set()
+
+        self._thread = threading.Thread(target=read, daemon=True)
         self._thread.start()
+        self._first.wait(timeout=5)
+        self._window = (time.monotonic(), 0.0)
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
-        if self._thread:
-            self._thread.join(timeout=6)
+        end = time.monotonic()
+        self._window = (self._window[0], end)
+        if self._proc is not None:
+            time.sleep(0.06)  # one more sample period: a line for the region's last 50 ms
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+            self._thread.join(timeout=5)
+        begin, end = self._window
+        inside = [f for t, f in self._lines if begin <= t <= end + 0.06]
+        self.samples = inside or [f for t, f in self._lines if t >= begin][:1]
 
     def summary(self):
         if not self.samples:
