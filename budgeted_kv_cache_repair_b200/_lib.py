@@ -74,6 +74,7 @@ SIGNATURES = {
     "kvr_kernel_launches": (ctypes.c_uint64, []),
     "kvr_graph_replays": (ctypes.c_uint64, []),
     "kvr_release_graphs": (_I, []),
+    "kvr_rope_tables": (_I, [_P, _I, _P, _L, _F, _P, _P, _I, _P]),
     "kvr_copy_layers": (_I, [_PP, _PP, _I, _I, _L, _I, _L, _L, _L, _L, _I, _P]),
     "kvr_rope_shift_layers": (_I, [_PP, _PP, _I, _I, _L, _I, _L, _L, _L, _L, _P, _I, _P]),
     "kvr_shift_cache_layers": (_I, [_PP, _PP, _PP, _PP, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L,

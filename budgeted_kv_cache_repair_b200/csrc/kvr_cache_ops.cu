@@ -313,6 +313,35 @@ __global__ void __launch_bounds__(256) embed_rows_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Rotary tables at the selected positions, by the op sequence of the
+// transformers rotary forward (LlamaRotaryEmbedding / Qwen3RotaryEmbedding):
+// freq = inv_freq[i] * float(position) (its K=1 matmul: one fp32 product),
+// cos/sin of the duplicated halves, times attention_scaling, rounded to the
+// element type. cosf/sinf are CUDA's full-precision functions, as torch's
+// elementwise cos/sin kernels call them.
+// ---------------------------------------------------------------------------
+template <class T>
+__global__ void __launch_bounds__(128) rope_tables_kernel(const float* __restrict__ inv_freq, int half,
+                                                          const int64_t* __restrict__ positions, int64_t rows,
+                                                          float scaling, uint16_t* __restrict__ cos_out,
+                                                          uint16_t* __restrict__ sin_out) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // positions may come from the previous kernel
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= rows * half) return;
+  const int64_t r = idx / half;
+  const int i = static_cast<int>(idx - r * half);
+  const float f = __fmul_rn(inv_freq[i], static_cast<float>(positions[r]));
+  const uint16_t c = T::from_f(__fmul_rn(cosf(f), scaling));
+  const uint16_t sn = T::from_f(__fmul_rn(sinf(f), scaling));
+  const int64_t o = r * 2 * half + i;
+  cos_out[o] = c;
+  cos_out[o + half] = c;
+  sin_out[o] = sn;
+  sin_out[o + half] = sn;
+}
+
 }  // namespace kvr
 
 using namespace kvr;
@@ -523,6 +552,24 @@ int kvr_scatter_rows(const void* k_fresh, const void* v_fresh, void* k_cache, vo
       static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), positions, rows, heads,
       vpr, cache_rows, fresh_head_stride, fresh_row_stride, cache_head_stride, cache_row_stride,
       error_count);
+}
+
+int kvr_rope_tables(const float* inv_freq, int half_dim, const int64_t* positions, int64_t rows, float scaling,
+                    void* cos_out, void* sin_out, int dtype, void* stream) {
+  if (!inv_freq || !positions || !cos_out || !sin_out || half_dim <= 0 || rows < 0 || !valid_dtype(dtype))
+    return KVR_ERR_INVALID_ARG;
+  if (!rows) return KVR_OK;
+  const int64_t n = rows * half_dim;
+  if ((n + 127) / 128 > 0x7fffffffLL) return KVR_ERR_UNSUPPORTED;
+  const dim3 grid(static_cast<unsigned>((n + 127) / 128));
+  auto s = static_cast<cudaStream_t>(stream);
+  auto* c = static_cast<uint16_t*>(cos_out);
+  auto* sn = static_cast<uint16_t*>(sin_out);
+  if (dtype == KVR_DTYPE_BF16)
+    return launch_pdl<rope_tables_kernel<BF16>>(grid, dim3(128), 0, s, 1, inv_freq, half_dim, positions, rows, scaling,
+                                                c, sn);
+  return launch_pdl<rope_tables_kernel<F16>>(grid, dim3(128), 0, s, 1, inv_freq, half_dim, positions, rows, scaling, c,
+                                             sn);
 }
 
 int kvr_embed_rows(const void* embed, int64_t vocab, int hidden, const int64_t* ids,

@@ -108,12 +108,25 @@ class ModelView:
                 if not t.is_contiguous():
                     raise ValueError("projection weights must be contiguous")
 
-    def rope_tables(self, positions: torch.Tensor):
-        """cos/sin ``[B, D]`` at absolute positions through the model's own
-        rotary module, exactly as its forward builds position_embeddings."""
-        probe = torch.empty(0, dtype=self.dtype, device=positions.device)
-        cos, sin = self.rotary(probe, positions.unsqueeze(0))
-        return cos[0].contiguous(), sin[0].contiguous()
+    def rope_tables(self, positions: torch.Tensor, out=None):
+        """cos/sin ``[B, D]`` at absolute positions (``kvr_rope_tables``): the
+        op sequence of the model's rotary forward on its own ``inv_freq`` and
+        ``attention_scaling``, in one launch. ``out``: optional ``(cos, sin)``
+        contiguous ``[B, D]`` tensors of the model dtype to write."""
+        inv_freq = self.rotary.inv_freq
+        if inv_freq.numel() * 2 != self.head_dim:
+            raise ValueError("partial rotary embeddings are outside the supported model families")
+        if inv_freq.dtype != torch.float32 or inv_freq.device != positions.device or not inv_freq.is_contiguous():
+            inv_freq = inv_freq.to(device=positions.device, dtype=torch.float32).contiguous()
+        rows = positions.numel()
+        if out is None:
+            out = tuple(torch.empty(rows, self.head_dim, dtype=self.dtype, device=positions.device) for _ in range(2))
+        cos, sin = out
+        _lib.check(_lib.load().kvr_rope_tables(
+            inv_freq.data_ptr(), self.head_dim // 2, positions.data_ptr(), rows,
+            float(getattr(self.rotary, "attention_scaling", 1.0)), cos.data_ptr(), sin.data_ptr(),
+            _lib.dtype_code(self.dtype), _lib.stream_handle(positions.device)), "rope_tables")
+        return cos, sin
 
 
 _views: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
@@ -160,23 +173,22 @@ def release_graphs() -> None:
             del _staging[key]
 
 
-def _staged(device, ids, positions, cos, sin, need) -> _Staging:
+def _staged(view: ModelView, device, ids, positions, need) -> _Staging:
     """This thread's staging buffers for the request's geometry on the current
-    stream, filled with its values (stream-ordered copies)."""
+    stream, filled with its ids, positions and rotary tables (stream-ordered)."""
     stream = torch.cuda.current_stream(device)
-    key = (threading.get_ident(), device.index, stream.cuda_stream, ids.numel(), positions.numel(), cos.shape[1],
-           cos.dtype, need)
+    key = (threading.get_ident(), device.index, stream.cuda_stream, ids.numel(), positions.numel(), view.head_dim,
+           view.dtype, need)
     with _staging_lock:
         st = _staging.pop(key, None)
         if st is None:
-            st = _Staging(device, ids.numel(), positions.numel(), cos.shape[1], cos.dtype, need)
+            st = _Staging(device, ids.numel(), positions.numel(), view.head_dim, view.dtype, need)
             while len(_staging) >= _STAGING_KEEP:
                 _staging.popitem(last=False)
         _staging[key] = st
     st.ids.copy_(ids)
     st.positions.copy_(positions)
-    st.cos.copy_(cos)
-    st.sin.copy_(sin)
+    view.rope_tables(st.positions, out=(st.cos, st.sin))
     return st
 
 
@@ -308,14 +320,13 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
         raise ValueError("every cache layer must share one (head, row) stride pair")
     head_stride, row_stride = strides.pop()
     model = _native_model(view)
-    cos, sin = view.rope_tables(positions)
     k_ptrs = _lib.ptr_array([k for k, _ in layers])
     v_ptrs = _lib.ptr_array([v for _, v in layers])
     request = _lib.RefreshRequest(
         k_cache=k_ptrs, v_cache=v_ptrs, cache_rows=cache_rows, cache_head_stride=head_stride,
         cache_row_stride=row_stride, ids=ids.data_ptr(), id_count=ids.numel(), positions=positions.data_ptr(),
-        rows=rows, max_position=max_position, cos_tab=cos.data_ptr(), sin_tab=sin.data_ptr(),
-        attention_precision=ATTENTION_PRECISION, tp_comm=tp_comm, projections=PROJECTIONS)
+        rows=rows, max_position=max_position, attention_precision=ATTENTION_PRECISION, tp_comm=tp_comm,
+        projections=PROJECTIONS)
     if sources is not None:
         from .cache import uniform_layout
 
@@ -334,12 +345,15 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
     if rows and not need:
         raise ValueError("model geometry is outside the built kernels")
     if GRAPH_REPLAY and rows and tp_comm is None:
-        st = _staged(device, ids, positions, cos, sin, need)
+        st = _staged(view, device, ids, positions, need)
         request.ids, request.positions = st.ids.data_ptr(), st.positions.data_ptr()
         request.cos_tab, request.sin_tab = st.cos.data_ptr(), st.sin.data_ptr()
         request.graph_replay = 1
         workspace = st.workspace
     else:
+        cos, sin = view.rope_tables(positions) if rows else (None, None)
+        if rows:
+            request.cos_tab, request.sin_tab = cos.data_ptr(), sin.data_ptr()
         workspace = torch.empty(need, dtype=torch.uint8, device=device)
     _lib.check(lib.kvr_packed_refresh(model, request, workspace.data_ptr(), need, _lib.stream_handle(device)),
                "packed_refresh")

@@ -123,6 +123,17 @@ KVR_API int kvr_scatter_rows(const void* k_fresh, const void* v_fresh, void* k_c
                      int* error_count, int dtype, void* stream);
 
 /*
+ * Rotary cos/sin tables at the selected positions ([rows, 2*half_dim] each, the
+ * element type), by the op sequence of the transformers rotary forward that
+ * the reference's packed forward calls (LlamaRotaryEmbedding.forward, default
+ * rope type): freq = inv_freq[i] * float(positions[r]) in fp32, cos/sin of
+ * cat(freq, freq), times `scaling` (attention_scaling), cast to the element
+ * type. inv_freq: device fp32 [half_dim].
+ */
+KVR_API int kvr_rope_tables(const float* inv_freq, int half_dim, const int64_t* positions, int64_t rows,
+                            float scaling, void* cos_out, void* sin_out, int dtype, void* stream);
+
+/*
  * Embedding gather of the selected rows (the native forward's embed_tokens on
  * edited_ids.index_select(1, positions), kernels/packed_cache.py:291):
  *   out[r, :] = embed[ids[positions[r]], :]

@@ -355,3 +355,30 @@ def test_attention_c_abi_status_word_and_precision_modes(lib, precision, dim, he
     assert int(ws[:4].view(torch.int32).item()) == 0
     expected = oracle.selected_attention_fp64(q.permute(1, 0, 2)[None].cpu(), k.cpu(), v.cpu(), positions)
     _assert_attention_close(out.permute(1, 0, 2)[None], expected)
+
+
+@pytest.mark.parametrize("arch,theta,dim", [("llama", 500000.0, 128), ("qwen3", 1000000.0, 128),
+                                            ("llama", 10000.0, 64)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rope_tables_are_bit_exact_with_the_rotary_module(arch, theta, dim, dtype):
+    """kvr_rope_tables against the model's own rotary forward (transformers
+    LlamaRotaryEmbedding / Qwen3RotaryEmbedding) at the same positions."""
+    from transformers import LlamaConfig, Qwen3Config
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+
+    from budgeted_kv_cache_repair_b200.engine import ModelView
+
+    cls, rot = (Qwen3Config, Qwen3RotaryEmbedding) if arch == "qwen3" else (LlamaConfig, LlamaRotaryEmbedding)
+    config = cls(hidden_size=dim * 4, num_attention_heads=4, num_key_value_heads=2, head_dim=dim, rope_theta=theta,
+                 max_position_embeddings=131072)
+    module = rot(config=config).to("cuda")
+    gen = torch.Generator().manual_seed(dim)
+    positions = torch.cat((torch.tensor([0, 1, 2, 4095, 131071]),
+                           torch.randint(0, 131072, (3000,), generator=gen))).sort().values.cuda()
+    view = ModelView.__new__(ModelView)  # only the fields rope_tables reads
+    view.rotary, view.head_dim, view.dtype = module, dim, dtype
+    cos, sin = view.rope_tables(positions)
+    probe = torch.empty(0, dtype=dtype, device="cuda")
+    ref_cos, ref_sin = module(probe, positions.unsqueeze(0))
+    assert bits_equal(cos, ref_cos[0].contiguous()) and bits_equal(sin, ref_sin[0].contiguous())
