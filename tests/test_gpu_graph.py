@@ -231,3 +231,41 @@ def test_threads_on_one_stream_keep_their_own_requests(monkeypatch):
     for t in threads:
         t.join()
     assert not failures, failures
+
+
+def _word_tokenizer(words):
+    from tokenizers import Tokenizer
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import WhitespaceSplit
+    from transformers import PreTrainedTokenizerFast
+
+    backend = Tokenizer(WordLevel({w: i for i, w in enumerate(words)}, unk_token="[UNK]"))
+    backend.pre_tokenizer = WhitespaceSplit()
+    return PreTrainedTokenizerFast(tokenizer_object=backend, unk_token="[UNK]")
+
+
+def test_in_place_refresh_of_repair_after_deletion_replays(monkeypatch):
+    """repair_after_deletion refreshes the shifted cache it owns in place (no
+    copy source): repeated calls replay that graph with the direct bytes."""
+    from budgeted_kv_cache_repair_b200 import engine, repair_after_deletion
+    from helpers import to_cache
+
+    record = load_golden("api_llama_bfloat16.pt")
+    tokenizer = _word_tokenizer(record["words"])
+    model = fixture_model(record, DEV)
+    old = to_cache(record["old_layers"], DEV)
+
+    def call():
+        result = repair_after_deletion(model, tokenizer, old, record["original_text"],
+                                       delete_span=tuple(record["delete_span"]), query=record["query"],
+                                       budget_percent=record["budget_percent"])
+        return list(result.selection.positions), layers_cpu(result.cache)
+
+    monkeypatch.setattr(engine, "GRAPH_REPLAY", False)
+    positions, expect = call()
+    monkeypatch.setattr(engine, "GRAPH_REPLAY", True)
+    replays0, _ = _counters()
+    for _ in range(4):
+        got_positions, got = call()
+        assert got_positions == positions and _same(got, expect)
+    assert _counters()[0] - replays0 >= 2
