@@ -69,7 +69,19 @@ CONFIG3 = dict(name="qwen3-8b-shape", arch="qwen3", layers=36, hidden=4096, head
 CONFIG1 = dict(CONFIG, context=2048, delete_at=512, delete=128, intervals=1, rows=64,
                metric="repaired rows/s (packed refresh stage, Llama-3-8B shape, 2048 ctx, 1 interval, 64 rows)",
                workload="config1: Llama-3-8B shape, 2048 ctx, delete 128@512 (N=1920), 1 interval x 64 rows")
-WORKLOADS = {"config1": CONFIG1, "config2": CONFIG, "config3": CONFIG3}
+# The reference benchmark's own geometry (benchmarks/benchmark_refresh.py:
+# 35-61, 176-177): edited length L in {2048, 8192} after deleting 8 tokens at
+# L // 8, a 64-token budget in 1, 4 or 16 intervals placed symmetrically about
+# the middle of the context (--intervals picks the count; 16 by default).
+REF2048 = dict(CONFIG, context=2048 + 8, delete_at=2048 // 8, delete=8, intervals=16, rows=64, placement="midpoint",
+               metric="repaired rows/s (packed refresh stage, Llama-3-8B shape, reference benchmark geometry, "
+                      "2048 ctx, 16 intervals, 64 rows)",
+               workload="reference benchmark geometry: Llama-3-8B shape, 2048 ctx, delete 8@256, 64 rows in 16 "
+                        "intervals about the middle")
+REF8192 = dict(REF2048, context=8192 + 8, delete_at=8192 // 8,
+               metric=REF2048["metric"].replace("2048 ctx", "8192 ctx"),
+               workload=REF2048["workload"].replace("2048 ctx, delete 8@256", "8192 ctx, delete 8@1024"))
+WORKLOADS = {"config1": CONFIG1, "config2": CONFIG, "config3": CONFIG3, "ref2048": REF2048, "ref8192": REF8192}
 # Untimed refresh calls before the timed ones, whatever --warmup asks (more
 # only): enough for every CUDA graph of the repeated request to be captured.
 GRAPH_WARMUP = 6
@@ -123,6 +135,31 @@ def budget_intervals(seed: int, suffix_start: int, length: int, count: int, rows
             for i, s in enumerate(picks)]
 
 
+def midpoint_intervals(length: int, rows: int, count: int):
+    """The reference benchmark's placement (benchmarks/benchmark_refresh.py:
+    35-49): ``count`` intervals of ``rows // count`` tokens, one centred in the
+    context, or starts spread evenly from L/4 to 3L/4 (rounded)."""
+    if rows <= 0 or count <= 0 or rows % count:
+        raise ValueError("rows must be a positive multiple of the interval count")
+    width = rows // count
+    if count == 1:
+        starts = [(length - width) // 2]
+    else:
+        starts = [round(length / 4 + i * length / (2 * (count - 1)) - width / 2) for i in range(count)]
+    intervals = [(a, a + width) for a in starts]
+    if intervals[0][0] < 0 or intervals[-1][1] > length or any(
+            left[1] >= right[0] for left, right in zip(intervals, intervals[1:])):
+        raise ValueError("the intervals do not fit the context separated")
+    return intervals
+
+
+def workload_intervals(cfg, seed: int, length: int):
+    """The workload's selected intervals on an edited prompt of ``length``."""
+    if cfg.get("placement") == "midpoint":
+        return midpoint_intervals(length, cfg["rows"], cfg["intervals"])
+    return budget_intervals(seed, cfg["delete_at"], length, cfg["intervals"], cfg["rows"])
+
+
 def build_model(cfg, seed, device):
     from transformers import LlamaConfig, LlamaForCausalLM, Qwen3Config, Qwen3ForCausalLM
 
@@ -156,7 +193,7 @@ def synthetic_request(cfg, seed, device):
         k = torch.randn(shape, device=device, generator=gen, dtype=torch.float32).to(torch.bfloat16)
         v = (0.5 * torch.randn(shape, device=device, generator=gen, dtype=torch.float32)).to(torch.bfloat16)
         pairs.append((k, v))
-    intervals = budget_intervals(seed, a, new_ids.shape[1], cfg["intervals"], cfg["rows"])
+    intervals = workload_intervals(cfg, seed, new_ids.shape[1])
     return old_ids, new_ids, pairs, intervals
 
 
@@ -324,7 +361,7 @@ def _sample_request(cfg, seed, device, layers):
     shape = (1, cfg["kv_heads"], length, cfg["head_dim"])
     base = [(torch.randn(shape, device=device, generator=gen).to(torch.bfloat16),
              (0.5 * torch.randn(shape, device=device, generator=gen)).to(torch.bfloat16)) for _ in range(layers)]
-    intervals = budget_intervals(seed, cfg["delete_at"], length, cfg["intervals"], cfg["rows"])
+    intervals = workload_intervals(cfg, seed, length)
     return ids, base, [p for a, b in intervals for p in range(a, b)]
 
 
@@ -722,10 +759,12 @@ def main():
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     parser.add_argument("--device", choices=["cpu", "cuda"], default="cpu",
                         help="with --impl reference: cpu (the reference arm) or cuda (the GPU comparator)")
-    parser.add_argument("--workload", choices=["config1", "config2", "config3", "70b-tp"], default="config2",
+    parser.add_argument("--workload", choices=["config1", "config2", "config3", "ref2048", "ref8192", "70b-tp"],
+                        default="config2",
                         help="config2: Llama-3-8B refresh, 8k context, 64 rows (DP replicas when N>1); config1: the "
                              "same at 2k context, one interval; config3: Qwen3-8B, 32k context, 1383 rows (DP "
-                             "replicas); 70b-tp: configs[4], head-sharded")
+                             "replicas); ref2048/ref8192: the reference benchmark's own geometry (8 tokens deleted, "
+                             "64 rows about the middle, --intervals 1/4/16); 70b-tp: configs[4], head-sharded")
     parser.add_argument("--intervals", type=int, default=None,
                         help="re-split the workload's rows into this many intervals (config 2 sweep: 1, 4, 16)")
     args = parser.parse_args()

@@ -44,3 +44,23 @@ def test_config2_interval_sweep(count):
 
 def test_even_split_matches_plain_intervals():
     assert bench.budget_intervals(1, 1024, 7936, 16, 64) == bench.make_intervals(1, 1024, 7936, 16, 4)
+
+
+@pytest.mark.parametrize("name", ["ref2048", "ref8192"])
+@pytest.mark.parametrize("count", [1, 4, 16])
+def test_reference_benchmark_geometry(name, count):
+    """The reference benchmark's placement (benchmarks/benchmark_refresh.py:35-61):
+    8 tokens deleted at L // 8, 64 rows in `count` intervals about the middle,
+    every interval after the deletion."""
+    cfg = bench.workload_config(argparse.Namespace(workload=name, intervals=count))
+    length = cfg["context"] - cfg["delete"]
+    assert length in (2048, 8192) and cfg["delete_at"] == length // 8 and cfg["delete"] == 8
+    intervals = bench.workload_intervals(cfg, 1, length)
+    assert len(intervals) == count
+    _check(intervals, length, 64, cfg["delete_at"])
+    if count == 1:
+        assert intervals == [((length - 64) // 2, (length - 64) // 2 + 64)]
+    else:
+        width = 64 // count
+        assert intervals[0][0] == round(length / 4 - width / 2)
+        assert intervals[-1][1] == round(3 * length / 4 - width / 2) + width
