@@ -64,6 +64,12 @@ def test_native_argument_checks_run_without_a_gpu(built):
     assert lib.kvr_linear_workspace_size(64, 4096, ctypes.byref(gated), 1) == 256 + 512 + 148 * 2 * 64 * 128 * 4
     assert lib.kvr_attention_workspace_size(64, 32, 8, 128, 7936) > 0
     assert lib.kvr_attention_workspace_size(20000, 32, 8, 128, 7936) == 256  # enough tiles: status word only
+    assert lib.kvr_rope_tables(None, 64, None, 4, 1.0, None, None, 0, None) == _lib.ERR_INVALID_ARG
+    assert lib.kvr_rope_tables(256, 64, 256, 4, 1.0, 256, 256, 5, None) == _lib.ERR_INVALID_ARG
+    assert lib.kvr_rope_tables(256, 64, 256, 0, 1.0, 256, 256, 0, None) == _lib.OK  # no rows: no launch
+    # No graph was made in this process: releasing is a no-op and nothing replayed.
+    assert lib.kvr_release_graphs() == _lib.OK
+    assert lib.kvr_graph_replays() == 0
 
 
 def test_refresh_request_source_cache_checks_run_without_a_gpu(built):
