@@ -24,7 +24,7 @@ import torch
 from .cache import OperatorShim, build_halo_cache
 from .packed import make_receipt, refresh_owned_layers
 from .selection import sur_selector
-from .validate import cache_layers
+from .validate import cache_layers, check_model_arithmetic
 
 
 @dataclass(frozen=True)
@@ -130,6 +130,7 @@ def _check_model(model: Any) -> None:
         raise ValueError("repair_after_deletion supports native dense Llama and Qwen3 models")
     if any(module.training for module in model.modules()):
         raise ValueError("call model.eval() before repairing its cache")
+    check_model_arithmetic(model.config, base, "repair")
     device = model.get_input_embeddings().weight.device
     if device.type != "cuda" or any(p.device != device for p in model.parameters()):
         raise ValueError("repair on the B200 engine requires one CUDA device holding the whole model")
@@ -139,6 +140,8 @@ def _check_model(model: Any) -> None:
         raise ValueError("repair does not support per-instance forward overrides")
     if getattr(model, "is_quantized", False):
         raise ValueError("repair does not support quantized models")
+    if any(p.dtype not in (torch.bfloat16, torch.float16) for p in base.parameters()):
+        raise ValueError("repair on the B200 engine requires a bfloat16 or float16 model")
 
 
 @torch.no_grad()
@@ -173,6 +176,8 @@ def repair_after_deletion(model: Any, tokenizer: Any, old_cache: Any, original_t
             raise ValueError("old_cache shape does not match the batch-one original prompt")
         if key.device != old_ids.device or value.device != old_ids.device:
             raise ValueError("cache and model must be on the same device")
+        if key.dtype != value.dtype or key.dtype != model.get_input_embeddings().weight.dtype:
+            raise ValueError("old_cache must hold K/V in the model's dtype")
     edited_text = original_text[:start] + original_text[end:]
     edited_ids = _encode(model, tokenizer, edited_text)
     shim = OperatorShim(model, tokenizer)

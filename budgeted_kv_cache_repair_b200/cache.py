@@ -221,9 +221,7 @@ def build_halo_cache(model: Any, old_cache: Any, old_input_ids: torch.Tensor, ne
     the prefix and the recomputed rows before it, and nothing after it, which
     is the reference's ``run_tokens_from_prefix`` over the prefix cache.
     """
-    old_ids = [int(v) for v in old_input_ids[0].tolist()]
-    new_ids = [int(v) for v in new_input_ids[0].tolist()]
-    alignment = token_alignment(old_ids, new_ids)
+    alignment = token_alignment(old_input_ids[0].cpu().numpy(), new_input_ids[0].cpu().numpy())
     halo = min(max(int(halo_tokens), 0), alignment["suffix"])
     recompute_end = alignment["new_suffix_start"] + halo
     old_tail_start = alignment["old_suffix_start"] + halo

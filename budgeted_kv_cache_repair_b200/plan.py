@@ -22,12 +22,69 @@ BLOCK_M = 16
 BLOCK_N = 64
 
 
+_INT64_MAX = (1 << 63) - 1
+
+
+def _host_length(value) -> int:
+    if isinstance(value, bool) or not isinstance(value, Integral):
+        raise ValueError("logical_length must be a host integer")
+    if not 0 <= int(value) <= _INT64_MAX:
+        raise ValueError("logical_length must fit nonnegative signed int64")
+    return int(value)
+
+
+def scan_positions(positions, length: int) -> tuple[tuple[int, ...], tuple[int, ...], tuple[int, ...]]:
+    """Validate host positions and derive the per-tile key bounds in one pass.
+
+    Each element is classified as it streams by (not an integer, outside
+    ``[0, length)``, not above its predecessor); the pass remembers which
+    kinds of fault it saw and, at the end, reports the most basic one, so the
+    message for a given input is the reference's (kernels/indexed_attention.py:
+    54-76 checks the three kinds in that order over the whole sequence). Tile
+    bounds ride along: a 16-row tile opens at its first row
+    (``full = (p + 1) // 64`` key tiles every row sees) and closes at its last
+    (``total = (p + 64) // 64`` tiles reaching it).
+    """
+    if isinstance(positions, torch.Tensor):
+        raise ValueError("positions must be host integers, not a tensor")
+    try:
+        items = iter(positions)
+    except TypeError as error:
+        raise ValueError("positions must be a sequence of host integers") from error
+    values: list[int] = []
+    full: list[int] = []
+    total: list[int] = []
+    not_int = out_of_range = unordered = False
+    previous = None
+    for index, item in enumerate(items):
+        if isinstance(item, bool) or not isinstance(item, Integral):
+            not_int = True
+            continue
+        p = int(item)
+        out_of_range |= not 0 <= p < length
+        unordered |= previous is not None and p <= previous
+        previous = p
+        values.append(p)
+        if index % BLOCK_M == 0:
+            full.append((p + 1) // BLOCK_N)
+    if not_int:
+        raise ValueError("positions must contain host integers")
+    if out_of_range:
+        raise ValueError("positions must lie within logical_length")
+    if unordered:
+        raise ValueError("positions must be strictly increasing and unique")
+    for last in range(BLOCK_M - 1, len(values) + BLOCK_M - 1, BLOCK_M):
+        total.append((values[min(last, len(values) - 1)] + BLOCK_N) // BLOCK_N)
+    return tuple(values), tuple(full), tuple(total)
+
+
 @dataclass(frozen=True)
 class IndexedPlan:
     """Sorted absolute positions, validated entirely on the CPU.
 
-    Tensor positions are rejected: creating a plan never hides a device-to-host
-    synchronisation (kernels/indexed_attention.py:44-49).
+    The constructor, public fields and error texts are the reference's
+    (kernels/indexed_attention.py:42-110). Tensor positions are rejected:
+    building a plan never hides a device-to-host synchronisation.
     """
 
     positions: Sequence[int]
@@ -36,33 +93,11 @@ class IndexedPlan:
     total_tiles: tuple[int, ...] = field(init=False)
 
     def __post_init__(self):
-        if isinstance(self.logical_length, bool) or not isinstance(self.logical_length, Integral):
-            raise ValueError("logical_length must be a host integer")
-        length = int(self.logical_length)
-        if length < 0 or length > (1 << 63) - 1:
-            raise ValueError("logical_length must fit nonnegative signed int64")
-        if isinstance(self.positions, torch.Tensor):
-            raise ValueError("positions must be host integers, not a tensor")
-        try:
-            original = tuple(self.positions)
-        except TypeError as error:
-            raise ValueError("positions must be a sequence of host integers") from error
-        if any(isinstance(p, bool) or not isinstance(p, Integral) for p in original):
-            raise ValueError("positions must contain host integers")
-        positions = tuple(int(p) for p in original)
-        if any(p < 0 or p >= length for p in positions):
-            raise ValueError("positions must lie within logical_length")
-        if any(a >= b for a, b in zip(positions, positions[1:])):
-            raise ValueError("positions must be strictly increasing and unique")
-        full, total = [], []
-        for row in range(0, len(positions), BLOCK_M):
-            tile = positions[row:row + BLOCK_M]
-            full.append((tile[0] + 1) // BLOCK_N)
-            total.append((tile[-1] + BLOCK_N) // BLOCK_N)
-        object.__setattr__(self, "positions", positions)
-        object.__setattr__(self, "logical_length", length)
-        object.__setattr__(self, "full_prefix_tiles", tuple(full))
-        object.__setattr__(self, "total_tiles", tuple(total))
+        length = _host_length(self.logical_length)
+        positions, full, total = scan_positions(self.positions, length)
+        for name, value in (("positions", positions), ("logical_length", length),
+                            ("full_prefix_tiles", full), ("total_tiles", total)):
+            object.__setattr__(self, name, value)
 
     @property
     def selected_count(self) -> int:

@@ -34,27 +34,40 @@ def cache_layers(cache: Any) -> list[tuple[torch.Tensor, torch.Tensor]]:
     return out
 
 
+# Per-layer rules of the reference's cache check (kernels/executor.py:19-47),
+# in the order it applies them; the first rule a layer breaks names the fault.
+# The messages are the contract, the table is this module's own.
+_LAYER_RULES = (
+    (lambda k, v, n: isinstance(k, torch.Tensor) and isinstance(v, torch.Tensor),
+     "cache layer {i} K/V must be tensors"),
+    (lambda k, v, n: k.ndim == 4 and v.ndim == 4,
+     "cache layer {i} K/V must have rank four"),
+    (lambda k, v, n: k.shape == v.shape and k.dtype == v.dtype and k.device == v.device,
+     "cache layer {i} K/V geometry, dtype, and device must agree"),
+    (lambda k, v, n: k.shape[0] == 1 and k.shape[2] == n,
+     "cache layer {i} must match the single-batch edited token length"),
+    (lambda k, v, n: k.shape[1] > 0 and k.shape[3] > 0 and k.is_floating_point(),
+     "cache layer {i} requires nonempty floating-point KV heads"),
+)
+
+
 def validate_cache(cache: Any, logical_length: int) -> list[tuple[torch.Tensor, torch.Tensor]]:
-    """Rank-4 ``[1, Hkv, N, D]`` floating K/V, identical geometry on every layer
-    (kernels/executor.py:19-47). Returns the layer pairs."""
+    """Rank-4 ``[1, Hkv, N, D]`` floating K/V, one geometry and dtype on every
+    layer. Returns the layer pairs.
+
+    Every layer is run through the rule table; its (shape, dtype) signature
+    must then equal the first layer's.
+    """
     layers = cache_layers(cache)
     if not layers:
         raise ValueError("base_cache must contain at least one K/V layer")
-    expected_shape = expected_dtype = None
+    signatures = set()
     for index, (key, value) in enumerate(layers):
-        if not isinstance(key, torch.Tensor) or not isinstance(value, torch.Tensor):
-            raise ValueError(f"cache layer {index} K/V must be tensors")
-        if key.ndim != 4 or value.ndim != 4:
-            raise ValueError(f"cache layer {index} K/V must have rank four")
-        if key.shape != value.shape or key.dtype != value.dtype or key.device != value.device:
-            raise ValueError(f"cache layer {index} K/V geometry, dtype, and device must agree")
-        if key.shape[0] != 1 or key.shape[2] != logical_length:
-            raise ValueError(f"cache layer {index} must match the single-batch edited token length")
-        if key.shape[1] <= 0 or key.shape[3] <= 0 or not key.is_floating_point():
-            raise ValueError(f"cache layer {index} requires nonempty floating-point KV heads")
-        if expected_shape is None:
-            expected_shape, expected_dtype = key.shape, key.dtype
-        elif key.shape != expected_shape or key.dtype != expected_dtype:
+        broken = next((text for rule, text in _LAYER_RULES if not rule(key, value, logical_length)), None)
+        if broken is not None:
+            raise ValueError(broken.format(i=index))
+        signatures.add((tuple(key.shape), key.dtype))
+        if len(signatures) > 1:
             raise ValueError("cache layers must have regular shapes and matching dtypes")
     return layers
 
@@ -182,21 +195,30 @@ def qualify_model(model: Any, base: Any, layer_count: int, device: torch.device,
     config = model.config
     if config.num_hidden_layers != layer_count or len(base.layers) != layer_count:
         raise ValueError("model and cache layer counts must agree")
+    check_model_arithmetic(config, base, "packed executor")
+    _check_modules(model, base, device, dtype)
+    if getattr(model, "is_quantized", False):
+        raise ValueError("packed executor does not support quantized models")
+
+
+def check_model_arithmetic(config: Any, base: Any, who: str) -> None:
+    """The model features the kernels implement: default fixed RoPE, full
+    attention on every layer, SiLU-gated MLP, bias-free projections
+    (kernels/packed_cache.py:123-163, api.py:148-155). Raises ``ValueError``
+    naming ``who``; reads only the config and module attributes (no device
+    work), so the public API runs it before positional correction."""
     rope = getattr(config, "rope_parameters", None)
     rope_type = rope.get("rope_type", "default") if isinstance(rope, dict) else None
     if rope is None:
         scaling = getattr(config, "rope_scaling", None)
         rope_type = "default" if scaling is None else scaling.get("rope_type", scaling.get("type"))
-    if rope_type != "default" or getattr(base.rotary_emb, "rope_type", "default") != "default":
-        raise ValueError("packed executor supports default fixed RoPE only")
+    if rope_type != "default" or getattr(getattr(base, "rotary_emb", None), "rope_type", "default") != "default":
+        raise ValueError(f"{who} supports default fixed RoPE only")
     if getattr(config, "use_sliding_window", False) or getattr(base, "has_sliding_layers", False):
-        raise ValueError("packed executor requires full attention")
+        raise ValueError(f"{who} requires full attention, not sliding or hybrid attention")
     if any(kind != "full_attention" for kind in getattr(config, "layer_types", []) or []):
-        raise ValueError("packed executor rejects sliding/hybrid attention")
-    _check_modules(model, base, device, dtype)
-    if getattr(model, "is_quantized", False):
-        raise ValueError("packed executor does not support quantized models")
+        raise ValueError(f"{who} requires full attention, not sliding or hybrid attention")
     if getattr(config, "hidden_act", "silu") != "silu":
-        raise ValueError("packed executor implements the SiLU-gated MLP only")
+        raise ValueError(f"{who} implements the SiLU-gated MLP only")
     if getattr(config, "attention_bias", False) or getattr(config, "mlp_bias", False):
-        raise ValueError("packed executor implements bias-free projections only")
+        raise ValueError(f"{who} implements bias-free projections only")

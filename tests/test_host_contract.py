@@ -285,3 +285,49 @@ def test_dynamic_cache_construction_keeps_storage():
     assert cache.get_seq_length() == 5 and len(cache_layers(cache)) == 3
     for (k, v), (k2, v2) in zip(pairs, cache_layers(cache)):
         assert k is k2 and v is v2
+
+
+def _model_fault(model, fault):
+    """The reference's contract faults (tests/test_packed_cache.py:255-288),
+    plus a float32 model, which the B200 engine does not compute in."""
+    from transformers import LlamaForCausalLM
+
+    if fault == "class":
+        class CustomLlama(LlamaForCausalLM):
+            pass
+
+        model.__class__ = CustomLlama
+    elif fault == "training":
+        model.train()
+    elif fault == "rope":
+        model.config.rope_scaling = {"rope_type": "dynamic", "factor": 2.0}
+    elif fault == "sliding":
+        model.config.layer_types = ["full_attention", "sliding_attention"]
+    elif fault == "base_forward":
+        model.model.forward = lambda **kwargs: None
+    elif fault == "activation":
+        model.config.hidden_act = "gelu"
+    elif fault == "dtype":
+        model.float()
+    return model
+
+
+@pytest.mark.parametrize("fault,match", [("class", "native dense"), ("training", "eval"), ("rope", "RoPE"),
+                                         ("sliding", "full attention"), ("activation", "SiLU")])
+def test_api_rejects_unsupported_models_before_any_device_work(fault, match):
+    """repair_after_deletion checks the model class, mode, RoPE type,
+    attention kind and MLP before it tokenises, shifts or selects anything
+    (api.py:135-166): the library launches nothing and the tokenizer is never
+    called."""
+    from budgeted_kv_cache_repair_b200 import _lib, repair_after_deletion
+
+    model = _model_fault(_tiny_model().to(torch.bfloat16), fault)
+
+    def tokenizer(*args, **kwargs):
+        raise AssertionError("the model contract must be checked before tokenisation")
+
+    launches = _lib.load().kvr_kernel_launches()
+    with pytest.raises(ValueError, match=match):
+        repair_after_deletion(model, tokenizer, None, "abcdef", delete_span=(1, 2), query="q")
+    assert _lib.load().kvr_kernel_launches() == launches
+
