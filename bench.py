@@ -28,9 +28,15 @@ request (data parallel, weak scaling).
 
 ``--impl reference`` times the reference's packed path restated on the same
 transformers modules (oracle/hf_packed.py; the reference package itself cannot
-be installed on the GPU box) on all host cores, on a bounded sample of the same
-workload (2 of 32 layers, scaled), on rank 0 only. ``--impl reference --device
-cuda`` times that path on one B200 at full depth (the GPU comparator).
+be installed on the GPU box) on all host cores, at full depth on the same
+request as the B200 arm (same seed, weights, stale cache, positional
+correction and intervals), on rank 0 only.
+
+The B200 arm's line also carries, from its baseline legs: a self-check of its
+refreshed rows against the reference path (the bench exits without a number
+on a mismatch), the reference benchmark's interleaved wall-clock comparison of
+this engine and the reference's packed SDPA path on the same GPU
+(``gpu_comparator``), and the CPU baseline on this run's request.
 """
 
 from __future__ import annotations
@@ -85,10 +91,11 @@ WORKLOADS = {"config1": CONFIG1, "config2": CONFIG, "config3": CONFIG3, "ref2048
 # Untimed refresh calls before the timed ones, whatever --warmup asks (more
 # only): enough for every CUDA graph of the repeated request to be captured.
 GRAPH_WARMUP = 6
-# DRAM bytes of one RoPE-fix launch at config 2, from one ncu capture of a
-# 4-layer case of the same kernel scaled to 32 layers: reads 130.1 MB + writes
-# 79.9 MB, x8 (profiles/shift_cache_config2_traffic.md).
-ROPE_TRAFFIC = int((130.1e6 + 79.9e6) * 8)
+# DRAM traffic of one RoPE-fix launch at config 2 (dram__bytes_read.sum +
+# dram__bytes_write.sum from one ncu capture of the full 32-layer launch of
+# kvr_shift_cache_layers at this geometry; None until such a capture exists).
+ROPE_TRAFFIC = None
+ROPE_TRAFFIC_NOTE = "not captured"
 
 
 def workload_config(args):
@@ -288,6 +295,20 @@ def _barrier(world):
         dist.barrier()
 
 
+def workload_seed(args, rank: int = 0) -> int:
+    """Seed of rank ``rank``'s request (weights, ids, stale cache, intervals)."""
+    return (3 if args.workload == "config3" else 1) + rank
+
+
+def line_config(cfg, world: int, intervals, length: int, seed: int) -> dict:
+    """The ``config`` object of the JSON line; both arms print the same one."""
+    return {"workload": cfg["workload"], "rows": sum(b - a for a, b in intervals), "logical_length": length,
+            "interval_count": len(intervals),
+            "intervals": [list(x) for x in intervals[:4]] + (["..."] if len(intervals) > 4 else []),
+            "seed": seed, "parallelism": f"dp{world}",
+            "l2": "no flush: >= 14 GB of weights stream per step (>> 126 MB L2)"}
+
+
 def _time_attention(cache, intervals, cfg, device, reps=20):
     """kvr_selected_attention alone on layer 0 of the request: (launches, total ms),
     device time of `reps` back-to-back calls replayed from one CUDA graph (a
@@ -331,6 +352,42 @@ def _time_attention(cache, intervals, cfg, device, reps=20):
     return {"selected_attention": (reps, b.elapsed_time(e))}
 
 
+def time_rope_fix(shim, old_pairs, alignment, reps: int = 20) -> float:
+    """Device time of one ``kvr_shift_cache_layers`` launch over every layer
+    of the request (the RoPE fix with the shift-cache compaction), in
+    seconds: ``reps`` back-to-back launches through the C ABI into one
+    preallocated output, between one pair of CUDA events on the launching
+    stream, after two warm-up launches."""
+    from budgeted_kv_cache_repair_b200 import _lib
+    from budgeted_kv_cache_repair_b200.cache import _shift_table, allocate_layers
+
+    lib = _lib.load()
+    k0 = old_pairs[0][0]
+    _, heads, old_rows, dim = k0.shape
+    prefix, old_tail, new_tail = alignment["prefix"], alignment["old_suffix_start"], alignment["new_suffix_start"]
+    new_rows = new_tail + old_rows - old_tail
+    out = allocate_layers(len(old_pairs), heads, new_rows, dim, k0.dtype, k0.device)
+    table = _shift_table(shim, k0, int(alignment["position_shift"]))
+    args = (_lib.ptr_array([k for k, _ in old_pairs]), _lib.ptr_array([v for _, v in old_pairs]),
+            _lib.ptr_array([k for k, _ in out]), _lib.ptr_array([v for _, v in out]), len(old_pairs), heads, dim,
+            new_rows, prefix, old_tail, new_tail, k0.stride(1), k0.stride(2), out[0][0].stride(1),
+            out[0][0].stride(2), table.data_ptr(), 1, _lib.dtype_code(k0.dtype), _lib.stream_handle(k0.device))
+
+    def launch():
+        _lib.check(lib.kvr_shift_cache_layers(*args), "shift_cache_layers")
+
+    launch()
+    launch()
+    torch.cuda.synchronize()
+    b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b.record()
+    for _ in range(reps):
+        launch()
+    e.record()
+    torch.cuda.synchronize()
+    return b.elapsed_time(e) / reps / 1e3
+
+
 def rope_fix_bytes(cfg, new_rows, suffix_rows):
     """Algorithmic bytes: the fused shift kernel reads and writes every kept K
     and V row; the delta-RoPE part alone is the K suffix read + write."""
@@ -352,89 +409,183 @@ def refresh_bytes(cfg, length):
     return weights + 2 * cache + cache, params
 
 
-def _sample_request(cfg, seed, device, layers):
-    """Shifted-cache stand-in (K ~ N(0,1), V ~ N(0,0.5)), edited ids and the
-    benchmark's intervals for ``layers`` layers on ``device``."""
-    gen = torch.Generator(device=device).manual_seed(seed)
-    length = cfg["context"] - cfg["delete"]
-    ids = torch.randint(0, cfg["vocab"], (1, length), device=device, generator=gen)
-    shape = (1, cfg["kv_heads"], length, cfg["head_dim"])
-    base = [(torch.randn(shape, device=device, generator=gen).to(torch.bfloat16),
-             (0.5 * torch.randn(shape, device=device, generator=gen)).to(torch.bfloat16)) for _ in range(layers)]
-    intervals = workload_intervals(cfg, seed, length)
-    return ids, base, [p for a, b in intervals for p in range(a, b)]
+def _summary(samples):
+    ordered = sorted(samples)
+    return {"median": statistics.median(samples), "mean": statistics.mean(samples),
+            "p95": ordered[max(0, -(-95 * len(ordered) // 100) - 1)], "n": len(samples)}
 
 
-def run_cpu_baseline(cfg, sample_layers, threads, seed=0):
-    """The reference's packed path (oracle/hf_packed.py: transformers modules,
-    index_copy_ cache layers, masked SDPA, two-copy clone) on the host cores,
-    on a bounded sample: ``sample_layers`` of the model's layers at full
-    context and rows; rows/s scaled to the full depth."""
+def _row_agreement(actual_layers, expected_layers, positions):
+    """Minimum per-row cosine and largest |difference| of the refreshed K/V
+    rows of the given layers (fp64 on the host)."""
+    pos = torch.tensor(positions)
+    worst_cos, worst_abs = 1.0, 0.0
+    for (ka, va), (ke, ve) in zip(actual_layers, expected_layers):
+        for a, e in ((ka, ke), (va, ve)):
+            ra = a[0].index_select(1, pos.to(a.device)).double().cpu().reshape(-1, a.shape[-1])
+            re = e[0].index_select(1, pos.to(e.device)).double().cpu().reshape(-1, e.shape[-1])
+            cos = torch.nn.functional.cosine_similarity(ra, re, dim=-1)
+            worst_cos = min(worst_cos, float(cos.min()))
+            worst_abs = max(worst_abs, float((ra - re).abs().max()))
+    return worst_cos, worst_abs
+
+
+def _first_layers_view(base, count):
+    """A shallow copy of a LlamaModel/Qwen3Model that runs only its first
+    ``count`` decoder layers (the weights are shared, nothing is copied)."""
+    import copy
+
+    view = copy.copy(base)
+    view._modules = base._modules.copy()
+    view._modules["layers"] = torch.nn.ModuleList(list(base.layers)[:count])
+    view.config = copy.deepcopy(base.config)
+    view.config.num_hidden_layers = count
+    return view
+
+
+# ---------------------------------------------------------------------------
+# Baseline legs. These, and nothing else in the measured path, run the
+# reference's packed path as restated in oracle/hf_packed.py (same
+# transformers modules, index_copy_ cache layers, masked SDPA with repeat_kv,
+# two-copy clone): as the checker of this engine's output, as the timed GPU
+# comparator, and as the CPU baseline.
+# ---------------------------------------------------------------------------
+
+def self_check(model, base_layers, ids, positions, out_layers, check_layers: int = 2):
+    """The engine's refreshed rows of the first ``check_layers`` layers against
+    the reference's packed SDPA path run over those layers on the same GPU
+    (K/V of layer l depend on layers 0..l only), and every unselected row of
+    every layer bit-identical to the base. Returns the verdict dict; ``ok``
+    False means the bench must not print a number."""
+    from oracle.hf_packed import packed_refresh_hf
+
+    view = _first_layers_view(model.model, check_layers)
+    expect = packed_refresh_hf(view, base_layers[:check_layers], ids, positions)
+    cos, diff = _row_agreement(out_layers[:check_layers], expect, positions)
+    keep = torch.ones(ids.shape[-1], dtype=torch.bool, device=ids.device)
+    keep[torch.tensor(positions, device=ids.device)] = False
+    untouched = all(torch.equal(a[:, :, keep].view(torch.int16), b[:, :, keep].view(torch.int16))
+                    for (ka, va), (kb, vb) in zip(out_layers, base_layers) for a, b in ((ka, kb), (va, vb)))
+    return {"layers": check_layers, "against": "reference packed SDPA path on the same GPU",
+            "min_row_cosine": cos, "max_abs_diff": diff, "unselected_rows_bit_identical": untouched,
+            "ok": bool(untouched and cos >= 0.999)}
+
+
+def gpu_comparator(shim, model, shifted, base_layers, ids, intervals, warmups=10, repeats=20, seed=71):
+    """The reference benchmark's timing method (benchmarks/benchmark_refresh.py:
+    106-126: ``warmups`` rounds, then ``repeats`` rounds in a seeded shuffled
+    order, each call between two synchronisations, wall clock) applied to
+    this engine's ``packed_interval_repair`` and to the reference's packed
+    SDPA path on the same GPU, same model, cache, ids and intervals."""
+    import random
+
+    from budgeted_kv_cache_repair_b200 import packed_interval_repair
+    from oracle.hf_packed import packed_refresh_hf
+
+    positions = [p for a, b in intervals for p in range(a, b)]
+    calls = {"b200_engine": lambda: packed_interval_repair(shim, shifted, ids, intervals)[0],
+             "reference_packed_sdpa": lambda: packed_refresh_hf(model.model, base_layers, ids, positions)}
+    names = list(calls)
+    for _ in range(warmups):
+        for name in names:
+            out = calls[name]()
+            torch.cuda.synchronize()
+            del out
+    samples = {name: [] for name in names}
+    rng = random.Random(seed)
+    for _ in range(repeats):
+        order = names.copy()
+        rng.shuffle(order)
+        for name in order:
+            torch.cuda.synchronize()
+            started = time.perf_counter()
+            out = calls[name]()
+            torch.cuda.synchronize()
+            samples[name].append((time.perf_counter() - started) * 1e3)
+            del out
+    ours, ref = _summary(samples["b200_engine"]), _summary(samples["reference_packed_sdpa"])
+    return {"method": f"reference benchmark timing: {warmups} warm-up rounds, {repeats} shuffled interleaved "
+                      f"rounds, synchronize + perf_counter per call (benchmarks/benchmark_refresh.py:106-126)",
+            "ours_ms": ours, "reference_packed_sdpa_ms": ref, "ratio": ref["median"] / ours["median"],
+            "reference_path": "the reference's packed_interval_repair default path (SDPA with the dense mask and "
+                              "repeat_kv, index_copy_ writes, two-copy clone) restated on the same transformers "
+                              "modules (oracle/hf_packed.py)"}
+
+
+def cpu_leg(model, base_layers, ids, positions, layers: int, threads: int, budget_s: float, min_reps: int,
+            max_reps: int, warmups: int = 1):
+    """The reference's packed path on the host cores over the model's first
+    ``layers`` layers: ``warmups`` untimed calls, then timed calls until
+    ``max_reps`` or ``budget_s`` seconds (at least ``min_reps``). Returns (ms
+    per call, reps, output layers of the last call)."""
     from oracle.hf_packed import packed_refresh_hf
 
     torch.set_num_threads(threads)
-    small = dict(cfg, layers=sample_layers)
-    model = build_model(small, seed, torch.device("cpu"))
-    ids, base, positions = _sample_request(cfg, seed, torch.device("cpu"), sample_layers)
-    packed_refresh_hf(model.model, base, ids, positions)  # warm-up
+    view = model.model if layers == len(model.model.layers) else _first_layers_view(model.model, layers)
+    for _ in range(max(1, warmups)):
+        out = packed_refresh_hf(view, base_layers[:layers], ids, positions)
     reps, t0 = 0, time.perf_counter()
-    while True:
-        packed_refresh_hf(model.model, base, ids, positions)
+    while reps < max_reps:
+        del out
+        out = packed_refresh_hf(view, base_layers[:layers], ids, positions)
         reps += 1
-        if time.perf_counter() - t0 > 8.0 or reps >= 5:
+        if reps >= min_reps and time.perf_counter() - t0 > budget_s:
             break
-    per_step = (time.perf_counter() - t0) / reps
-    per_request = per_step * cfg["layers"] / sample_layers
-    return {"value": len(positions) / per_request, "unit": "rows/s", "cores": threads, "kind": "port",
-            "sample": f"{sample_layers} of {cfg['layers']} layers (full context {ids.shape[1]}, {len(positions)} rows), "
-                      f"{reps} timed reps, scaled x{cfg['layers'] / sample_layers:g} to full depth; the reference's "
-                      f"packed path restated on the same transformers modules (oracle/hf_packed.py)",
-            "ms_per_request": per_request * 1e3}
+    return (time.perf_counter() - t0) / reps * 1e3, reps, out
 
 
-def gpu_comparator(args):
-    """The reference's packed SDPA path (oracle/hf_packed.py) on one B200 at
-    full depth: the "reference CUDA SDPA path" the north star compares with.
-    Same workload as our arm; CUDA events around each call, median."""
-    device = torch.device("cuda", 0)
-    cfg = workload_config(args)
-    from oracle.hf_packed import packed_refresh_hf
-
-    model = build_model(cfg, 1, device)
-    ids, base, positions = _sample_request(cfg, 1, device, cfg["layers"])
-    for _ in range(args.warmup):
-        packed_refresh_hf(model.model, base, ids, positions)
-    torch.cuda.synchronize()
-    times = []
-    for _ in range(args.steps):
-        b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        b.record()
-        packed_refresh_hf(model.model, base, ids, positions)
-        e.record()
-        e.synchronize()
-        times.append(b.elapsed_time(e))
-    ms = statistics.median(times)
-    print(json.dumps({"impl": "reference-cuda-comparator", "metric": cfg["metric"], "value": len(positions) / (ms / 1e3),
-                      "unit": "rows/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
-                      "n_gpus": 1, "note": "reference packed SDPA path restated on transformers (oracle/hf_packed.py)"}),
-          flush=True)
+def cpu_sample_layers(cfg) -> int:
+    """Layers the CPU legs run: full depth at a few dozen rows; two layers
+    (scaled to full depth) at configs[3]'s 1383 rows, where one full-depth
+    CPU call takes tens of seconds."""
+    return cfg["layers"] if cfg["rows"] <= 256 else 2
 
 
 def reference_arm(args):
+    """The reference's packed path on the host cores at the workload's
+    config (same seed, weights, stale cache, positional correction and
+    intervals as ``bench.py`` times on the GPU), rank 0 only. Inputs are
+    generated on the GPU exactly as the other arm generates them, then moved
+    to the host; the shifted cache comes from the reference's positional
+    correction restated in oracle/packed_oracle.py (bit-identical to the
+    engine's, untimed)."""
     world, rank, _ = _dist()
     if rank != 0:
         return
+    from oracle import packed_oracle
+
     threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
     cfg = workload_config(args)
-    base = run_cpu_baseline(cfg, sample_layers=2, threads=threads)
-    line = {"impl": "reference", "metric": cfg["metric"], "value": base["value"], "unit": "rows/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["ms_per_request"],
+    seed = workload_seed(args)
+    gen_device = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    model = build_model(cfg, seed, gen_device).cpu()
+    old_ids, new_ids, old_pairs, intervals = synthetic_request(cfg, seed, gen_device)
+    old_ids, new_ids = old_ids.cpu(), new_ids.cpu()
+    old_pairs = [(k.cpu(), v.cpu()) for k, v in old_pairs]
+    if gen_device.type == "cuda":
+        torch.cuda.empty_cache()
+    inv_freq = model.model.rotary_emb.inv_freq.cpu()
+    shifted, _ = packed_oracle.build_shift_cache(old_pairs, old_ids[0].tolist(), new_ids[0].tolist(), inv_freq)
+    del old_pairs
+    positions = [p for a, b in intervals for p in range(a, b)]
+    layers = cpu_sample_layers(cfg)
+    ms, reps, _ = cpu_leg(model, shifted, new_ids, positions, layers, threads, 120.0, 1, args.steps, args.warmup)
+    ms_request = ms * cfg["layers"] / layers
+    value = len(positions) / (ms_request / 1e3)
+    depth = "full depth" if layers == cfg["layers"] else f"{layers} of {cfg['layers']} layers, scaled " \
+                                                         f"x{cfg['layers'] / layers:g}"
+    sample = (f"{reps} timed calls ({depth}) after {args.warmup} untimed calls, {len(positions)} rows, "
+              f"context {new_ids.shape[1]}; the reference's packed path restated on the same transformers modules "
+              f"(oracle/hf_packed.py), torch CPU ops in bf16")
+    line = {"impl": "reference", "metric": cfg["metric"], "value": value, "unit": "rows/s", "n_gpus": world,
+            "steps": reps, "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": ms_request,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded random weights N(0,0.02), ids, stale cache)",
-            "config": {"workload": cfg["workload"], "parallelism": f"dp{world} (rank 0 only)",
-                       "l2": "weights >= 14 GB >> L2"},
-            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "e2e": {"value": base["value"], "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "data": "synthetic (seeded random weights N(0,0.02), ids, stale cache; the same seed and intervals as "
+                    "the B200 arm)" + ("" if gen_device.type == "cuda" else "; generated on the CPU (no GPU here)"),
+            "config": line_config(cfg, world, intervals, new_ids.shape[1], seed),
+            "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -442,6 +593,7 @@ def our_arm(args):
     from budgeted_kv_cache_repair_b200 import OperatorShim, build_halo_cache, packed_interval_repair
     from budgeted_kv_cache_repair_b200 import _lib, engine
     from budgeted_kv_cache_repair_b200 import build as native_build
+    from budgeted_kv_cache_repair_b200.cache import copy_layers, make_cache
     from budgeted_kv_cache_repair_b200.validate import cache_layers
 
     world, rank, local = _dist()
@@ -458,15 +610,14 @@ def our_arm(args):
     native_build.build()
     _lib.load()
     cfg = workload_config(args)
-    seed = (3 if args.workload == "config3" else 1) + rank
+    seed = workload_seed(args, rank)
     model = build_model(cfg, seed, device)
     shim = OperatorShim(model)
     old_ids, new_ids, old_pairs, intervals = synthetic_request(cfg, seed, device)
-    from budgeted_kv_cache_repair_b200.cache import copy_layers, make_cache
-
     old_cache = make_cache(old_pairs)
     length = new_ids.shape[1]
-    rows = sum(b - a for a, b in intervals)
+    selected = [p for a, b in intervals for p in range(a, b)]
+    rows = len(selected)
     hbm, tflops, peak_src = _peaks()
     stream = torch.cuda.current_stream()
 
@@ -474,20 +625,11 @@ def our_arm(args):
     for _ in range(args.warmup):
         shifted, alignment = build_halo_cache(shim, old_cache, old_ids, new_ids, 0)
     torch.cuda.synchronize()
-    from budgeted_kv_cache_repair_b200.cache import shift_layers
-
-    rope_timer = engine.KernelTimer()
     torch.cuda.nvtx.range_push("rope_fix")
-    engine.set_kernel_timer(rope_timer)
-    for _ in range(max(args.steps, 5)):
-        layers = shift_layers(shim, old_pairs, alignment, alignment["new_suffix_start"], alignment["old_suffix_start"])
-        del layers
-    engine.set_kernel_timer(None)
+    rope_t = time_rope_fix(shim, old_pairs, alignment, reps=max(args.steps, 20))
     torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    n_rope, rope_total = rope_timer.totals_ms()["shift_cache_layers"]
     fused_bytes, rope_bytes = rope_fix_bytes(cfg, length, alignment["suffix"])
-    rope_t = rope_total / n_rope / 1e3
+    shifted_layers = cache_layers(shifted)
 
     # ---- refresh stage through the public API ----
     # At least GRAPH_WARMUP untimed calls: a repeated request runs directly
@@ -526,16 +668,38 @@ def our_arm(args):
     ms_per_step = region_ms / args.steps
     value = world * rows * args.steps / (region_ms / 1e3)
 
-    # ---- e2e: host ids in, refreshed rows of the last layer out ----
+    # ---- the same steps with every kernel launched directly (no graph) ----
+    engine.GRAPH_REPLAY = False
+    try:
+        for _ in range(3):
+            out, _ = packed_interval_repair(shim, shifted, ids_dev, intervals)
+            del out
+        torch.cuda.synchronize()
+        _barrier(world)
+        d_begin, d_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d_begin.record(stream)
+        for _ in range(args.steps):
+            out, _ = packed_interval_repair(shim, shifted, ids_dev, intervals)
+            del out
+        d_end.record(stream)
+        torch.cuda.synchronize()
+    finally:
+        engine.GRAPH_REPLAY = True
+    direct_ms = _max_over_ranks(d_begin.elapsed_time(d_end), world) / args.steps
+
+    # ---- e2e: host ids in, every refreshed K/V row of every layer out ----
     host_ids = new_ids.cpu().pin_memory()
-    pos_dev = torch.tensor([p for a, b in intervals for p in range(a, b)], device=device)
-    readback = torch.empty((2, cfg["kv_heads"], rows, cfg["head_dim"]), dtype=torch.bfloat16).pin_memory()
+    pos_dev = torch.tensor(selected, device=device)
+    picked = torch.empty((cfg["layers"], 2, cfg["kv_heads"], rows, cfg["head_dim"]), dtype=torch.bfloat16,
+                         device=device)
+    readback = torch.empty(picked.shape, dtype=picked.dtype).pin_memory()
 
     def e2e_step():
         out, _ = packed_interval_repair(shim, shifted, host_ids, intervals)
-        k_last, v_last = cache_layers(out)[-1]
-        sel = torch.stack((k_last[0].index_select(1, pos_dev), v_last[0].index_select(1, pos_dev)))
-        readback.copy_(sel, non_blocking=True)
+        for l, (k, v) in enumerate(cache_layers(out)):
+            torch.index_select(k[0], 1, pos_dev, out=picked[l, 0])
+            torch.index_select(v[0], 1, pos_dev, out=picked[l, 1])
+        readback.copy_(picked, non_blocking=True)
 
     # The warm-up runs the whole step, readback included: the first
     # index_select loads its CUDA module, which must not land in the timing.
@@ -553,6 +717,22 @@ def our_arm(args):
     e2e_ms = _max_over_ranks(e_begin.elapsed_time(e_end), world) / args.steps
     e2e_value = world * rows / (e2e_ms / 1e3)
 
+    # ---- single-call latency: one call on an idle GPU, host work included ----
+    latency = []
+    for _ in range(10):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out, _ = packed_interval_repair(shim, shifted, ids_dev, intervals)
+        torch.cuda.synchronize()
+        latency.append((time.perf_counter() - t0) * 1e3)
+        del out
+    latency_ms = _max_over_ranks(statistics.median(latency), world)
+
+    # The output the checks read: one more call of the same request.
+    final_out, _ = packed_interval_repair(shim, shifted, ids_dev, intervals)
+    final_layers = cache_layers(final_out)
+    torch.cuda.synchronize()
+
     if rank != 0:
         if world > 1:
             import torch.distributed as dist
@@ -568,15 +748,14 @@ def our_arm(args):
     timer = engine.KernelTimer()
     engine.set_kernel_timer(timer)
     for _ in range(3):
-        copy_layers(cache_layers(shifted))
+        copy_layers(shifted_layers)
     engine.set_kernel_timer(None)
     torch.cuda.synchronize()
     totals = timer.totals_ms()
     totals.update(_time_attention(shifted, intervals, cfg, device))
     kernels = {}
     algo_bytes, params = refresh_bytes(cfg, length)
-    selected = [p for a, b in intervals for p in range(a, b)]
-    step_flops = 2.0 * params * len(selected) * cfg["layers"] + \
+    step_flops = 2.0 * params * rows * cfg["layers"] + \
         4.0 * cfg["heads"] * cfg["head_dim"] * sum(p + 1 for p in selected) * cfg["layers"]
     cache_bytes = 2 * cfg["layers"] * cfg["kv_heads"] * length * cfg["head_dim"] * 2
     if "copy_layers" in totals:
@@ -587,8 +766,8 @@ def our_arm(args):
                                   "note": "isolated launch; overlapped with the refresh inside the API call"}
     if "selected_attention" in totals:
         n, ms = totals["selected_attention"]
-        kv_bytes = 2 * cfg["kv_heads"] * (max(p for a, b in intervals for p in range(a, b)) + 1) * cfg["head_dim"] * 2
-        flops = 4.0 * cfg["heads"] * cfg["head_dim"] * sum(p + 1 for a, b in intervals for p in range(a, b))
+        kv_bytes = 2 * cfg["kv_heads"] * (max(selected) + 1) * cfg["head_dim"] * 2
+        flops = 4.0 * cfg["heads"] * cfg["head_dim"] * sum(p + 1 for p in selected)
         kernels["selected_attention"] = {
             "launches": n, "avg_us": ms / n * 1e3, "kv_bytes_per_launch": kv_bytes,
             "achieved_gbs": kv_bytes / (ms / n / 1e3) / 1e9, "frac_hbm": kv_bytes / (ms / n / 1e3) / 1e9 / hbm,
@@ -597,26 +776,54 @@ def our_arm(args):
             "note": "back-to-back calls on layer 0 of the request replayed from a CUDA graph (L2-warm K/V)"}
     rope_gbs = fused_bytes / rope_t / 1e9
     clocks = sampler.summary()
-    cpu = run_cpu_baseline(cfg, sample_layers=2, threads=os.cpu_count() or 1) if world == 1 and not args.no_cpu else None
+
+    # ---- baseline legs (rank 0): the checker, the GPU comparator, the CPU baseline ----
+    check = self_check(model, shifted_layers, ids_dev, selected, final_layers)
+    if not check["ok"]:
+        print(json.dumps({"error": "self-check failed: the refreshed rows do not match the reference path",
+                          "self_check": check}), file=sys.stderr, flush=True)
+        sys.exit(1)
+    comparator = None
+    if world == 1 and not args.no_comparator:
+        comparator = gpu_comparator(shim, model, shifted, shifted_layers, ids_dev, intervals)
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        layers = cpu_sample_layers(cfg)
+        ours_cpu = [(k.cpu(), v.cpu()) for k, v in final_layers]
+        base_cpu = [(k.cpu(), v.cpu()) for k, v in shifted_layers]
+        del final_out, final_layers
+        model.cpu()
+        torch.cuda.empty_cache()
+        ms, reps, expect = cpu_leg(model, base_cpu, new_ids.cpu(), selected, layers, threads, 15.0, 3, 10)
+        per_request = ms * cfg["layers"] / layers
+        cos, diff = _row_agreement(ours_cpu[:layers], expect, selected)
+        depth = "full depth" if layers == cfg["layers"] else f"{layers} of {cfg['layers']} layers, scaled " \
+                                                             f"x{cfg['layers'] / layers:g}"
+        cpu = {"value": rows / (per_request / 1e3), "unit": "rows/s", "cores": threads, "kind": "port",
+               "sample": f"{reps} timed calls after one untimed call ({depth}), this run's request (same weights, "
+                         f"shifted cache, ids and intervals); the reference's packed path restated on the same "
+                         f"transformers modules (oracle/hf_packed.py), torch CPU ops in bf16",
+               "ms_per_request": per_request,
+               "agreement_with_b200": {"layers": layers, "min_row_cosine": cos, "max_abs_diff": diff}}
+
     line = {
         "metric": cfg["metric"], "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random weights N(0,0.02), ids, stale cache)",
-        "config": {"workload": cfg["workload"],
-                   "rows": rows, "logical_length": length, "intervals": intervals[:4] + ["..."],
-                   "parallelism": f"dp{world}", "l2": "no flush: >= 14 GB of weights stream per step (>> 126 MB L2)",
-                   "refresh_warmup_calls": max(args.warmup, GRAPH_WARMUP)},
-        "refresh_ms": {"median": statistics.median(step_ms), "min": min(step_ms), "max": max(step_ms)},
+        "config": line_config(cfg, world, intervals, length, workload_seed(args)),
+        "refresh_ms": {"median": statistics.median(step_ms), "min": min(step_ms), "max": max(step_ms),
+                       "graph_replay_warmup_calls": max(args.warmup, GRAPH_WARMUP)},
+        "direct_ms_per_step": direct_ms,
+        "single_call_latency_ms": latency_ms,
         "roofline": {"bound": "hbm",
                      "kernel": f"kvr_shift_cache_layers (RoPE fix + shift, {cfg['layers']} layers, 1 launch)",
                      "achieved": rope_gbs, "peak": hbm, "unit": "GB/s", "frac": rope_gbs / hbm,
-                     "traffic": ROPE_TRAFFIC if args.workload == "config2" and not args.intervals else None,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the same kernel on 4 of "
-                                       "the 32 layers (260 MB algorithmic, > L2), scaled x8 "
-                                       "(profiles/shift_cache_config2_traffic.md); writes still in L2 at the end "
-                                       "of the launch are not counted",
+                     "traffic": ROPE_TRAFFIC if args.workload == "config2" else None,
+                     "traffic_source": ROPE_TRAFFIC_NOTE if args.workload == "config2" else None,
                      "algorithmic_bytes": fused_bytes, "rope_only_bytes": rope_bytes,
-                     "avg_us": rope_t * 1e6, "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"},
+                     "avg_us": rope_t * 1e6, "launches_timed": max(args.steps, 20),
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"},
         "step_roofline": {"bound": "hbm" if algo_bytes / hbm / 1e6 >= step_flops / tflops / 1e9 else "tensor",
                           "algorithmic_bytes": algo_bytes, "flops": step_flops,
                           "achieved_gbs": algo_bytes / (ms_per_step / 1e3) / 1e9,
@@ -626,12 +833,19 @@ def our_arm(args):
         "kernels": kernels,
         "e2e": {"value": e2e_value, "unit": "rows/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": int(host_ids.numel() * 8),
-                "d2h_bytes_per_step": int(readback.numel() * 2)},
+                "d2h_bytes_per_step": int(readback.numel() * 2),
+                "note": "host ids (pinned) in; every refreshed K and V row of every layer read back to pinned "
+                        "host memory"},
         "gpu_launches": int(launches),
         "clocks": clocks,
+        "self_check": check,
     }
+    if comparator is not None:
+        line["gpu_comparator"] = comparator
     if cpu is not None:
         line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line["cpu_baseline"]["ms_per_request"] = cpu["ms_per_request"]
+        line["cpu_baseline"]["agreement_with_b200"] = cpu["agreement_with_b200"]
     print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -757,8 +971,8 @@ def main():
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    parser.add_argument("--device", choices=["cpu", "cuda"], default="cpu",
-                        help="with --impl reference: cpu (the reference arm) or cuda (the GPU comparator)")
+    parser.add_argument("--no-comparator", action="store_true",
+                        help="skip the interleaved GPU comparison with the reference's packed SDPA path")
     parser.add_argument("--workload", choices=["config1", "config2", "config3", "ref2048", "ref8192", "70b-tp"],
                         default="config2",
                         help="config2: Llama-3-8B refresh, 8k context, 64 rows (DP replicas when N>1); config1: the "
@@ -770,9 +984,7 @@ def main():
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
-    if args.impl == "reference" and args.device == "cuda":
-        gpu_comparator(args)
-    elif args.impl == "reference":
+    if args.impl == "reference":
         reference_arm(args)
     elif args.workload == "70b-tp":
         tp_arm(args)

@@ -96,6 +96,7 @@ SIGNATURES = {
     "kvr_tp_comm_init": (_I, [_P, _I, _I, ctypes.POINTER(ctypes.c_void_p)]),
     "kvr_tp_comm_destroy": (_I, [_P]),
     "kvr_selected_attention_static": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _I, _I, _P]),
+    "kvr_attention_static_status": (_I, [_P, _P]),
     "kvr_query_relevance_workspace_size": (ctypes.c_size_t, [_I, _I]),
     "kvr_query_relevance": (_I, [_P, _L, _I, _I, _P, _L, _P, _I, _F, _P, _P, ctypes.c_size_t, _P]),
 }

@@ -944,4 +944,22 @@ int kvr_selected_attention_static(const void* q, const void* k_cache, const void
                                 scratch, KVR_STATIC_SCRATCH_BYTES, dtype, stream);
 }
 
+// The status word of the last kvr_selected_attention_static call on the
+// current device, copied on `stream` (one 4-byte cudaMemcpyAsync, no
+// allocation) into `status_out`, which may be host or device memory; the
+// value is there once the stream has reached the copy.
+int kvr_attention_static_status(int* status_out, void* stream) {
+  if (!status_out) return KVR_ERR_INVALID_ARG;
+  void* scratch = nullptr;
+  const int st = scratch_address(&scratch);
+  if (st != KVR_OK) return st;
+  const cudaError_t e =
+      cudaMemcpyAsync(status_out, scratch, sizeof(int), cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return KVR_ERR_CUDA;
+  }
+  return KVR_OK;
+}
+
 }  // extern "C"

@@ -360,8 +360,9 @@ KVR_API int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request
  * cleared on the stream before each launch): calls that overlap on the GPU,
  * on any streams, race. Nothing here calls cudaMalloc, cudaFree or an
  * allocating library routine. Arguments and results otherwise match
- * kvr_selected_attention (the workspace status word lives in the array's
- * first 4 bytes and is not exposed by this variant).
+ * kvr_selected_attention; the status word (0, or the code of a bounded device
+ * wait that gave up, when the output is not valid) lives in the array's first
+ * 4 bytes and kvr_attention_static_status reads it.
  */
 #define KVR_STATIC_SCRATCH_BYTES (16u << 20)
 KVR_API int kvr_selected_attention_static(const void* q, const void* k_cache, const void* v_cache, void* out,
@@ -370,6 +371,11 @@ KVR_API int kvr_selected_attention_static(const void* q, const void* k_cache, co
                                           int64_t cache_head_stride, int64_t cache_row_stride,
                                           int64_t max_position, float scale, int precision,
                                           int dtype, void* stream);
+/* Copies the status word of the last kvr_selected_attention_static call on the
+ * current device into *status_out (host or device memory) with one 4-byte
+ * cudaMemcpyAsync on `stream`; read it after the stream has reached the copy.
+ * Like the variant it serves, it has no counterpart in the reference. */
+KVR_API int kvr_attention_static_status(int* status_out, void* stream);
 
 /*
  * Query relevance of prompt tokens from the frozen input embeddings

@@ -60,8 +60,12 @@ def test_static_scratch_entry_matches_workspace_entry_on_two_calls():
         out = torch.full_like(q, float("nan"))
         lib.check(L.kvr_selected_attention_static(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), *args,
                                                   lib.DTYPE_BF16, stream), "static entry")
+        # The static call's own status word, read through its accessor.
+        status = torch.full((1,), -1, dtype=torch.int32).pin_memory()
+        lib.check(L.kvr_attention_static_status(status.data_ptr(), stream), "static status")
         torch.cuda.synchronize()
         assert int(ws[:4].view(torch.int32).item()) == 0
+        assert int(status.item()) == 0
         assert torch.isfinite(out.float()).all()
         torch.testing.assert_close(out.float(), ref.float(), atol=0.002, rtol=0.02)
         expected = oracle.selected_attention_fp64(q.permute(1, 0, 2)[None].cpu(), k.cpu(), v.cpu(), positions)
