@@ -91,11 +91,13 @@ WORKLOADS = {"config1": CONFIG1, "config2": CONFIG, "config3": CONFIG3, "ref2048
 # Untimed refresh calls before the timed ones, whatever --warmup asks (more
 # only): enough for every CUDA graph of the repeated request to be captured.
 GRAPH_WARMUP = 6
-# DRAM traffic of one RoPE-fix launch at config 2 (dram__bytes_read.sum +
-# dram__bytes_write.sum from one ncu capture of the full 32-layer launch of
-# kvr_shift_cache_layers at this geometry; None until such a capture exists).
-ROPE_TRAFFIC = None
-ROPE_TRAFFIC_NOTE = "not captured"
+# DRAM traffic of one RoPE-fix launch at config 2: dram__bytes_read.sum +
+# dram__bytes_write.sum of one ncu capture (one pass) of the full 32-layer
+# launch of kvr_shift_cache_layers at this geometry (2.080 GB algorithmic).
+ROPE_TRAFFIC = int(1.040e9 + 993.34e6)
+ROPE_TRAFFIC_NOTE = ("ncu dram__bytes_read.sum (1.040 GB, the algorithmic reads) + dram__bytes_write.sum "
+                     "(0.993 GB) of one full 32-layer launch at this geometry; the ~47 MB of writes not counted "
+                     "were still in L2 when the launch ended")
 
 
 def workload_config(args):

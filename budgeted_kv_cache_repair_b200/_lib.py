@@ -16,7 +16,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIBRARY = os.path.join(HERE, "lib", "libkvr_b200.so")
 
-OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_SCRATCH_LIMIT = 0, 1, 2, 3, 4, 5
+OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_SCRATCH_LIMIT, ERR_INJECTED = 0, 1, 2, 3, 4, 5, 6
 STATIC_SCRATCH_BYTES = 16 << 20
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 ATTN_P_SPLIT, ATTN_P_ROUNDED = 0, 1
@@ -97,6 +97,8 @@ SIGNATURES = {
     "kvr_tp_comm_destroy": (_I, [_P]),
     "kvr_selected_attention_static": (_I, [_P, _P, _P, _P, _P, _L, _I, _I, _I, _L, _L, _L, _L, _F, _I, _I, _P]),
     "kvr_attention_static_status": (_I, [_P, _P]),
+    "kvr_set_wait_limit": (_I, [_L]),
+    "kvr_debug_fail_refresh_after_layer": (_I, [_I]),
     "kvr_query_relevance_workspace_size": (ctypes.c_size_t, [_I, _I]),
     "kvr_query_relevance": (_I, [_P, _L, _I, _I, _P, _L, _P, _I, _F, _P, _P, ctypes.c_size_t, _P]),
 }

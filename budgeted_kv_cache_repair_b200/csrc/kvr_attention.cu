@@ -59,7 +59,7 @@ constexpr int THREADS = 352;
 constexpr int SUB = BM * 128;  // one [128 rows x 128 B] swizzled sub-tile
 constexpr int STATUS_BYTES = 256;
 constexpr int kEpilogueBar = 1;        // named barrier of the softmax warps (0 is __syncthreads)
-constexpr long long WAIT_LIMIT = 4000000000LL;  // SM clocks (~2 s)
+constexpr long long WAIT_LIMIT = kDefaultWaitLimit;  // drains of the CTA's own copies and MMAs
 
 enum Err : int { ERR_KV_EMPTY = 1, ERR_Q_FULL, ERR_KV_FULL, ERR_S_FREE, ERR_P_FULL, ERR_S_FULL,
                  ERR_PV_DONE, ERR_DRAIN, ERR_RED, ERR_SMEM_ALIGN };
@@ -77,6 +77,7 @@ struct Args {
   int q_by_tma;   // Q tile fetched by TMA (128 % group == 0) or by cp.async
   float* ws_o;    // [hkv][tiles][nchunks][BM][D] unnormalised O
   float* ws_ml;   // [hkv][tiles][nchunks][BM][2] (running max, sum)
+  long long wait_limit;  // SM clocks before a pipeline wait gives up
 };
 
 template <int D, bool SPLIT>
@@ -257,6 +258,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   // half, [256, 256+D) and [256+D, 256+2D).
   constexpr uint32_t TM_O = 256;
 
+  // Copies this CTA's producer has issued (Q by TMA, K and V blocks): an
+  // aborted CTA waits for them to land before it exits (see the teardown).
+  int issued_k = 0, issued_v = 0;
   if (nblk == 0) {
     // No keys for this tile in this chunk: no role has work, but the combine
     // reads every chunk's (max, sum), so the rows record an empty chunk.
@@ -276,33 +280,23 @@ __global__ void __launch_bounds__(THREADS, 1)
           sm100::tma_load_3d(base + L::Q_OFF + ds * SUB, &tmap_q, q_full, ds * 64, h * G,
                              static_cast<int>(m0 / G));
       }
-      int issued_k = 0, issued_v = 0;
       for (int j = 0; j < nblk; ++j) {
         const int s = j % NS;
         const int key0 = static_cast<int>(k_begin + static_cast<int64_t>(j) * BN);
-        if (j >= NS && !sm100::mbar_wait(k_empty(s), ((j / NS) - 1) & 1, abort, err, ERR_KV_EMPTY, WAIT_LIMIT))
+        if (j >= NS && !sm100::mbar_wait(k_empty(s), ((j / NS) - 1) & 1, abort, err, ERR_KV_EMPTY, a.wait_limit))
           break;
         sm100::mbar_arrive_expect_tx(k_full(s), L::HALF_TX);
 #pragma unroll
         for (int ds = 0; ds < DS; ++ds)
           sm100::tma_load_3d(base + L::K_OFF + (s * DS + ds) * SUB, &tmap_k, k_full(s), ds * 64, key0, h);
         issued_k = j + 1;
-        if (j >= NS && !sm100::mbar_wait(v_empty(s), ((j / NS) - 1) & 1, abort, err, ERR_KV_EMPTY, WAIT_LIMIT))
+        if (j >= NS && !sm100::mbar_wait(v_empty(s), ((j / NS) - 1) & 1, abort, err, ERR_KV_EMPTY, a.wait_limit))
           break;
         sm100::mbar_arrive_expect_tx(v_full(s), L::HALF_TX);
 #pragma unroll
         for (int ds = 0; ds < DS; ++ds)
           sm100::tma_load_3d(base + L::V_OFF + (s * DS + ds) * SUB, &tmap_v, v_full(s), ds * 64, key0, h);
         issued_v = j + 1;
-      }
-      // Never leave the CTA while one of our copies may still land in shared memory.
-      if (*abort) {
-        volatile int keep_waiting = 0;
-        if (a.q_by_tma) sm100::mbar_wait(q_full, 0, &keep_waiting, nullptr, 0, WAIT_LIMIT);
-        for (int j = issued_k > NS ? issued_k - NS : 0; j < issued_k; ++j)
-          sm100::mbar_wait(k_full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
-        for (int j = issued_v > NS ? issued_v - NS : 0; j < issued_v; ++j)
-          sm100::mbar_wait(v_full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
       }
     }
   } else if (warp == kQkWarp) {
@@ -312,11 +306,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       // block j has freed the buffer, never behind a P.V issue (tcgen05.mma
       // issue blocks while the tensor pipe is busy).
       constexpr uint32_t IQK = sm100::idesc_f16(kBF16, BM, BN, false);
-      bool ok = sm100::mbar_wait(q_full, 0, abort, err, ERR_Q_FULL, WAIT_LIMIT);
+      bool ok = sm100::mbar_wait(q_full, 0, abort, err, ERR_Q_FULL, a.wait_limit);
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % NS, b = j & 1;
-        if (!sm100::mbar_wait(k_full(s), (j / NS) & 1, abort, err, ERR_KV_FULL, WAIT_LIMIT)) break;
-        if (j >= 2 && !sm100::mbar_wait(s_free(b), ((j >> 1) - 1) & 1, abort, err, ERR_S_FREE, WAIT_LIMIT)) break;
+        if (!sm100::mbar_wait(k_full(s), (j / NS) & 1, abort, err, ERR_KV_FULL, a.wait_limit)) break;
+        if (j >= 2 && !sm100::mbar_wait(s_free(b), ((j >> 1) - 1) & 1, abort, err, ERR_S_FREE, a.wait_limit)) break;
         sm100::tc_fence_after();
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
@@ -339,8 +333,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       constexpr uint32_t IPV = sm100::idesc_f16(kBF16, BM, D, true);
       for (int j = 0; j < nblk; ++j) {
         const int pb = j & 1;  // P of block j sits in S buffer j & 1
-        if (!sm100::mbar_wait(p_full(pb), (j >> 1) & 1, abort, err, ERR_P_FULL, WAIT_LIMIT)) break;
-        if (!sm100::mbar_wait(v_full(j % NS), (j / NS) & 1, abort, err, ERR_KV_FULL, WAIT_LIMIT)) break;
+        if (!sm100::mbar_wait(p_full(pb), (j >> 1) & 1, abort, err, ERR_P_FULL, a.wait_limit)) break;
+        if (!sm100::mbar_wait(v_full(j % NS), (j / NS) & 1, abort, err, ERR_KV_FULL, a.wait_limit)) break;
         sm100::tc_fence_after();
         const int s = j % NS;
         // P of key half `half`: 32 TMEM columns at pb*BN + half*64 (two 16-bit
@@ -397,7 +391,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int j = 0; j < nblk; ++j) {
       const int b = j & 1;
       // Warp-uniform decisions: tcgen05.ld/st are .sync.aligned.
-      if (!__all_sync(0xffffffffu, sm100::mbar_wait(s_full(b), (j >> 1) & 1, abort, err, ERR_S_FULL, WAIT_LIMIT))) {
+      if (!__all_sync(0xffffffffu, sm100::mbar_wait(s_full(b), (j >> 1) & 1, abort, err, ERR_S_FULL, a.wait_limit))) {
         ok = false;
         break;
       }
@@ -432,7 +426,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (__any_sync(0xffffffffu, rescale)) {
         // This half's O must be final up to block j-1 before it is rescaled in TMEM.
         if (j > 0 && !__all_sync(0xffffffffu, sm100::mbar_wait(pv_done((j - 1) & 1), ((j - 1) >> 1) & 1, abort,
-                                                                err, ERR_PV_DONE, WAIT_LIMIT))) {
+                                                                err, ERR_PV_DONE, a.wait_limit))) {
           ok = false;
           break;
         }
@@ -498,7 +492,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       red[(half * BM + row) * 2 + 0] = m_used;
       red[(half * BM + row) * 2 + 1] = lsum;
       sm100::mbar_arrive(red_bar);
-      ok = __all_sync(0xffffffffu, sm100::mbar_wait(red_bar, 0, abort, err, ERR_RED, WAIT_LIMIT));
+      ok = __all_sync(0xffffffffu, sm100::mbar_wait(red_bar, 0, abort, err, ERR_RED, a.wait_limit));
       if (ok) {
         const float m_o = red[((half ^ 1) * BM + row) * 2 + 0];
         const float l_o = red[((half ^ 1) * BM + row) * 2 + 1];
@@ -509,7 +503,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
     bool ready = ok && __all_sync(0xffffffffu, sm100::mbar_wait(pv_done((nblk - 1) & 1), ((nblk - 1) >> 1) & 1,
-                                                                abort, err, ERR_PV_DONE, WAIT_LIMIT));
+                                                                abort, err, ERR_PV_DONE, a.wait_limit));
     // One decision for all softmax warps (the staging below has a barrier).
     ready = sm100::bar_and_named(kEpilogueBar, kSoftmaxThreads, ready);
     if (ready) {
@@ -573,6 +567,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   sm100::tc_fence_before();
+  __syncthreads();
+  // Every role has stopped; `abort` is final. After an abort, consumers may
+  // have left copies unread: never leave the CTA while one of ours may still
+  // land in shared memory. (Without an abort every copy was waited for.)
+  if (*abort && nblk > 0 && warp == kTmaWarp && lane == 0) {
+    volatile int keep_waiting = 0;
+    if (a.q_by_tma) sm100::mbar_wait(q_full, 0, &keep_waiting, nullptr, 0, WAIT_LIMIT);
+    for (int j = issued_k > NS ? issued_k - NS : 0; j < issued_k; ++j)
+      sm100::mbar_wait(k_full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
+    for (int j = issued_v > NS ? issued_v - NS : 0; j < issued_v; ++j)
+      sm100::mbar_wait(v_full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
+  }
   __syncthreads();
   if (warp == kMmaWarp) {
     sm100::tc_fence_after();
@@ -865,6 +871,7 @@ int selected_attention(const void* q, const void* k_cache, const void* v_cache, 
   a.nchunks = p.nchunks;
   a.chunk = p.chunk;
   a.status = static_cast<int*>(workspace);
+  a.wait_limit = pipeline_wait_limit();
   a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + attn::STATUS_BYTES);
   const size_t units = static_cast<size_t>(kv_heads) * p.tiles * p.nchunks;
   a.ws_ml = a.ws_o + units * attn::BM * head_dim;

@@ -26,6 +26,9 @@ void count_launch() {
   else
     __atomic_add_fetch(&g_launches, 1ull, __ATOMIC_RELAXED);
 }
+long long g_wait_limit = kDefaultWaitLimit;
+long long pipeline_wait_limit() { return __atomic_load_n(&g_wait_limit, __ATOMIC_RELAXED); }
+
 void count_launches(uint64_t n) { __atomic_add_fetch(&g_launches, static_cast<unsigned long long>(n), __ATOMIC_RELAXED); }
 void count_captured_launches(uint64_t* sink) { g_captured = sink; }
 
@@ -398,11 +401,18 @@ const char* kvr_status_string(int status) {
     case KVR_ERR_CUDA: return "CUDA error";
     case KVR_ERR_TIMEOUT: return "bounded device wait timed out";
     case KVR_ERR_SCRATCH_LIMIT: return "needs more scratch than the static device array holds";
+    case KVR_ERR_INJECTED: return "failure injected by a test hook";
     default: return "unknown status";
   }
 }
 
 int kvr_last_cuda_error(void) { return g_last_cuda_error; }
+
+int kvr_set_wait_limit(int64_t cycles) {
+  if (cycles < 0) return KVR_ERR_INVALID_ARG;
+  __atomic_store_n(&g_wait_limit, cycles ? static_cast<long long>(cycles) : kDefaultWaitLimit, __ATOMIC_RELAXED);
+  return KVR_OK;
+}
 
 uint64_t kvr_kernel_launches(void) { return __atomic_load_n(&g_launches, __ATOMIC_RELAXED); }
 

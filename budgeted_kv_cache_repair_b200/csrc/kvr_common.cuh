@@ -19,6 +19,13 @@ void set_last_cuda_error(cudaError_t e);
 void count_launch();
 // Adds n launches at once (the kernels of a replayed CUDA graph).
 void count_launches(uint64_t n);
+// Default limit, in SM clocks (~2 s), of every bounded device wait.
+constexpr long long kDefaultWaitLimit = 4000000000LL;
+// Limit of the pipeline waits (producer/consumer hand-offs) of the kernels
+// launched from now on: kDefaultWaitLimit unless kvr_set_wait_limit changed
+// it. The waits that drain a CTA's own copies and MMAs before it exits always
+// use kDefaultWaitLimit.
+long long pipeline_wait_limit();
 // While `sink` is set, this thread's launches are being captured into a graph
 // (recorded, not run): count_launch() adds to *sink instead. NULL ends it.
 void count_captured_launches(uint64_t* sink);

@@ -63,7 +63,7 @@ constexpr int THREADS = 320;
 constexpr int kMaxSplit = 8;        // portable cluster size
 constexpr int MAX_SEGS = KVR_LINEAR_MAX_SEGMENTS;
 constexpr int STATUS_BYTES = 256;
-constexpr long long WAIT_LIMIT = 4000000000LL;  // SM clocks (~2 s)
+constexpr long long WAIT_LIMIT = kDefaultWaitLimit;  // drains of the CTA's own copies and MMAs
 // Named barriers: 1 + warpgroup (128 threads each), kAllEpi (all 256 epilogue
 // threads), kTmemBar (every warp but the producer, after TMEM allocation).
 constexpr int kAllEpi = 3;
@@ -122,6 +122,7 @@ struct Args {
   int* status;
   int* counters;    // [tiles - dp_tiles]
   float* partials;  // [sk_grid][2 slots][BN / 4][128][4]
+  long long wait_limit;  // SM clocks before a pipeline wait gives up
 };
 
 struct Maps {
@@ -306,6 +307,9 @@ __global__ void __launch_bounds__(THREADS, 1) linear_kernel(const __grid_constan
     tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   }
 
+  // Stages this CTA's producer has filled (each with its weight and x tiles
+  // issued): an aborted CTA waits for them to land before it exits.
+  int it = 0;
   if (warp == kTmaWarp) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
@@ -315,7 +319,7 @@ __global__ void __launch_bounds__(THREADS, 1) linear_kernel(const __grid_constan
         if (seg_at(a, i).paired) sm100::prefetch_tmap(&maps.w[2 * i + 1]);
       }
       Cursor cur = make_cursor(a, b);
-      int it = 0, t, c0, c1;
+      int t, c0, c1;
       bool ok = true;
       // The first NS stages get their weight tiles before the previous kernel
       // has finished (weights are never written); their x tiles, which that
@@ -336,7 +340,7 @@ __global__ void __launch_bounds__(THREADS, 1) linear_kernel(const __grid_constan
         for (int c = c0; c < c1; ++c, ++it) {
           if (!waited && it == NS) release_x();
           const int s = it % NS;
-          if (it >= NS && !sm100::mbar_wait(empty(s), ((it / NS) - 1) & 1, abort, err, ERR_EMPTY, WAIT_LIMIT)) {
+          if (it >= NS && !sm100::mbar_wait(empty(s), ((it / NS) - 1) & 1, abort, err, ERR_EMPTY, a.wait_limit)) {
             ok = false;
             break;
           }
@@ -353,12 +357,6 @@ __global__ void __launch_bounds__(THREADS, 1) linear_kernel(const __grid_constan
         }
       }
       if (!waited) release_x();
-      // Never leave the CTA while one of our copies may still land in shared memory.
-      if (*abort) {
-        volatile int keep_waiting = 0;
-        for (int j = it > NS ? it - NS : 0; j < it; ++j)
-          sm100::mbar_wait(full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
-      }
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
@@ -370,12 +368,12 @@ __global__ void __launch_bounds__(THREADS, 1) linear_kernel(const __grid_constan
       for (; ok && cur.next(t, c0, c1); ++job) {
         const int buf = job & 1;
         if (job >= 2 &&
-            !sm100::mbar_wait(acc_empty(buf), ((job >> 1) - 1) & 1, abort, err, ERR_ACC_EMPTY, WAIT_LIMIT))
+            !sm100::mbar_wait(acc_empty(buf), ((job >> 1) - 1) & 1, abort, err, ERR_ACC_EMPTY, a.wait_limit))
           break;
         sm100::tc_fence_after();
         for (int c = c0; c < c1; ++c, ++it) {
           const int s = it % NS;
-          if (!sm100::mbar_wait(full(s), (it / NS) & 1, abort, err, ERR_FULL, WAIT_LIMIT)) {
+          if (!sm100::mbar_wait(full(s), (it / NS) & 1, abort, err, ERR_FULL, a.wait_limit)) {
             ok = false;
             break;
           }
@@ -412,7 +410,7 @@ __global__ void __launch_bounds__(THREADS, 1) linear_kernel(const __grid_constan
     for (; cur.next(t, c0, c1); ++job) {
       const int buf = job & 1;
       // One decision for all eight warps (they meet at named barriers below).
-      const bool ready = sm100::mbar_wait(acc_full(buf), (job >> 1) & 1, abort, err, ERR_ACC_FULL, WAIT_LIMIT);
+      const bool ready = sm100::mbar_wait(acc_full(buf), (job >> 1) & 1, abort, err, ERR_ACC_FULL, a.wait_limit);
       if (!sm100::bar_and_named(kAllEpi, kEpiThreads, ready)) break;
       sm100::tc_fence_after();
       const Segment sg = seg_at(a, seg_index(a, t));
@@ -573,8 +571,12 @@ __global__ void __launch_bounds__(THREADS, 1) linear_kernel(const __grid_constan
       sm100::bulk_commit();
     }
     if (warp < kEpiWarps) {
-      const bool got = sm100::mbar_wait(red_full, 0, abort, err, ERR_REDUCE, WAIT_LIMIT);
-      if (sm100::bar_and_named(kAllEpi, kEpiThreads, got)) {
+      // Every peer sends its slices once past the barrier above, aborted or
+      // not, so this waits for them in any case: they must land before the
+      // CTA may exit.
+      volatile int keep_waiting = 0;
+      const bool got = sm100::mbar_wait(red_full, 0, &keep_waiting, err, ERR_REDUCE, WAIT_LIMIT);
+      if (sm100::bar_and_named(kAllEpi, kEpiThreads, got && !*abort)) {
         const float* part = reinterpret_cast<const float*>(gbase);
         const float* rcv = reinterpret_cast<const float*>(gbase + L::PART_BYTES);
         const int slot_f = static_cast<int>(slice_bytes / 4);
@@ -618,6 +620,15 @@ __global__ void __launch_bounds__(THREADS, 1) linear_kernel(const __grid_constan
   }
 
   sm100::tc_fence_before();
+  __syncthreads();
+  // Every role has stopped; `abort` is final. After an abort, consumers may
+  // have left stages unread: never leave the CTA while one of our copies may
+  // still land in shared memory. (Without an abort every stage was waited for.)
+  if (*abort && warp == kTmaWarp && lane == 0) {
+    volatile int keep_waiting = 0;
+    for (int j = it > NS ? it - NS : 0; j < it; ++j)
+      sm100::mbar_wait(full(j % NS), (j / NS) & 1, &keep_waiting, nullptr, 0, WAIT_LIMIT);
+  }
   __syncthreads();
   if (warp == kMmaWarp) {
     sm100::tc_fence_after();
@@ -883,6 +894,7 @@ int linear_forward(const void* x, int64_t x_stride, int64_t rows, int64_t k, con
   a.status = reinterpret_cast<int*>(ws);
   a.counters = reinterpret_cast<int*>(ws + lin::STATUS_BYTES);
   a.partials = reinterpret_cast<float*>(ws + need - lin::partial_bytes(p));
+  a.wait_limit = pipeline_wait_limit();
   if (!counters_zeroed) {
     const cudaError_t e = cudaMemsetAsync(ws, 0, need - lin::partial_bytes(p), stream);
     if (e != cudaSuccess) {

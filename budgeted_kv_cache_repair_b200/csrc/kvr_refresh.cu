@@ -220,6 +220,10 @@ int allreduce(void* buf, int64_t count, int dtype, void* comm, cudaStream_t s) {
   return st == ncclSuccess ? KVR_OK : KVR_ERR_CUDA;
 }
 
+// Test hook (kvr_debug_fail_refresh_after_layer): the layer after whose K/V
+// scatter this thread's next refresh reports KVR_ERR_INJECTED; -1 when unarmed.
+thread_local int g_fail_after_layer = -1;
+
 bool valid_model(const kvr_model* m) {
   if (!m || !m->layers || !m->embed || m->num_layers <= 0 || m->num_layers > KVR_MAX_LAYER_TENSORS / 2) return false;
   if (m->hidden <= 0 || m->hidden % 8 || m->q_heads <= 0 || m->kv_heads <= 0 || m->q_heads % m->kv_heads) return false;
@@ -440,6 +444,12 @@ static int refresh_direct(const kvr_model* model, const kvr_refresh_request* req
                                 final ? nullptr : q_rot, r.k_cache[l], r.v_cache[l], r.cache_rows,
                                 r.cache_head_stride, r.cache_row_stride, nullptr, m.dtype, stream,
                                 defer ? &qkv_parts : nullptr, true));
+    if (l == g_fail_after_layer) {
+      // Injected failure: layer l of the owned cache is written, the rest of
+      // the call is not issued, as after a CUDA call failing part-way.
+      g_fail_after_layer = -1;
+      return KVR_ERR_INJECTED;
+    }
     if (final) break;
     KVR_TRY(selected_attention(q_rot, r.k_cache[l], r.v_cache[l], attn, r.positions, rows, m.q_heads, m.kv_heads,
                                D, r.cache_rows, r.cache_head_stride, r.cache_row_stride, r.max_position, scale,
@@ -688,8 +698,14 @@ int refresh_graphed(const kvr_model* model, const kvr_refresh_request* req, void
 
 extern "C" {
 
+int kvr_debug_fail_refresh_after_layer(int layer) {
+  g_fail_after_layer = layer < 0 ? -1 : layer;
+  return KVR_OK;
+}
+
 int kvr_packed_refresh(const kvr_model* model, const kvr_refresh_request* req, void* workspace,
                        size_t workspace_bytes, void* stream) {
+  if (g_fail_after_layer >= 0) return refresh_direct(model, req, workspace, workspace_bytes, stream);
   if (req && req->graph_replay && req->rows > 0 && !req->tp_comm && valid_model(model) && req->k_cache &&
       req->v_cache) {
     // The key and cache bookkeeping allocate host memory: no exception may

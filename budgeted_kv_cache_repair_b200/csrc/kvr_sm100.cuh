@@ -43,14 +43,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// Non-blocking test of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Limits below this many SM clocks (~0.5 ms) poll with the non-blocking test,
+// so that the limit, not the hardware's suspend window of try_wait, decides
+// when a wait gives up (short limits are set on purpose, to exercise the
+// give-up path).
+constexpr long long kPollLimit = 1000000LL;
+
 // Bounded wait: gives up after `limit_cycles` SM clocks or as soon as another
 // thread of the CTA has raised `*abort` (shared), then reports failure.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           int* error, int code, long long limit_cycles) {
-  if (mbar_try_wait(bar, parity)) return true;
+  const bool poll = limit_cycles < kPollLimit;
+  if (poll ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (poll ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
     if (clock64() - start > limit_cycles) {
       *abort = 1;

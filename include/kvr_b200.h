@@ -37,6 +37,7 @@ extern "C" {
 #define KVR_ERR_CUDA 3          /* a CUDA runtime call failed; see kvr_last_cuda_error */
 #define KVR_ERR_TIMEOUT 4       /* a bounded device wait gave up */
 #define KVR_ERR_SCRATCH_LIMIT 5 /* problem needs more than the static scratch array holds */
+#define KVR_ERR_INJECTED 6      /* failure injected by kvr_debug_fail_refresh_after_layer */
 
 #define KVR_DTYPE_BF16 0
 #define KVR_DTYPE_F16 1
@@ -58,6 +59,21 @@ KVR_API uint64_t kvr_kernel_launches(void);
 /* Packed refreshes this process ran as a CUDA graph (request.graph_replay):
  * the graph launches of captured keys, the capturing call's own included. */
 KVR_API uint64_t kvr_graph_replays(void);
+/* Diagnostics for failure handling; neither has a counterpart in the
+ * reference, whose tests inject failures by patching Python (tests/
+ * test_packed_cache.py:227-252).
+ * kvr_set_wait_limit: SM clocks after which the pipeline waits of the kernels
+ * launched from now on (attention, projections) give up and record an error
+ * code in their workspace status word; 0 restores the default (~2 s). The
+ * waits in which a CTA drains its own copies and MMAs before exiting keep the
+ * default, so an early give-up still leaves nothing in flight. Process-wide.
+ * kvr_debug_fail_refresh_after_layer: the calling thread's next
+ * kvr_packed_refresh returns KVR_ERR_INJECTED right after launching layer
+ * `layer`'s K/V scatter (the owned output cache is then partly written), the
+ * way a CUDA call failing part-way through would end it; that call runs
+ * directly, never from a cached graph. A negative layer disarms it. */
+KVR_API int kvr_set_wait_limit(int64_t cycles);
+KVR_API int kvr_debug_fail_refresh_after_layer(int layer);
 /* Destroys the calling thread's cached refresh graphs (on every device, each
  * after its latest launch has finished) and forgets the keys seen once, e.g.
  * when a model is unloaded; later calls start over (direct, then capture). */
