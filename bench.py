@@ -611,6 +611,9 @@ def our_arm(args):
     torch.cuda.set_device(device)
     native_build.build()
     _lib.load()
+    if args.projections != "default":
+        engine.PROJECTIONS = {"cublas": _lib.PROJ_CUBLAS, "sm100": _lib.PROJ_SM100,
+                              "fused": _lib.PROJ_FUSED}[args.projections]
     cfg = workload_config(args)
     seed = workload_seed(args, rank)
     model = build_model(cfg, seed, device)
@@ -981,6 +984,8 @@ def main():
                              "same at 2k context, one interval; config3: Qwen3-8B, 32k context, 1383 rows (DP "
                              "replicas); ref2048/ref8192: the reference benchmark's own geometry (8 tokens deleted, "
                              "64 rows about the middle, --intervals 1/4/16); 70b-tp: configs[4], head-sharded")
+    parser.add_argument("--projections", choices=["default", "cublas", "sm100", "fused"], default="default",
+                        help="projection path of the layer loop (default: the engine's)")
     parser.add_argument("--intervals", type=int, default=None,
                         help="re-split the workload's rows into this many intervals (config 2 sweep: 1, 4, 16)")
     args = parser.parse_args()

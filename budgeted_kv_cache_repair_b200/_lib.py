@@ -57,7 +57,7 @@ class RefreshRequest(ctypes.Structure):
 
 
 LINEAR_MAX_SEGMENTS = 4
-PROJ_CUBLAS, PROJ_SM100 = 0, 1
+PROJ_CUBLAS, PROJ_SM100, PROJ_FUSED = 0, 1, 2
 
 
 class LinearSegment(ctypes.Structure):

@@ -34,6 +34,7 @@
 
 #include "kvr_common.cuh"
 #include "kvr_linear.h"
+#include "kvr_proj.h"
 
 namespace kvr {
 namespace {
@@ -43,10 +44,18 @@ constexpr size_t kAlign = 256;
 inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct Buffers {
-  bool lin;  // room for the sm_100a projection kernel (rows <= kMaxRows)
+  bool lin;   // room for the sm_100a projection kernel (rows <= kMaxRows)
+  bool fused; // room for the fused projections (rows <= kProjMaxRows, head_dim 128)
   size_t hidden, normed, delta, qkv, q_rot, attn, gate, up, act, lin_ws, lin_bytes, lin_zero, parts, attn_ws, total;
+  size_t proj_ws, proj_bytes, proj_zero, ssq;
   int max_split;  // slices the deferred-projection buffer holds
 };
+
+// The fused projections' geometry rule: head_dim 128 (one tile per head),
+// hidden a multiple of 128 (whole residual tiles), at most kProjMaxRows rows.
+bool fused_geometry(const kvr_model* m, int64_t rows) {
+  return rows <= kProjMaxRows && m->head_dim == 128 && m->hidden % 128 == 0 && m->intermediate % 8 == 0;
+}
 
 // Workspace of the projection launches of one layer: the largest of the four
 // (q/k/v, o, gate/up, down); every launch leaves its counters zero, so one
@@ -118,6 +127,21 @@ Buffers layout(const kvr_model* m, int64_t rows, int64_t cache_rows) {
     need(s_down, H);
   }
   b.parts = take(parts_floats * sizeof(float));
+  // Fused projections: one workspace for the four launches of a layer (the
+  // largest tile count: q/k/v heads, hidden / 128 or intermediate / 64) and
+  // the per-tile row sums of squares of the residual stream.
+  b.fused = fused_geometry(m, rows);
+  b.proj_bytes = b.proj_zero = 0;
+  int64_t proj_tiles_max = 0;
+  if (b.fused) {
+    proj_tiles_max = static_cast<int64_t>(m->q_heads) + 2 * m->kv_heads;
+    if (m->hidden / 128 > proj_tiles_max) proj_tiles_max = m->hidden / 128;
+    if ((m->intermediate + 63) / 64 > proj_tiles_max) proj_tiles_max = (m->intermediate + 63) / 64;
+    b.proj_bytes = proj_workspace_bytes(rows, proj_tiles_max);
+    b.proj_zero = proj_zero_bytes(proj_tiles_max);
+  }
+  b.proj_ws = take(b.proj_bytes);
+  b.ssq = take(b.fused ? static_cast<size_t>(m->hidden / 128) * kProjMaxRows * sizeof(float) : 0);
   b.attn_ws = take(kvr_attention_workspace_size(rows, m->q_heads, m->kv_heads, m->head_dim, cache_rows));
   b.total = off;
   return b;
@@ -281,7 +305,8 @@ static int refresh_direct(const kvr_model* model, const kvr_refresh_request* req
       r.max_position >= r.cache_rows)
     return KVR_ERR_INVALID_ARG;
   if (r.rows > 0x7fffffffLL) return KVR_ERR_UNSUPPORTED;
-  if (r.projections != KVR_PROJ_CUBLAS && r.projections != KVR_PROJ_SM100) return KVR_ERR_INVALID_ARG;
+  if (r.projections != KVR_PROJ_CUBLAS && r.projections != KVR_PROJ_SM100 && r.projections != KVR_PROJ_FUSED)
+    return KVR_ERR_INVALID_ARG;
   const Buffers b = layout(&m, r.rows, r.cache_rows);
   if (!workspace || workspace_bytes < b.total || !aligned16(workspace)) return KVR_ERR_INVALID_ARG;
 
@@ -319,6 +344,9 @@ static int refresh_direct(const kvr_model* model, const kvr_refresh_request* req
 
   void* lin_ws = ws + b.lin_ws;
   float* parts = reinterpret_cast<float*>(ws + b.parts);
+  // Fused projections (requests outside their geometry or tensor-parallel run
+  // on cuBLAS instead).
+  const bool fused = b.fused && r.projections == KVR_PROJ_FUSED && !r.tp_comm;
   const bool lin = b.lin && r.projections == KVR_PROJ_SM100;
   // Deferred reduction of q/k/v, o and down (their consumers sum the fp32
   // slices); the tensor-parallel all-reduce needs the rounded sums, so there
@@ -346,6 +374,7 @@ static int refresh_direct(const kvr_model* model, const kvr_refresh_request* req
   {
     cudaError_t e = cudaMemsetAsync(attn_ws, 0, sizeof(int), s);
     if (e == cudaSuccess && lin) e = cudaMemsetAsync(lin_ws, 0, b.lin_zero, s);
+    if (e == cudaSuccess && fused) e = cudaMemsetAsync(ws + b.proj_ws, 0, b.proj_zero, s);
     if (e != cudaSuccess) {
       set_last_cuda_error(e);
       return KVR_ERR_CUDA;
@@ -396,6 +425,116 @@ static int refresh_direct(const kvr_model* model, const kvr_refresh_request* req
 
   KVR_TRY(kvr_embed_rows(m.embed, m.vocab, H, r.ids, r.id_count, r.positions, rows, hidden, nullptr, m.dtype,
                          stream));
+  if (fused) {
+    // Four fused projection launches and the attention per layer; layer 0's
+    // input norm is the one separate RMSNorm (no residual sums exist yet).
+    void* proj_ws = ws + b.proj_ws;
+    float* ssq = reinterpret_cast<float*>(ws + b.ssq);
+    const int ssq_tiles = H / 128;
+    KVR_TRY(add_rmsnorm_ex(hidden, nullptr, nullptr, 0, 0, 0, m.layers[0].input_norm, normed, rows, H, H, H, H,
+                           m.eps, m.dtype, stream, true));
+    // The four projections of layer l, in launch order.
+    auto qkv_params = [&](int l) {
+      const kvr_layer_weights& w = m.layers[l];
+      const bool final = l == m.num_layers - 1;
+      const uint8_t* wq = static_cast<const uint8_t*>(w.qkv ? w.qkv : w.q);
+      ProjParams qp{};
+      qp.epilogue = PROJ_QKV_ROPE;
+      qp.dtype = m.dtype;
+      qp.rows = rows;
+      qp.k = H;
+      qp.x = l == 0 ? normed : hidden;
+      qp.x_stride = H;
+      if (l > 0) {
+        qp.norm_w = w.input_norm;
+        qp.ssq_in = ssq;
+        qp.ssq_tiles = ssq_tiles;
+      }
+      qp.eps = m.eps;
+      qp.w[0] = final ? nullptr : wq;
+      qp.w[1] = w.qkv ? static_cast<const void*>(wq + qd * H * 2) : w.k;
+      qp.w[2] = w.qkv ? static_cast<const void*>(wq + (qd + kd) * H * 2) : w.v;
+      qp.n_w[0] = final ? 0 : qd;
+      qp.n_w[1] = kd;
+      qp.n_w[2] = kd;
+      qp.q_heads = final ? 0 : m.q_heads;
+      qp.kv_heads = m.kv_heads;
+      qp.q_out = final ? nullptr : q_rot;
+      qp.k_cache = r.k_cache[l];
+      qp.v_cache = r.v_cache[l];
+      qp.cache_rows = r.cache_rows;
+      qp.c_hs = r.cache_head_stride;
+      qp.c_rs = r.cache_row_stride;
+      qp.positions = r.positions;
+      qp.cos_tab = r.cos_tab;
+      qp.sin_tab = r.sin_tab;
+      qp.q_norm = w.q_norm;
+      qp.k_norm = w.k_norm;
+      return qp;
+    };
+    auto residual_params = [&](const void* x, int64_t k, const void* wt) {
+      ProjParams op{};
+      op.epilogue = PROJ_RESIDUAL;
+      op.dtype = m.dtype;
+      op.rows = rows;
+      op.k = k;
+      op.x = x;
+      op.x_stride = k;
+      op.w[0] = wt;
+      op.n_w[0] = H;
+      op.out = hidden;
+      op.out_stride = H;
+      op.ssq_out = ssq;
+      return op;
+    };
+    auto gated_params = [&](const kvr_layer_weights& w) {
+      ProjParams gp{};
+      gp.epilogue = PROJ_GATED;
+      gp.dtype = m.dtype;
+      gp.rows = rows;
+      gp.k = H;
+      gp.x = hidden;
+      gp.x_stride = H;
+      gp.norm_w = w.post_norm;
+      gp.ssq_in = ssq;
+      gp.ssq_tiles = ssq_tiles;
+      gp.eps = m.eps;
+      gp.w[0] = w.gate;
+      gp.w[1] = w.up;
+      gp.n_w[0] = I;
+      gp.n_w[1] = I;
+      gp.out = act;
+      gp.out_stride = I;
+      return gp;
+    };
+    for (int l = 0; l < m.num_layers; ++l) {
+      const kvr_layer_weights& w = m.layers[l];
+      const bool final = l == m.num_layers - 1;
+      const ProjParams qp = qkv_params(l);
+      if (final) {
+        KVR_TRY(copied(l));  // the q/k/v launch writes layer l of the owned cache: its copy first
+        KVR_TRY(proj_forward(qp, proj_ws, b.proj_bytes, s));
+        if (l == g_fail_after_layer) {
+          g_fail_after_layer = -1;
+          return KVR_ERR_INJECTED;
+        }
+        break;
+      }
+      KVR_TRY(copied(l));
+      KVR_TRY(proj_forward(qp, proj_ws, b.proj_bytes, s));
+      if (l == g_fail_after_layer) {
+        g_fail_after_layer = -1;
+        return KVR_ERR_INJECTED;
+      }
+      KVR_TRY(selected_attention(q_rot, r.k_cache[l], r.v_cache[l], attn, r.positions, rows, m.q_heads, m.kv_heads,
+                                 D, r.cache_rows, r.cache_head_stride, r.cache_row_stride, r.max_position, scale,
+                                 r.attention_precision, attn_ws, attn_ws_bytes, m.dtype, stream, true));
+      KVR_TRY(proj_forward(residual_params(attn, qd, w.o), proj_ws, b.proj_bytes, s));
+      KVR_TRY(proj_forward(gated_params(w), proj_ws, b.proj_bytes, s));
+      KVR_TRY(proj_forward(residual_params(act, I, w.down), proj_ws, b.proj_bytes, s));
+    }
+    return KVR_OK;
+  }
   for (int l = 0; l < m.num_layers; ++l) {
     const kvr_layer_weights& w = m.layers[l];
     const bool final = l == m.num_layers - 1;

@@ -6,6 +6,8 @@
     python -m budgeted_kv_cache_repair_b200.profile_kernels copy      [--reps N] [--tensors T]
     python -m budgeted_kv_cache_repair_b200.profile_kernels linear    [--reps N] [--only NAME]
     python -m budgeted_kv_cache_repair_b200.profile_kernels relevance [--reps N]
+    python -m budgeted_kv_cache_repair_b200.profile_kernels refresh   [--reps N] [--layers L]
+                                                                      [--projections cublas|sm100|fused]
 
 Geometry: Llama-3-8B shape (32 layers, 8 KV heads, head_dim 128, bf16),
 8192-token context with 256 tokens deleted at 1024 (7936 rows), 64 selected
@@ -13,6 +15,10 @@ rows in 16 intervals of 4 (`linear`: the per-layer projections of that model
 at 64 rows, each timed beside torch's cuBLAS GEMMs for the same products, with
 enough weight copies in rotation that no launch finds its weights in L2, and
 replayed from a CUDA graph so that host launch cost is not measured).
+`refresh`: packed_interval_repair over the first `--layers` layers (2 by
+default: about 3 GB on the device with the embedding and head) of that model,
+every launch direct (no graph replay, unless `--replay`), so a profiler sees
+each kernel of the layer loop as issued.
 `relevance`: select_support's query relevance at config 3 (Qwen3-8B
 embedding table, 151936 x 4096 bf16; 31744 prompt tokens; 8 query tokens).
 `attention --geometry config3`: one layer of the Qwen3-8B shape at 32k context
@@ -212,19 +218,66 @@ def relevance(reps: int) -> None:
     print(f"kvr_query_relevance: {us:.1f} us/call, {algo / us / 1e3:.0f} GB/s of embedding rows ({algo} bytes)")
 
 
+def refresh(reps: int, layers: int, projections: str, replay: bool = False) -> None:
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from . import OperatorShim, engine, packed_interval_repair
+    from .cache import make_cache
+
+    config = LlamaConfig(vocab_size=128256, hidden_size=HIDDEN, intermediate_size=INTER, num_hidden_layers=layers,
+                         num_attention_heads=HEADS, num_key_value_heads=KV_HEADS, head_dim=D, rope_theta=500000.0,
+                         max_position_embeddings=131072, initializer_range=0.02)
+    torch.manual_seed(1)
+    previous = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device("cuda"):
+            model = LlamaForCausalLM(config).eval()
+    finally:
+        torch.set_default_dtype(previous)
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    ids = torch.randint(0, 128256, (1, NEW), device="cuda", generator=gen)
+    base = make_cache([(torch.randn(1, KV_HEADS, NEW, D, device="cuda", generator=gen).bfloat16(),
+                        torch.randn(1, KV_HEADS, NEW, D, device="cuda", generator=gen).bfloat16())
+                       for _ in range(layers)])
+    positions = _positions()
+    intervals = []
+    for p in positions:
+        if intervals and p == intervals[-1][1]:
+            intervals[-1] = (intervals[-1][0], p + 1)
+        else:
+            intervals.append((p, p + 1))
+    engine.GRAPH_REPLAY = replay
+    engine.PROJECTIONS = {"cublas": _lib.PROJ_CUBLAS, "sm100": _lib.PROJ_SM100, "fused": _lib.PROJ_FUSED}[projections]
+    shim = OperatorShim(model)
+    with torch.no_grad():
+        for _ in range(4):  # graph replay: the first calls run directly, then capture
+            packed_interval_repair(shim, base, ids, intervals)
+        ms = _time(lambda: packed_interval_repair(shim, base, ids, intervals), reps) / 1e3
+    how = "graph replay" if replay else "direct launches"
+    print(f"packed_interval_repair ({projections}, {layers} layers, {how}): {ms:.3f} ms/call, "
+          f"{ms / layers * 1e3:.1f} us/layer")
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("kernel", choices=["shift", "attention", "copy", "linear", "relevance"])
+    parser.add_argument("kernel", choices=["shift", "attention", "copy", "linear", "relevance", "refresh"])
+    parser.add_argument("--projections", choices=["cublas", "sm100", "fused"], default="fused",
+                        help="refresh: projection path of the layer loop")
+    parser.add_argument("--replay", action="store_true", help="refresh: replay repeated calls from a CUDA graph")
     parser.add_argument("--only", default=None, help="linear: one of qkv, o, gate_up, down")
     parser.add_argument("--reps", type=int, default=10)
-    parser.add_argument("--layers", type=int, default=LAYERS, help="shift: layers (fewer for a small capture)")
+    parser.add_argument("--layers", type=int, default=None,
+                        help="shift: layers (32 by default; fewer for a small capture); refresh: layers (2)")
     parser.add_argument("--tensors", type=int, default=2 * LAYERS, help="copy: K/V tensors per launch (2 to 64)")
     parser.add_argument("--precision", choices=["rounded", "split"], default="rounded")
     parser.add_argument("--geometry", choices=["config2", "config3"], default="config2", help="attention geometry")
     args = parser.parse_args()
     build.build()
     if args.kernel == "shift":
-        shift(args.reps, args.layers)
+        shift(args.reps, args.layers or LAYERS)
+    elif args.kernel == "refresh":
+        refresh(args.reps, args.layers or 2, args.projections, args.replay)
     elif args.kernel == "copy":
         copy(args.reps, args.tensors)
     elif args.kernel == "linear":

@@ -342,6 +342,10 @@ typedef struct kvr_refresh_request {
 } kvr_refresh_request;
 #define KVR_PROJ_CUBLAS 0  /* cuBLAS GEMMs, fp32 accumulation */
 #define KVR_PROJ_SM100 1   /* kvr_linear's weight-streaming kernel, gate/up fused with SiLU */
+#define KVR_PROJ_FUSED 2   /* fused projections (up to 128 rows, head_dim 128, no tensor parallelism;
+                              other requests run on cuBLAS): four launches per layer, the q/k/v one
+                              with q/k-norm + RoPE + K/V scatter, o and down with the residual add,
+                              gate/up with the post-attention RMSNorm applied to its input and SiLU*up */
 
 /*
  * Tensor-parallel group for kvr_packed_refresh (NCCL over NVLink). No

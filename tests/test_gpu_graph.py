@@ -25,11 +25,12 @@ def _fresh_graph_cache():
     engine.release_graphs()
 
 
-@pytest.fixture(params=["cublas", "sm100"])
+@pytest.fixture(params=["cublas", "sm100", "fused"])
 def projections(request, monkeypatch):
     from budgeted_kv_cache_repair_b200 import _lib, engine
 
-    monkeypatch.setattr(engine, "PROJECTIONS", {"cublas": _lib.PROJ_CUBLAS, "sm100": _lib.PROJ_SM100}[request.param])
+    monkeypatch.setattr(engine, "PROJECTIONS", {"cublas": _lib.PROJ_CUBLAS, "sm100": _lib.PROJ_SM100,
+                                                "fused": _lib.PROJ_FUSED}[request.param])
     return request.param
 
 

@@ -21,12 +21,13 @@ def _check_rows(actual_rows, expected_rows, what, min_cos=0.999):
     assert (err <= bound).all(), (what, err.max().item())
 
 
-@pytest.fixture(params=["cublas", "sm100"])
+@pytest.fixture(params=["cublas", "sm100", "fused"])
 def projections(request, monkeypatch):
     """Both projection paths of the layer loop: cuBLAS and the kvr_linear kernel."""
     from budgeted_kv_cache_repair_b200 import _lib, engine
 
-    monkeypatch.setattr(engine, "PROJECTIONS", {"cublas": _lib.PROJ_CUBLAS, "sm100": _lib.PROJ_SM100}[request.param])
+    monkeypatch.setattr(engine, "PROJECTIONS", {"cublas": _lib.PROJ_CUBLAS, "sm100": _lib.PROJ_SM100,
+                                                "fused": _lib.PROJ_FUSED}[request.param])
     return request.param
 
 

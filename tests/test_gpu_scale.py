@@ -146,6 +146,22 @@ def test_config2_geometry_own_projections_match_reference_packed_path():
 
 
 @torch.no_grad()
+def test_config2_geometry_fused_projections_match_reference_packed_path():
+    """configs[2] with the fused projections (q/k/v + RoPE + scatter, o and
+    down + residual, gate/up on the normalised residual stream + SiLU)."""
+    from budgeted_kv_cache_repair_b200 import _lib
+
+    _check_against_reference_path(bench.WORKLOADS["config2"], 3, 1, projections=_lib.PROJ_FUSED)
+
+
+@torch.no_grad()
+def test_config1_geometry_fused_projections_match_reference_packed_path():
+    from budgeted_kv_cache_repair_b200 import _lib
+
+    _check_against_reference_path(bench.WORKLOADS["config1"], 3, 1, projections=_lib.PROJ_FUSED)
+
+
+@torch.no_grad()
 def test_config3_geometry_matches_reference_packed_path():
     """Qwen3-8B shape, 31744 rows of context, 1383 rows in 32
     intervals, 2 of the 36 layers."""
