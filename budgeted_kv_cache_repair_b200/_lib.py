@@ -148,8 +148,11 @@ def stream_handle(device: torch.device | None = None) -> int:
 
 
 def ptr_array(tensors) -> ctypes.Array:
-    return (ctypes.c_void_p * len(tensors))(*[t.data_ptr() if isinstance(t, torch.Tensor) else int(t)
-                                               for t in tensors])
+    array = ctypes.c_void_p * len(tensors)
+    try:
+        return array(*map(torch.Tensor.data_ptr, tensors))
+    except TypeError:  # raw addresses among the entries
+        return array(*[t.data_ptr() if isinstance(t, torch.Tensor) else int(t) for t in tensors])
 
 
 def check(status: int, what: str) -> None:

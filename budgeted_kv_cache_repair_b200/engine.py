@@ -66,7 +66,8 @@ class LayerWeights:
     def fused_qkv(self) -> torch.Tensor:
         """``cat([Wq, Wk, Wv])`` for one GEMM per layer, rebuilt if any of the
         three parameters was replaced or modified in place since."""
-        key = tuple((id(t), t.data_ptr(), t._version) for t in (self.q, self.k, self.v))
+        q, k, v = self.q, self.k, self.v
+        key = (id(q), q.data_ptr(), q._version, id(k), k.data_ptr(), k._version, id(v), v.data_ptr(), v._version)
         if self.qkv is None or self.qkv_key != key:
             self.qkv = torch.cat((self.q, self.k, self.v), dim=0).contiguous()
             self.qkv_key = key
@@ -146,7 +147,11 @@ _STAGING_KEEP = 8
 
 
 class _Staging:
-    """Per (device, stream, geometry) input buffers and workspace of a refresh."""
+    """Per (device, stream, geometry) input buffers and workspace of a refresh.
+
+    Host positions reach ``positions`` through ``host_positions`` (pinned), one
+    stream-ordered copy; ``host_ready`` marks the end of that copy, and the
+    pinned buffer is written again only after it (normally long done)."""
 
     def __init__(self, device, id_count: int, rows: int, dim: int, dtype, workspace_bytes: int):
         self.ids = torch.empty(id_count, dtype=torch.int64, device=device)
@@ -154,6 +159,8 @@ class _Staging:
         self.cos = torch.empty(rows, dim, dtype=dtype, device=device)
         self.sin = torch.empty(rows, dim, dtype=dtype, device=device)
         self.workspace = torch.empty(workspace_bytes, dtype=torch.uint8, device=device)
+        self.host_positions = None
+        self.host_ready = None
 
 
 # Keyed by (thread, device, stream, geometry): two threads issuing requests on
@@ -175,19 +182,32 @@ def release_graphs() -> None:
 
 def _staged(view: ModelView, device, ids, positions, need) -> _Staging:
     """This thread's staging buffers for the request's geometry on the current
-    stream, filled with its ids, positions and rotary tables (stream-ordered)."""
+    stream, filled with its ids, positions and rotary tables (stream-ordered).
+    ``positions``: a device tensor, or host integers (copied from pinned
+    memory straight into the staged buffer)."""
     stream = torch.cuda.current_stream(device)
-    key = (threading.get_ident(), device.index, stream.cuda_stream, ids.numel(), positions.numel(), view.head_dim,
-           view.dtype, need)
+    rows = positions.numel() if isinstance(positions, torch.Tensor) else len(positions)
+    key = (threading.get_ident(), device.index, stream.cuda_stream, ids.numel(), rows, view.head_dim, view.dtype,
+           need)
     with _staging_lock:
         st = _staging.pop(key, None)
         if st is None:
-            st = _Staging(device, ids.numel(), positions.numel(), view.head_dim, view.dtype, need)
+            st = _Staging(device, ids.numel(), rows, view.head_dim, view.dtype, need)
             while len(_staging) >= _STAGING_KEEP:
                 _staging.popitem(last=False)
         _staging[key] = st
     st.ids.copy_(ids)
-    st.positions.copy_(positions)
+    if isinstance(positions, torch.Tensor):
+        st.positions.copy_(positions)
+    else:
+        if st.host_positions is None:
+            st.host_positions = torch.empty(rows, dtype=torch.int64).pin_memory()
+            st.host_ready = torch.cuda.Event()
+        else:
+            st.host_ready.synchronize()  # the previous request's copy out of the pinned buffer
+        st.host_positions.numpy()[:] = positions
+        st.positions.copy_(st.host_positions, non_blocking=True)
+        st.host_ready.record(stream)
     view.rope_tables(st.positions, out=(st.cos, st.sin))
     return st
 
@@ -245,9 +265,12 @@ def model_view(base) -> ModelView:
 def _native_model(view: ModelView):
     """The kvr_model struct for this view, refreshed when fused weights were rebuilt."""
     qkv = [w.fused_qkv() for w in view.layers]
+    flat = getattr(view, "_flat", None)
+    if flat is None:
+        flat = view._flat = [view.embed] + [t for w in view.layers
+                                            for t in (w.in_norm, w.o, w.post_norm, w.gate, w.up, w.down)]
     # Any replaced parameter storage changes a data pointer: rebuild the struct.
-    key = tuple(t.data_ptr() for t in qkv) + (view.embed.data_ptr(),) + tuple(
-        t.data_ptr() for w in view.layers for t in (w.in_norm, w.o, w.post_norm, w.gate, w.up, w.down))
+    key = tuple(map(torch.Tensor.data_ptr, qkv)) + tuple(map(torch.Tensor.data_ptr, flat))
     if getattr(view, "_native_key", None) != key:
         arr = (_lib.LayerWeights * len(view.layers))()
         for i, (w, fused) in enumerate(zip(view.layers, qkv)):
@@ -299,13 +322,14 @@ def linear(x: torch.Tensor, weights, outs=None) -> list[torch.Tensor]:
     return result
 
 
-def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Tensor,
+def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions,
                  max_position: int, cache_rows: int, tp_comm=None, sources=None) -> None:
     """Recompute the selected rows through every layer, writing K/V in place.
 
     ``layers``: the owned output cache, ``[(K, V)]`` each ``[1, Hkv, N, D]``
     with unit D stride and one (head, row) stride pair; ``ids``: ``[N]`` int64
-    on the device; ``positions``: ``[B]`` int64 sorted, on the device. One
+    on the device; ``positions``: ``[B]`` sorted, a device int64 tensor or
+    host integers validated by the caller (an ``IndexedPlan``'s). One
     ``kvr_packed_refresh`` call runs every layer on the current stream.
     ``sources``: optional ``[(K, V)]`` of the same geometry that ``layers``
     first become a copy of (the ownership copy of clone_cache,
@@ -313,8 +337,9 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
     copy overlaps the work on layers before l.
     """
     lib = _lib.load()
-    device = positions.device
-    rows = positions.numel()
+    host_positions = not isinstance(positions, torch.Tensor)
+    device = ids.device if host_positions else positions.device
+    rows = len(positions) if host_positions else positions.numel()
     strides = {(t.stride(1), t.stride(2)) for pair in layers for t in pair}
     if len(strides) != 1:
         raise ValueError("every cache layer must share one (head, row) stride pair")
@@ -324,8 +349,8 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
     v_ptrs = _lib.ptr_array([v for _, v in layers])
     request = _lib.RefreshRequest(
         k_cache=k_ptrs, v_cache=v_ptrs, cache_rows=cache_rows, cache_head_stride=head_stride,
-        cache_row_stride=row_stride, ids=ids.data_ptr(), id_count=ids.numel(), positions=positions.data_ptr(),
-        rows=rows, max_position=max_position, attention_precision=ATTENTION_PRECISION, tp_comm=tp_comm,
+        cache_row_stride=row_stride, ids=ids.data_ptr(), id_count=ids.numel(),
+        positions=None if host_positions else positions.data_ptr(), rows=rows, max_position=max_position, attention_precision=ATTENTION_PRECISION, tp_comm=tp_comm,
         projections=PROJECTIONS)
     if sources is not None:
         from .cache import uniform_layout
@@ -351,6 +376,11 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions: torch.Te
         request.graph_replay = 1
         workspace = st.workspace
     else:
+        if host_positions and rows:
+            from .staging import upload_int64
+
+            positions = upload_int64(list(positions), device)
+            request.positions = positions.data_ptr()
         cos, sin = view.rope_tables(positions) if rows else (None, None)
         if rows:
             request.cos_tab, request.sin_tab = cos.data_ptr(), sin.data_ptr()

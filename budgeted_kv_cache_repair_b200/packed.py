@@ -94,10 +94,11 @@ def refresh_owned_layers(shim: Any, layers, edited_ids_t: torch.Tensor, interval
         raise ValueError("the B200 packed executor requires CUDA tensors")
     base = _base_and_dtype(shim, layers, device)
     host_plan = plan if plan is not None else IndexedPlan(selected, length)
-    device_plan = host_plan.to(device)
     with torch.cuda.device(device):
         ids = _device_ids(edited_ids_t, device)
-        refresh_rows(model_view(base), layers, ids, device_plan.positions, host_plan.max_position, length)
+        # The plan's validated host positions go to the device with the
+        # request's other inputs (one pinned copy into the staged buffer).
+        refresh_rows(model_view(base), layers, ids, host_plan.positions, host_plan.max_position, length)
 
 
 @torch.no_grad()
@@ -142,10 +143,10 @@ def packed_interval_repair(
     _lib.load()
     host_plan = plan if plan is not None else IndexedPlan(selected, length)
     with torch.cuda.device(device):
-        device_plan = host_plan.to(device)
         ids = _device_ids(edited_ids_t, device)
         # The ownership copy (kernels/packed_cache.py:287) runs inside the
-        # refresh call, each layer's copy overlapping earlier layers' work.
+        # refresh call, each layer's copy overlapping earlier layers' work; the
+        # plan's validated host positions reach the device there too.
         owned = allocate_layers(len(layers), view.kv_heads, length, view.head_dim, layers[0][0].dtype, device)
-        refresh_rows(view, owned, ids, device_plan.positions, host_plan.max_position, length, sources=layers)
+        refresh_rows(view, owned, ids, host_plan.positions, host_plan.max_position, length, sources=layers)
     return make_cache(owned), receipt

@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import weakref
 from numbers import Integral
+from operator import attrgetter, methodcaller
 from typing import Any, Sequence
 
 import torch
@@ -61,6 +62,16 @@ def validate_cache(cache: Any, logical_length: int) -> list[tuple[torch.Tensor, 
     layers = cache_layers(cache)
     if not layers:
         raise ValueError("base_cache must contain at least one K/V layer")
+    # Fast path: every K and V a tensor of one (shape, dtype, device) that
+    # passes the rules; otherwise the rule table below names the fault.
+    try:
+        kinds = {(type(t), t.shape, t.dtype, t.device) for pair in layers for t in pair}
+    except AttributeError:
+        kinds = ()
+    if len(kinds) == 1:
+        key, value = layers[0]
+        if isinstance(key, torch.Tensor) and all(rule(key, value, logical_length) for rule, _ in _LAYER_RULES):
+            return layers
     signatures = set()
     for index, (key, value) in enumerate(layers):
         broken = next((text for rule, text in _LAYER_RULES if not rule(key, value, logical_length)), None)
@@ -127,7 +138,8 @@ class _ModuleScan:
     """Flattened module/parameter lists of one model, so per-call checks need
     no recursive traversal; rebuilt when the decoder's structure changes."""
 
-    __slots__ = ("fingerprint", "modules", "in_base", "params", "param_state")
+    __slots__ = ("fingerprint", "modules", "in_base", "params", "param_list", "states", "base_states",
+                 "param_state")
 
     def __init__(self, model, base, fingerprint):
         self.fingerprint = fingerprint
@@ -136,6 +148,11 @@ class _ModuleScan:
         self.in_base = [id(m) in base_ids for m in self.modules]
         self.params = [(p, inb) for m, inb in zip(self.modules, self.in_base)
                        for p in m._parameters.values() if p is not None]
+        self.param_list = [p for p, _ in self.params]
+        # The modules' attribute dicts (the objects themselves, so a later
+        # per-instance forward or hook shows up in them).
+        self.states = [m.__dict__ for m in self.modules]
+        self.base_states = [m.__dict__ for m, inb in zip(self.modules, self.in_base) if inb]
         self.param_state = None
 
 
@@ -144,14 +161,25 @@ _scans: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
 
 def _fingerprint(model, base):
     """Identities of the decoder's modules two levels below each layer."""
-    ids = [id(base), id(base.layers), id(getattr(model, "lm_head", None))]
-    for layer in base.layers:
+    holder = base._modules["layers"]
+    ids = [id(base), id(holder), id(model._modules.get("lm_head"))]
+    extend = ids.extend
+    for layer in holder._modules.values():
+        children = layer._modules.values()
         ids.append(id(layer))
-        for child in layer._modules.values():
-            ids.append(id(child))
+        extend(map(id, children))
+        for child in children:
             if child is not None:
-                ids.extend(map(id, child._modules.values()))
+                extend(map(id, child._modules.values()))
     return tuple(ids)
+
+
+_training = attrgetter("training")
+_has_forward = methodcaller("__contains__", "forward")
+
+
+def _has_hook(state: dict) -> bool:
+    return state.get("_hf_hook") is not None
 
 
 def _check_modules(model, base, device, dtype):
@@ -160,16 +188,14 @@ def _check_modules(model, base, device, dtype):
     if scan is None or scan.fingerprint != fp:
         scan = _ModuleScan(model, base, fp)
         _scans[model] = scan
-    for module, in_base in zip(scan.modules, scan.in_base):
-        if module.training:
-            raise ValueError("packed executor requires eval mode on all decoder modules")
-        state = module.__dict__
-        if state.get("_hf_hook") is not None:
-            raise ValueError("packed executor does not support dispatch/offload hooks")
-        if in_base and "forward" in state:
-            raise ValueError("packed executor does not support per-instance decoder forward overrides")
+    if any(map(_training, scan.modules)):
+        raise ValueError("packed executor requires eval mode on all decoder modules")
+    if any(map(_has_hook, scan.states)):
+        raise ValueError("packed executor does not support dispatch/offload hooks")
+    if any(map(_has_forward, scan.base_states)):
+        raise ValueError("packed executor does not support per-instance decoder forward overrides")
     # Parameter placement only needs re-checking when some parameter moved.
-    state = (device, dtype, tuple(p.data_ptr() for p, _ in scan.params))
+    state = (device, dtype, tuple(map(torch.Tensor.data_ptr, scan.param_list)))
     if scan.param_state != state:
         for p, in_base in scan.params:
             if p.device != device:
