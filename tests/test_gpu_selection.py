@@ -32,7 +32,7 @@ def _torch_scores(table, prompt, query, boost=0.25):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-@pytest.mark.parametrize("hidden, nq", [(64, 1), (4096, 3), (4096, 19), (520, 9)])
+@pytest.mark.parametrize("hidden, nq", [(64, 1), (4096, 3), (4096, 19), (520, 9), (8192, 5), (12288, 9)])
 def test_relevance_kernel_matches_torch(dtype, hidden, nq):
     from budgeted_kv_cache_repair_b200.selection import dense_query_relevance_scores
 
