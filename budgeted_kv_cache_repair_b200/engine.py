@@ -196,7 +196,7 @@ def _staged(view: ModelView, device, ids, positions, need) -> _Staging:
             while len(_staging) >= _STAGING_KEEP:
                 _staging.popitem(last=False)
         _staging[key] = st
-    st.ids.copy_(ids)
+    st.ids.copy_(ids, non_blocking=True)  # device ids, or pinned host ids
     if isinstance(positions, torch.Tensor):
         st.positions.copy_(positions)
     else:
@@ -328,7 +328,8 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions,
 
     ``layers``: the owned output cache, ``[(K, V)]`` each ``[1, Hkv, N, D]``
     with unit D stride and one (head, row) stride pair; ``ids``: ``[N]`` int64
-    on the device; ``positions``: ``[B]`` sorted, a device int64 tensor or
+    on the device, or in pinned host memory (copied once, into the request's
+    staged buffer); ``positions``: ``[B]`` sorted, a device int64 tensor or
     host integers validated by the caller (an ``IndexedPlan``'s). One
     ``kvr_packed_refresh`` call runs every layer on the current stream.
     ``sources``: optional ``[(K, V)]`` of the same geometry that ``layers``
@@ -338,7 +339,9 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions,
     """
     lib = _lib.load()
     host_positions = not isinstance(positions, torch.Tensor)
-    device = ids.device if host_positions else positions.device
+    device = layers[0][0].device
+    if ids.device.type == "cpu" and not (ids.dtype == torch.int64 and ids.is_pinned()):
+        raise ValueError("host ids must be pinned int64")
     rows = len(positions) if host_positions else positions.numel()
     strides = {(t.stride(1), t.stride(2)) for pair in layers for t in pair}
     if len(strides) != 1:
@@ -349,7 +352,7 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions,
     v_ptrs = _lib.ptr_array([v for _, v in layers])
     request = _lib.RefreshRequest(
         k_cache=k_ptrs, v_cache=v_ptrs, cache_rows=cache_rows, cache_head_stride=head_stride,
-        cache_row_stride=row_stride, ids=ids.data_ptr(), id_count=ids.numel(),
+        cache_row_stride=row_stride, ids=None, id_count=ids.numel(),
         positions=None if host_positions else positions.data_ptr(), rows=rows, max_position=max_position, attention_precision=ATTENTION_PRECISION, tp_comm=tp_comm,
         projections=PROJECTIONS)
     if sources is not None:
@@ -376,6 +379,9 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions,
         request.graph_replay = 1
         workspace = st.workspace
     else:
+        if ids.device.type == "cpu":
+            ids = ids.to(device, non_blocking=True)
+        request.ids = ids.data_ptr()
         if host_positions and rows:
             from .staging import upload_int64
 

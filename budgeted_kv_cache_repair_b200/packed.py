@@ -59,6 +59,16 @@ def _check_ids(edited_ids_t) -> int:
     return int(edited_ids_t.shape[1])
 
 
+def _request_ids(edited_ids_t: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """The ids row as the engine takes it: pinned host int64 ids as they are
+    (copied once, straight into the request's staged device buffer), anything
+    else as a contiguous int64 device tensor."""
+    ids = edited_ids_t[0]
+    if ids.device.type == "cpu" and ids.dtype == torch.int64 and ids.is_pinned() and ids.is_contiguous():
+        return ids
+    return _device_ids(edited_ids_t, device)
+
+
 def _device_ids(edited_ids_t: torch.Tensor, device: torch.device) -> torch.Tensor:
     ids = edited_ids_t[0]
     if ids.device != device:
@@ -82,6 +92,11 @@ def _base_and_dtype(shim, layers, device):
     return base
 
 
+def _check_plan(plan, selected, length: int) -> None:
+    if not isinstance(plan, IndexedPlan) or tuple(plan.positions) != selected or plan.logical_length != length:
+        raise ValueError("supplied IndexedPlan must match exact selected positions and cache length")
+
+
 def refresh_owned_layers(shim: Any, layers, edited_ids_t: torch.Tensor, intervals, plan: IndexedPlan | None = None):
     """Refresh ``intervals`` in place in caller-owned layer tensors (no copy, no receipt)."""
     length = _check_ids(edited_ids_t)
@@ -93,12 +108,13 @@ def refresh_owned_layers(shim: Any, layers, edited_ids_t: torch.Tensor, interval
     if device.type != "cuda":
         raise ValueError("the B200 packed executor requires CUDA tensors")
     base = _base_and_dtype(shim, layers, device)
-    host_plan = plan if plan is not None else IndexedPlan(selected, length)
+    if plan is not None:
+        _check_plan(plan, selected, length)
     with torch.cuda.device(device):
-        ids = _device_ids(edited_ids_t, device)
-        # The plan's validated host positions go to the device with the
-        # request's other inputs (one pinned copy into the staged buffer).
-        refresh_rows(model_view(base), layers, ids, host_plan.positions, host_plan.max_position, length)
+        ids = _request_ids(edited_ids_t, device)
+        # The validated host positions go to the device with the request's
+        # other inputs (one pinned copy into the staged buffer).
+        refresh_rows(model_view(base), layers, ids, selected, selected[-1], length)
 
 
 @torch.no_grad()
@@ -126,8 +142,7 @@ def packed_interval_repair(
     intervals = validate_intervals(intervals, length)
     selected = tuple(p for start, end in intervals for p in range(start, end))
     if plan is not None:
-        if not isinstance(plan, IndexedPlan) or tuple(plan.positions) != selected or plan.logical_length != length:
-            raise ValueError("supplied IndexedPlan must match exact selected positions and cache length")
+        _check_plan(plan, selected, length)
     receipt = make_receipt(intervals, length, len(layers), attention_backend, writeback_backend)
     if not selected:
         return base_cache, receipt
@@ -141,12 +156,14 @@ def packed_interval_repair(
     if layers[0][0].shape[1] != view.kv_heads or layers[0][0].shape[3] != view.head_dim:
         raise ValueError("cache head geometry does not match the model")
     _lib.load()
-    host_plan = plan if plan is not None else IndexedPlan(selected, length)
+    # The selected positions come from validated intervals (sorted, disjoint,
+    # inside the cache), so they already are what an IndexedPlan of them would
+    # hold; the engine needs no tile metadata, so none is built here.
     with torch.cuda.device(device):
-        ids = _device_ids(edited_ids_t, device)
+        ids = _request_ids(edited_ids_t, device)
         # The ownership copy (kernels/packed_cache.py:287) runs inside the
         # refresh call, each layer's copy overlapping earlier layers' work; the
-        # plan's validated host positions reach the device there too.
+        # validated host positions reach the device there too.
         owned = allocate_layers(len(layers), view.kv_heads, length, view.head_dim, layers[0][0].dtype, device)
-        refresh_rows(view, owned, ids, host_plan.positions, host_plan.max_position, length, sources=layers)
+        refresh_rows(view, owned, ids, selected, selected[-1], length, sources=layers)
     return make_cache(owned), receipt
