@@ -71,6 +71,38 @@ def test_packed_matches_reference_outputs(name, projections):
 
 
 @pytest.mark.parametrize("name", CASES)
+def test_up_weights_below_gate_weights(name):
+    """The gate and up projections run as one strided-batched GEMM whose
+    batch 0 is the lower-addressed weight; models whose up weights sit below
+    their gate weights in memory take the other order, with the same rows."""
+    from budgeted_kv_cache_repair_b200 import OperatorShim, packed_interval_repair
+
+    record = load_golden(name)
+    model = fixture_model(record, DEV)
+    for layer in model.model.layers:
+        gate, up = layer.mlp.gate_proj.weight, layer.mlp.up_proj.weight
+        block = torch.empty((2,) + tuple(gate.shape), dtype=gate.dtype, device=gate.device)
+        block[0].copy_(up.data)
+        block[1].copy_(gate.data)
+        up.data, gate.data = block[0], block[1]
+        assert up.data_ptr() < gate.data_ptr()
+    shim = OperatorShim(model)
+    base = to_cache(record["shifted_layers"], DEV)
+    snapshot = layers_cpu(base)
+    out, _ = packed_interval_repair(shim, base, record["new_ids"].to(DEV), record["intervals"])
+    torch.cuda.synchronize()
+    positions = record["positions"]
+    got = layers_cpu(out)
+    pos = torch.tensor(positions)
+    for layer, ((k, v), (ek, ev)) in enumerate(zip(got, record["packed_rows"])):
+        _check_rows(k[:, :, pos], ek, f"{name} K layer {layer}")
+        _check_rows(v[:, :, pos], ev, f"{name} V layer {layer}")
+    ref_model = oracle.OracleModel.from_state_dict(record["state_dict"], oracle_config(record), record["inv_freq"])
+    expected = oracle.packed_refresh(ref_model, snapshot, record["new_ids"], positions)
+    _check_rows(oracle.fresh_rows(got, positions), oracle.fresh_rows(expected, positions), f"{name} vs oracle")
+
+
+@pytest.mark.parametrize("name", CASES)
 def test_scatter_matches_index_copy_of_the_engines_own_rows(name):
     """K/V written by the fused epilogue equal index_copy_ of the same rows."""
     from budgeted_kv_cache_repair_b200 import OperatorShim, packed_interval_repair
