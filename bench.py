@@ -414,7 +414,8 @@ def refresh_bytes(cfg, length):
 def _summary(samples):
     ordered = sorted(samples)
     return {"median": statistics.median(samples), "mean": statistics.mean(samples),
-            "p95": ordered[max(0, -(-95 * len(ordered) // 100) - 1)], "n": len(samples)}
+            "p95": ordered[max(0, -(-95 * len(ordered) // 100) - 1)], "n": len(samples),
+            "samples": [round(x, 4) for x in samples]}
 
 
 def _row_agreement(actual_layers, expected_layers, positions):
