@@ -44,7 +44,7 @@ from dataclasses import dataclass
 
 import torch
 
-from . import _lib
+from . import _lib, registry
 
 
 @dataclass
@@ -80,6 +80,7 @@ class ModelView:
     def __init__(self, base):
         config = base.config
         self.base = base
+        self.epoch = -1  # registry.epoch() when this view was built
         self.rotary = base.rotary_emb
         self.embed = base.embed_tokens.weight
         self.hidden = config.hidden_size
@@ -251,13 +252,22 @@ def kernel_timer() -> KernelTimer | None:
 
 
 def model_view(base) -> ModelView:
-    """Cached view; rebuilt if any parameter was replaced since."""
-    view = _views.get(base)
-    if view is not None:
-        probe = base.layers[0].self_attn.q_proj.weight
-        if probe is view.layers[0].q and base.embed_tokens.weight is view.embed:
-            return view
+    """Cached view; rebuilt once a parameter, buffer or submodule of a module
+    of a cached model was registered or replaced since it was built
+    (registry.epoch)."""
+    old = _views.get(base)
+    epoch = registry.epoch()
+    if old is not None and old.epoch == epoch:
+        return old
     view = ModelView(base)
+    view.epoch = epoch
+    registry.watch(base.modules())
+    if old is not None:
+        # Layers whose q/k/v are the same parameter objects keep their stacked
+        # copy (fused_qkv still rebuilds it if one of them changed in place).
+        for new_w, old_w in zip(view.layers, old.layers):
+            if new_w.q is old_w.q and new_w.k is old_w.k and new_w.v is old_w.v:
+                new_w.qkv, new_w.qkv_key = old_w.qkv, old_w.qkv_key
     _views[base] = view
     return view
 

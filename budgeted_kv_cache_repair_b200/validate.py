@@ -14,6 +14,8 @@ from typing import Any, Sequence
 
 import torch
 
+from . import registry
+
 
 def cache_layers(cache: Any) -> list[tuple[torch.Tensor, torch.Tensor]]:
     """``(K, V)`` of every layer of a transformers Cache (4.57 or 5.x) or a
@@ -138,13 +140,14 @@ class _ModuleScan:
     """Flattened module/parameter lists of one model, so per-call checks need
     no recursive traversal; rebuilt when the decoder's structure changes."""
 
-    __slots__ = ("fingerprint", "modules", "in_base", "params", "param_list", "states", "base_states",
+    __slots__ = ("epoch", "modules", "in_base", "params", "param_list", "states", "base_states",
                  "param_state")
 
-    def __init__(self, model, base, fingerprint):
-        self.fingerprint = fingerprint
+    def __init__(self, model, base, epoch):
+        self.epoch = epoch
         base_ids = {id(m) for m in base.modules()}
         self.modules = list(model.modules())
+        registry.watch(self.modules)
         self.in_base = [id(m) in base_ids for m in self.modules]
         self.params = [(p, inb) for m, inb in zip(self.modules, self.in_base)
                        for p in m._parameters.values() if p is not None]
@@ -159,21 +162,6 @@ class _ModuleScan:
 _scans: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
 
 
-def _fingerprint(model, base):
-    """Identities of the decoder's modules two levels below each layer."""
-    holder = base._modules["layers"]
-    ids = [id(base), id(holder), id(model._modules.get("lm_head"))]
-    extend = ids.extend
-    for layer in holder._modules.values():
-        children = layer._modules.values()
-        ids.append(id(layer))
-        extend(map(id, children))
-        for child in children:
-            if child is not None:
-                extend(map(id, child._modules.values()))
-    return tuple(ids)
-
-
 _training = attrgetter("training")
 _has_forward = methodcaller("__contains__", "forward")
 
@@ -183,10 +171,13 @@ def _has_hook(state: dict) -> bool:
 
 
 def _check_modules(model, base, device, dtype):
-    fp = _fingerprint(model, base)
+    # The module list, parameters and attribute dicts are re-collected once a
+    # submodule or parameter of a watched model was registered or replaced
+    # since the last scan (registry.epoch); the checks below run on every call.
+    epoch = registry.epoch()
     scan = _scans.get(model)
-    if scan is None or scan.fingerprint != fp:
-        scan = _ModuleScan(model, base, fp)
+    if scan is None or scan.epoch != epoch:
+        scan = _ModuleScan(model, base, epoch)
         _scans[model] = scan
     if any(map(_training, scan.modules)):
         raise ValueError("packed executor requires eval mode on all decoder modules")

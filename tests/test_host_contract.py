@@ -331,3 +331,48 @@ def test_api_rejects_unsupported_models_before_any_device_work(fault, match):
         repair_after_deletion(model, tokenizer, None, "abcdef", delete_span=(1, 2), query="q")
     assert _lib.load().kvr_kernel_launches() == launches
 
+
+
+def _view_model():
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(5)
+    config = LlamaConfig(vocab_size=64, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                         num_attention_heads=2, num_key_value_heads=1, head_dim=64, max_position_embeddings=64)
+    return LlamaForCausalLM(config).to(torch.bfloat16).eval()
+
+
+def test_model_view_follows_replaced_parameter_objects():
+    """A parameter object swapped anywhere in the decoder (not an in-place
+    change, and not only in the first layer) rebuilds the engine's cached
+    view, so no call computes with the old tensor; layers whose q/k/v are
+    unchanged keep their stacked q/k/v copy."""
+    from budgeted_kv_cache_repair_b200.engine import model_view
+
+    model = _view_model()
+    base = model.model
+    view = model_view(base)
+    assert model_view(base) is view
+    stacked = view.layers[0].fused_qkv()
+    down = base.layers[1].mlp.down_proj
+    down.weight = torch.nn.Parameter(torch.zeros_like(down.weight))
+    again = model_view(base)
+    assert again is not view
+    assert again.layers[1].down is down.weight
+    assert again.layers[0].fused_qkv() is stacked
+    assert model_view(base) is again
+
+
+def test_model_contract_sees_parameter_objects_replaced_between_calls():
+    """The per-call model checks re-collect the parameters once one was
+    replaced after an earlier call: a replacement in the wrong dtype is
+    rejected."""
+    from budgeted_kv_cache_repair_b200.validate import qualify_model
+
+    model = _view_model()
+    base = model.model
+    qualify_model(model, base, 2, torch.device("cpu"), torch.bfloat16)
+    up = base.layers[0].mlp.up_proj
+    up.weight = torch.nn.Parameter(up.weight.detach().float())
+    with pytest.raises(ValueError, match="dtype"):
+        qualify_model(model, base, 2, torch.device("cpu"), torch.bfloat16)
