@@ -24,7 +24,11 @@ _watched: "weakref.WeakSet" = weakref.WeakSet()
 
 
 def _count(module, *_args) -> None:
-    if module in _watched:
+    try:
+        watched = module in _watched
+    except TypeError:  # a module class without a hash is never watched
+        watched = False
+    if watched:
         _epoch[0] += 1
     return None
 

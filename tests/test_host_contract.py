@@ -376,3 +376,24 @@ def test_model_contract_sees_parameter_objects_replaced_between_calls():
     up.weight = torch.nn.Parameter(up.weight.detach().float())
     with pytest.raises(ValueError, match="dtype"):
         qualify_model(model, base, 2, torch.device("cpu"), torch.bfloat16)
+
+
+def test_registration_count_ignores_unwatched_and_unhashable_modules():
+    """The registration hooks count only modules of models the engine has
+    cached, and never fail another module's registration (a module class
+    with ``__eq__`` and no ``__hash__`` is unhashable)."""
+    from budgeted_kv_cache_repair_b200 import registry
+
+    class Unhashable(torch.nn.Module):
+        def __eq__(self, other):
+            return self is other
+
+        def __init__(self):
+            super().__init__()
+            self.lin = torch.nn.Linear(2, 2)
+            self.w = torch.nn.Parameter(torch.zeros(1))
+
+    before = registry.epoch()
+    Unhashable()
+    torch.nn.Linear(3, 3)
+    assert registry.epoch() == before
