@@ -179,18 +179,62 @@ struct ShiftPtrs {
 // shared memory as one 16-byte (cos_lo, sin_lo, cos_hi, sin_hi) entry per
 // element, padded to 9 entries per pair index so that the 8 pair indices of a
 // warp read disjoint banks.
+//
+// Each thread streams its pairs through a private ring in shared memory:
+// kShiftStages stages of kShiftUnroll pairs, filled by 16-byte cp.async copies
+// (L2 only), so the next stages' loads stay in flight while the thread
+// rotates and stores the oldest one. With 4 CTAs per SM that keeps about
+// 190 KB of loads outstanding per SM; a register version that issued a batch
+// of loads, then its stores, held half of that on average and reached 0.85 of
+// the copy peak against 0.91 for the ring. A thread reads back only its own
+// copies (cp.async.wait_group), so the loop needs no CTA barrier.
+constexpr int kShiftThreads = 256;
+constexpr int kShiftUnroll = 2;  // pairs per stage
+constexpr int kShiftStages = 3;  // stages per thread's ring
+constexpr int kShiftRingBytes = kShiftStages * kShiftUnroll * 2 * kShiftThreads * 16;  // 48 KB
+
+// Source and destination of pair i (pair index j) of the flat sequence, or
+// false for a row the caller recomputes (rows in [prefix, new_tail)).
+template <int D>
+__device__ __forceinline__ bool shift_pair(const ShiftPtrs& ptrs, const ShiftArgs& a, uint32_t i, uint32_t per_seg,
+                                           int j, const uint16_t*& src, uint16_t*& dst, bool& rot) {
+  constexpr int PAIRS = D / 16;
+  const uint32_t seg = i / per_seg;
+  const int64_t r = (i - seg * per_seg) / PAIRS;
+  const int comp = seg & 1;
+  const int lh = seg >> 1;
+  const int l = lh / a.heads;
+  const int h = lh - l * a.heads;
+  int64_t sr = -1;
+  if (r < a.prefix) sr = r;
+  else if (r >= a.new_tail) sr = r - a.new_tail + a.old_tail;
+  if (sr < 0) return false;
+  rot = comp == 0 && a.apply_rope && r >= a.new_tail;
+  src = static_cast<const uint16_t*>(comp ? ptrs.v_old[l] : ptrs.k_old[l]) + h * a.old_hs + sr * a.old_rs + j * 8;
+  dst = static_cast<uint16_t*>(comp ? ptrs.v_new[l] : ptrs.k_new[l]) + h * a.new_hs + r * a.new_rs + j * 8;
+  return true;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+
 template <class T, int D>
-__global__ void __launch_bounds__(256, 3) shift_cache_kernel(ShiftPtrs ptrs, ShiftArgs a,
-                                                          const uint16_t* __restrict__ cos_sin) {
+__global__ void __launch_bounds__(kShiftThreads, 4) shift_cache_kernel(ShiftPtrs ptrs, ShiftArgs a,
+                                                                    const uint16_t* __restrict__ cos_sin) {
   pdl_launch_dependents();  // the next kernel may start its independent prologue
   pdl_wait();  // every input may come from the previous kernel
   constexpr int PAIRS = D / 16;
   constexpr int HALF = D / 2;
-  constexpr int U = 4;  // pairs in flight per thread (8 x 16-byte loads)
+  constexpr int U = kShiftUnroll;
+  constexpr int S = kShiftStages;
+  extern __shared__ uint4 ring[];  // [stage][2U vectors][thread]: each warp's 16-byte slots are contiguous
+  __shared__ float4 cs4[PAIRS * 9];  // [pair index][element (+1 pad)] = (cos_lo, sin_lo, cos_hi, sin_hi)
   const uint32_t tid0 = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t step = gridDim.x * blockDim.x;  // multiple of PAIRS (host-checked)
   const int j = static_cast<int>(tid0 % PAIRS);
-  __shared__ float4 cs4[PAIRS * 9];  // [pair index][element (+1 pad)] = (cos_lo, sin_lo, cos_hi, sin_hi)
+  const int t = threadIdx.x;
   if (a.apply_rope) {  // the table is only non-null when the tail rotates
     for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
       cs4[(i >> 3) * 9 + (i & 7)] = make_float4(T::to_f(cos_sin[i]), T::to_f(cos_sin[D + i]),
@@ -201,61 +245,61 @@ __global__ void __launch_bounds__(256, 3) shift_cache_kernel(ShiftPtrs ptrs, Shi
   const float4* csj = cs4 + j * 9;
   const uint32_t per_seg = static_cast<uint32_t>(a.new_rows) * PAIRS;
   const uint32_t total = per_seg * a.segments;
-  for (uint32_t i0 = tid0; i0 < total; i0 += U * step) {
-    Vec8 lo[U], hi[U];
-    uint16_t* dst[U];
-    bool live[U], rot[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {  // all loads first
-      const uint32_t i = i0 + u * step;
-      live[u] = false;
-      rot[u] = false;
-      dst[u] = nullptr;
-      if (i < total) {
-        const uint32_t seg = i / per_seg;
-        const int64_t r = (i - seg * per_seg) / PAIRS;
-        const int comp = seg & 1;
-        const int lh = seg >> 1;
-        const int l = lh / a.heads;
-        const int h = lh - l * a.heads;
-        int64_t sr = -1;
-        if (r < a.prefix) sr = r;
-        else if (r >= a.new_tail) sr = r - a.new_tail + a.old_tail;
-        // rows in [prefix, new_tail) are recomputed by the caller
-        if (sr >= 0) {
-          live[u] = true;
-          rot[u] = comp == 0 && a.apply_rope && r >= a.new_tail;
-          const uint16_t* s = static_cast<const uint16_t*>(comp ? ptrs.v_old[l] : ptrs.k_old[l]) + h * a.old_hs +
-                              sr * a.old_rs + j * 8;
-          dst[u] = static_cast<uint16_t*>(comp ? ptrs.v_new[l] : ptrs.k_new[l]) + h * a.new_hs + r * a.new_rs +
-                   j * 8;
-          lo[u] = ld_vec8_stream(s);
-          hi[u] = ld_vec8_stream(s + HALF);
-        }
-      }
-    }
+  // Stage k holds pairs tid0 + (k * U + u) * step, u < U. Every stage commits
+  // one cp.async group (empty past the end), so wait_group<S - 1> after
+  // issuing stage k + S - 1 means stage k has landed.
+  auto issue = [&](uint32_t k) {
+    uint4* slot = ring + (k % S) * (2 * U * kShiftThreads) + t;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      if (!live[u]) continue;
-      if (rot[u]) {
+      const uint32_t i = tid0 + (k * U + u) * step;
+      const uint16_t* src;
+      uint16_t* dst;
+      bool rot;
+      if (i < total && shift_pair<D>(ptrs, a, i, per_seg, j, src, dst, rot)) {
+        cp_async16(slot + (2 * u) * kShiftThreads, src);
+        cp_async16(slot + (2 * u + 1) * kShiftThreads, src + HALF);
+      }
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+  const uint32_t iters = total > tid0 ? (total - tid0 + U * step - 1) / (U * step) : 0;
+#pragma unroll
+  for (int k = 0; k < S - 1; ++k) issue(k);
+  for (uint32_t k = 0; k < iters; ++k) {
+    issue(k + S - 1);
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(S - 1) : "memory");
+    const uint4* slot = ring + (k % S) * (2 * U * kShiftThreads) + t;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = tid0 + (k * U + u) * step;
+      const uint16_t* src;
+      uint16_t* dst;
+      bool rot;
+      if (!(i < total && shift_pair<D>(ptrs, a, i, per_seg, j, src, dst, rot))) continue;
+      Vec8 lo, hi;
+      *reinterpret_cast<uint4*>(&lo) = slot[(2 * u) * kShiftThreads];
+      *reinterpret_cast<uint4*>(&hi) = slot[(2 * u + 1) * kShiftThreads];
+      if (rot) {
         Vec8 olo, ohi;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float xl = T::to_f(lo[u].h[e]);
-          const float xh = T::to_f(hi[u].h[e]);
+          const float xl = T::to_f(lo.h[e]);
+          const float xh = T::to_f(hi.h[e]);
           // d < D/2: rotate_half = -x[d + D/2];  d >= D/2: rotate_half = x[d - D/2].
-          const float4 t = csj[e];
-          olo.h[e] = rope_elem_hw<T>(xl, -xh, t.x, t.y);
-          ohi.h[e] = rope_elem_hw<T>(xh, xl, t.z, t.w);
+          const float4 c = csj[e];
+          olo.h[e] = rope_elem_hw<T>(xl, -xh, c.x, c.y);
+          ohi.h[e] = rope_elem_hw<T>(xh, xl, c.z, c.w);
         }
-        st_vec8_stream(dst[u], olo);
-        st_vec8_stream(dst[u] + HALF, ohi);
+        st_vec8_stream(dst, olo);
+        st_vec8_stream(dst + HALF, ohi);
       } else {
-        st_vec8_stream(dst[u], lo[u]);
-        st_vec8_stream(dst[u] + HALF, hi[u]);
+        st_vec8_stream(dst, lo);
+        st_vec8_stream(dst + HALF, hi);
       }
     }
   }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");  // only empty groups remain; none may outlive the CTA
 }
 
 // ---------------------------------------------------------------------------
@@ -353,20 +397,31 @@ namespace {
 
 bool valid_dtype(int dtype) { return dtype == KVR_DTYPE_BF16 || dtype == KVR_DTYPE_F16; }
 
-// CTAs of `kernel` (256 threads, static shared memory only) resident on all
-// SMs at once, queried once per device: the grid of a persistent kernel.
+// Once per device: lets `kernel` (256 threads) take `smem` bytes of dynamic
+// shared memory, prefers the largest shared-memory carveout, and returns how
+// many of its CTAs are resident on all SMs at once (the grid of a persistent
+// kernel); 0 when the device refused the attribute (its error is recorded).
 template <auto kernel>
-int resident_blocks() {
+int resident_blocks(int smem) {
   static int cache[64] = {0};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_last_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidDevice);
     cudaGetLastError();
-    return kNumSMs;
+    return 0;
   }
   int n = __atomic_load_n(&cache[dev], __ATOMIC_ACQUIRE);
   if (!n) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      cudaGetLastError();
+      return 0;
+    }
+    prefer_shared_once<kernel>();
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess || per_sm < 1) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem) != cudaSuccess || per_sm < 1) {
       cudaGetLastError();
       per_sm = 1;
     }
@@ -374,6 +429,15 @@ int resident_blocks() {
     __atomic_store_n(&cache[dev], n, __ATOMIC_RELEASE);
   }
   return n;
+}
+
+// The shift kernel on as many CTAs as are resident at once, at most `need`.
+template <auto kernel>
+int launch_shift(int64_t need, cudaStream_t s, const ShiftPtrs& p, const ShiftArgs& a, const uint16_t* cs) {
+  const int resident = resident_blocks<kernel>(kShiftRingBytes);
+  if (resident <= 0) return KVR_ERR_CUDA;
+  const dim3 grid(static_cast<unsigned>(need < resident ? need : resident));
+  return launch_pdl<kernel>(grid, dim3(kShiftThreads), kShiftRingBytes, s, 1, p, a, cs);
 }
 
 int blocks_per_segment(int64_t segment_vecs, int segments, int threads) {
@@ -514,32 +578,21 @@ int kvr_shift_cache_layers(const void* const* k_old, const void* const* v_old, v
   ShiftArgs a{heads, segs, new_rows, prefix, old_tail_start, new_tail_start,
               old_head_stride, old_row_stride, new_head_stride, new_row_stride, apply_rope};
   const int64_t pairs = new_rows * (head_dim / 16);
-  if (pairs * segs + 8LL * kNumSMs * 256 * 4 > 0xffffffffLL) return KVR_ERR_UNSUPPORTED;  // 32-bit pair index
+  // 32-bit pair index: the issue side runs up to kShiftStages stages past the
+  // end of a thread's pairs (grid of at most 4 CTAs per SM).
+  if (pairs * segs + (kShiftStages + 1LL) * kShiftUnroll * 4 * kNumSMs * kShiftThreads > 0xffffffffLL)
+    return KVR_ERR_UNSUPPORTED;
   // Persistent: as many CTAs of 256 threads as are resident at once (the grid
   // stride, a multiple of 256, is then a multiple of the pairs per row).
-  const int64_t need = (pairs * segs + 255) / 256;
-  auto grid_for_kernel = [&](int resident) {
-    return dim3(static_cast<unsigned>(need < resident ? need : resident));
-  };
+  const int64_t need = (pairs * segs + kShiftThreads - 1) / kShiftThreads;
   auto s = static_cast<cudaStream_t>(stream);
   const uint16_t* cs = static_cast<const uint16_t*>(cos_sin);
-  int st = KVR_OK;
   if (dtype == KVR_DTYPE_BF16) {
-    if (head_dim == 128)
-      st = launch_pdl<shift_cache_kernel<BF16, 128>>(grid_for_kernel(resident_blocks<shift_cache_kernel<BF16, 128>>()),
-                                                      dim3(256), 0, s, 1, p, a, cs);
-    else
-      st = launch_pdl<shift_cache_kernel<BF16, 64>>(grid_for_kernel(resident_blocks<shift_cache_kernel<BF16, 64>>()),
-                                                     dim3(256), 0, s, 1, p, a, cs);
-  } else {
-    if (head_dim == 128)
-      st = launch_pdl<shift_cache_kernel<F16, 128>>(grid_for_kernel(resident_blocks<shift_cache_kernel<F16, 128>>()),
-                                                     dim3(256), 0, s, 1, p, a, cs);
-    else
-      st = launch_pdl<shift_cache_kernel<F16, 64>>(grid_for_kernel(resident_blocks<shift_cache_kernel<F16, 64>>()),
-                                                    dim3(256), 0, s, 1, p, a, cs);
+    if (head_dim == 128) return launch_shift<shift_cache_kernel<BF16, 128>>(need, s, p, a, cs);
+    return launch_shift<shift_cache_kernel<BF16, 64>>(need, s, p, a, cs);
   }
-  return st;
+  if (head_dim == 128) return launch_shift<shift_cache_kernel<F16, 128>>(need, s, p, a, cs);
+  return launch_shift<shift_cache_kernel<F16, 64>>(need, s, p, a, cs);
 }
 
 int kvr_scatter_rows(const void* k_fresh, const void* v_fresh, void* k_cache, void* v_cache,

@@ -121,6 +121,46 @@ def test_shift_cache_special_values_match_torch_ops(lib, dtype):
         assert bits_equal(v_new[i][0].cpu()[:, new_tail:], v[i, :, old_tail:])
 
 
+@pytest.mark.parametrize("dtype, dim", [(torch.bfloat16, 64), (torch.float16, 64), (torch.bfloat16, 128)])
+def test_shift_cache_gap_rows_strides_and_many_grid_strides(lib, dtype, dim):
+    """Rows in [prefix, new_tail) are left to the caller (never written), head
+    planes padded beyond their rows are read and written through their
+    strides, and a cache large enough that every thread walks many grid
+    strides matches torch's ops bit for bit (cache.py:47-77,103-144)."""
+    torch.manual_seed(12 + dim)
+    layers, heads, old_rows = 4, 8, 3001
+    prefix, old_tail, new_tail = 700, 1037, 709  # 9 rows for the caller, 328 deleted
+    new_rows = old_rows - (old_tail - new_tail)
+    pad_old, pad_new = 24, 40  # unused rows at the end of every head plane
+    k = torch.randn(layers, heads, old_rows + pad_old, dim).to(dtype)
+    v = torch.randn(layers, heads, old_rows + pad_old, dim).to(dtype)
+    cos = (torch.rand(dim) * 2 - 1).to(dtype)
+    sin = (torch.rand(dim) * 2 - 1).to(dtype)
+    sentinel = -3.0
+    kd, vd = k.to(DEV), v.to(DEV)
+    k_out = torch.full((layers, heads, new_rows + pad_new, dim), sentinel, dtype=dtype, device=DEV)
+    v_out = torch.full_like(k_out, sentinel)
+    L = lib.load()
+    lib.check(L.kvr_shift_cache_layers(lib.ptr_array([kd[i] for i in range(layers)]),
+                                       lib.ptr_array([vd[i] for i in range(layers)]),
+                                       lib.ptr_array([k_out[i] for i in range(layers)]),
+                                       lib.ptr_array([v_out[i] for i in range(layers)]), layers, heads, dim,
+                                       new_rows, prefix, old_tail, new_tail, (old_rows + pad_old) * dim, dim,
+                                       (new_rows + pad_new) * dim, dim, _rope_table(cos, sin).data_ptr(), 1,
+                                       lib.dtype_code(dtype), lib.stream_handle()), "shift")
+    torch.cuda.synchronize()
+    tail = k[:, :, old_tail:old_rows]
+    rot = torch.cat((-tail[..., dim // 2:], tail[..., : dim // 2]), dim=-1)
+    expected_k = torch.full((layers, heads, new_rows + pad_new, dim), sentinel, dtype=dtype)
+    expected_v = expected_k.clone()
+    expected_k[:, :, :prefix] = k[:, :, :prefix]
+    expected_k[:, :, new_tail:new_rows] = tail * cos + rot * sin
+    expected_v[:, :, :prefix] = v[:, :, :prefix]
+    expected_v[:, :, new_tail:new_rows] = v[:, :, old_tail:old_rows]
+    assert bits_equal(k_out.cpu(), expected_k)
+    assert bits_equal(v_out.cpu(), expected_v)
+
+
 @pytest.mark.parametrize("dense", [True, False])
 def test_copy_layers_is_bitwise(lib, dense):
     torch.manual_seed(2)
