@@ -9,6 +9,8 @@
 // blockIdx.x.
 #include <stdio.h>
 
+#include <algorithm>
+
 #include "kvr_common.cuh"
 
 namespace kvr {
@@ -171,135 +173,118 @@ struct ShiftPtrs {
   void* v_new[KVR_MAX_LAYER_TENSORS / 2];
 };
 
-// One persistent grid walks all (layer, head, component) segments as one flat
-// sequence of "pairs" (an 8-element vector of a row's low half and its partner
-// in the high half), so every SM moves the same number of bytes whatever the
-// segment count. The grid stride is a multiple of the pairs per row, so a
-// thread always handles the same pair index j of its rows. cos/sin sit in
-// shared memory as one 16-byte (cos_lo, sin_lo, cos_hi, sin_hi) entry per
-// element, padded to 9 entries per pair index so that the 8 pair indices of a
-// warp read disjoint banks.
+// The grid covers all (layer, head, component) segments as one flat sequence
+// of "pairs" (a vector of a row's low half and its partner in the high half,
+// so rotate_half needs no data exchange): one short CTA per 256 pairs, one
+// pair per thread, VB-byte vectors (32 when every pointer and stride allows
+// 256-bit accesses, else 16). CTAs of 256 threads are a multiple of the pairs
+// per row, so a thread's pair index is its thread index modulo that count.
+// cos/sin sit in shared memory as one 16-byte (cos_lo, sin_lo, cos_hi,
+// sin_hi) entry per element, padded by one entry per pair index so that the
+// pair indices of a warp read disjoint banks.
 //
-// Each thread streams its pairs through a private ring in shared memory:
-// kShiftStages stages of kShiftUnroll pairs, filled by 16-byte cp.async copies
-// (L2 only), so the next stages' loads stay in flight while the thread
-// rotates and stores the oldest one. With 4 CTAs per SM that keeps about
-// 190 KB of loads outstanding per SM; a register version that issued a batch
-// of loads, then its stores, held half of that on average and reached 0.85 of
-// the copy peak against 0.91 for the ring. A thread reads back only its own
-// copies (cp.async.wait_group), so the loop needs no CTA barrier.
+// Measured at config 2 (32 layers, 2.08 GB): 309 us = 1.04 of the measured
+// copy peak, launched with the driver's L1 / shared-memory split; the same
+// kernel under the largest shared-memory split, and persistent grids (all of
+// a thread's loads in flight, then its stores; or a per-thread cp.async ring
+// in shared memory), took 350-380 us. The old rows are read through the
+// non-coherent path, so the new tensors must not overlap them.
 constexpr int kShiftThreads = 256;
-constexpr int kShiftUnroll = 2;  // pairs per stage
-constexpr int kShiftStages = 3;  // stages per thread's ring
-constexpr int kShiftRingBytes = kShiftStages * kShiftUnroll * 2 * kShiftThreads * 16;  // 48 KB
 
-// Source and destination of pair i (pair index j) of the flat sequence, or
-// false for a row the caller recomputes (rows in [prefix, new_tail)).
-template <int D>
-__device__ __forceinline__ bool shift_pair(const ShiftPtrs& ptrs, const ShiftArgs& a, uint32_t i, uint32_t per_seg,
-                                           int j, const uint16_t*& src, uint16_t*& dst, bool& rot) {
-  constexpr int PAIRS = D / 16;
+template <int VB>
+struct ShiftVec {
+  uint32_t w[VB / 4];
+};
+
+template <int VB>
+__device__ __forceinline__ ShiftVec<VB> ld_shift(const void* p) {
+  ShiftVec<VB> v;
+  if constexpr (VB == 32) {
+    asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                   "=r"(v.w[6]), "=r"(v.w[7])
+                 : "l"(p));
+  } else {
+    asm volatile("ld.global.nc.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+                 : "l"(p));
+  }
+  return v;
+}
+
+template <int VB>
+__device__ __forceinline__ void st_shift(void* p, const ShiftVec<VB>& v) {
+  if constexpr (VB == 32) {
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
+                 "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]), "r"(v.w[7])
+                 : "memory");
+  } else {
+    asm volatile("st.global.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]), "r"(v.w[2]),
+                 "r"(v.w[3])
+                 : "memory");
+  }
+}
+
+template <class T, int D, int VB>
+__global__ void __launch_bounds__(kShiftThreads) shift_cache_kernel(ShiftPtrs ptrs, ShiftArgs a,
+                                                                 const uint16_t* __restrict__ cos_sin) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
+  constexpr int EV = VB / 2;           // 16-bit elements per vector
+  constexpr int PAIRS = D / (2 * EV);  // vector pairs per row
+  constexpr int HALF = D / 2;
+  constexpr int PAD = EV + 1;
+  static_assert(kShiftThreads % PAIRS == 0, "a CTA covers whole rows");
+  __shared__ float4 cs4[PAIRS * PAD];  // [pair index][element (+1 pad)] = (cos_lo, sin_lo, cos_hi, sin_hi)
+  if (a.apply_rope) {  // the table is only non-null when the tail rotates
+    for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
+      cs4[(i / EV) * PAD + (i % EV)] = make_float4(T::to_f(cos_sin[i]), T::to_f(cos_sin[D + i]),
+                                                  T::to_f(cos_sin[HALF + i]), T::to_f(cos_sin[D + HALF + i]));
+    }
+  }
+  __syncthreads();
+  const int j = threadIdx.x % PAIRS;
+  const uint32_t per_seg = static_cast<uint32_t>(a.new_rows) * PAIRS;
+  const uint32_t i = blockIdx.x * kShiftThreads + threadIdx.x;  // < 2^32 (host-checked)
+  if (i >= per_seg * static_cast<uint32_t>(a.segments)) return;
   const uint32_t seg = i / per_seg;
   const int64_t r = (i - seg * per_seg) / PAIRS;
   const int comp = seg & 1;
   const int lh = seg >> 1;
   const int l = lh / a.heads;
   const int h = lh - l * a.heads;
-  int64_t sr = -1;
+  int64_t sr;
   if (r < a.prefix) sr = r;
   else if (r >= a.new_tail) sr = r - a.new_tail + a.old_tail;
-  if (sr < 0) return false;
-  rot = comp == 0 && a.apply_rope && r >= a.new_tail;
-  src = static_cast<const uint16_t*>(comp ? ptrs.v_old[l] : ptrs.k_old[l]) + h * a.old_hs + sr * a.old_rs + j * 8;
-  dst = static_cast<uint16_t*>(comp ? ptrs.v_new[l] : ptrs.k_new[l]) + h * a.new_hs + r * a.new_rs + j * 8;
-  return true;
-}
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
-}
-
-template <class T, int D>
-__global__ void __launch_bounds__(kShiftThreads, 4) shift_cache_kernel(ShiftPtrs ptrs, ShiftArgs a,
-                                                                    const uint16_t* __restrict__ cos_sin) {
-  pdl_launch_dependents();  // the next kernel may start its independent prologue
-  pdl_wait();  // every input may come from the previous kernel
-  constexpr int PAIRS = D / 16;
-  constexpr int HALF = D / 2;
-  constexpr int U = kShiftUnroll;
-  constexpr int S = kShiftStages;
-  extern __shared__ uint4 ring[];  // [stage][2U vectors][thread]: each warp's 16-byte slots are contiguous
-  __shared__ float4 cs4[PAIRS * 9];  // [pair index][element (+1 pad)] = (cos_lo, sin_lo, cos_hi, sin_hi)
-  const uint32_t tid0 = blockIdx.x * blockDim.x + threadIdx.x;
-  const uint32_t step = gridDim.x * blockDim.x;  // multiple of PAIRS (host-checked)
-  const int j = static_cast<int>(tid0 % PAIRS);
-  const int t = threadIdx.x;
-  if (a.apply_rope) {  // the table is only non-null when the tail rotates
-    for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
-      cs4[(i >> 3) * 9 + (i & 7)] = make_float4(T::to_f(cos_sin[i]), T::to_f(cos_sin[D + i]),
-                                               T::to_f(cos_sin[HALF + i]), T::to_f(cos_sin[D + HALF + i]));
+  else return;  // rows in [prefix, new_tail) are recomputed by the caller
+  const uint16_t* src = static_cast<const uint16_t*>(comp ? ptrs.v_old[l] : ptrs.k_old[l]) + h * a.old_hs +
+                        sr * a.old_rs + j * EV;
+  uint16_t* dst = static_cast<uint16_t*>(comp ? ptrs.v_new[l] : ptrs.k_new[l]) + h * a.new_hs + r * a.new_rs +
+                  j * EV;
+  const ShiftVec<VB> lo = ld_shift<VB>(src);
+  const ShiftVec<VB> hi = ld_shift<VB>(src + HALF);
+  if (comp == 0 && a.apply_rope && r >= a.new_tail) {
+    const float4* csj = cs4 + j * PAD;
+    const uint16_t* xl = reinterpret_cast<const uint16_t*>(lo.w);
+    const uint16_t* xh = reinterpret_cast<const uint16_t*>(hi.w);
+    ShiftVec<VB> olo, ohi;
+    uint16_t* ol = reinterpret_cast<uint16_t*>(olo.w);
+    uint16_t* oh = reinterpret_cast<uint16_t*>(ohi.w);
+#pragma unroll
+    for (int e = 0; e < EV; ++e) {
+      const float fl = T::to_f(xl[e]);
+      const float fh = T::to_f(xh[e]);
+      // d < D/2: rotate_half = -x[d + D/2];  d >= D/2: rotate_half = x[d - D/2].
+      const float4 c = csj[e];
+      ol[e] = rope_elem_hw<T>(fl, -fh, c.x, c.y);
+      oh[e] = rope_elem_hw<T>(fh, fl, c.z, c.w);
     }
+    st_shift<VB>(dst, olo);
+    st_shift<VB>(dst + HALF, ohi);
+  } else {
+    st_shift<VB>(dst, lo);
+    st_shift<VB>(dst + HALF, hi);
   }
-  __syncthreads();
-  const float4* csj = cs4 + j * 9;
-  const uint32_t per_seg = static_cast<uint32_t>(a.new_rows) * PAIRS;
-  const uint32_t total = per_seg * a.segments;
-  // Stage k holds pairs tid0 + (k * U + u) * step, u < U. Every stage commits
-  // one cp.async group (empty past the end), so wait_group<S - 1> after
-  // issuing stage k + S - 1 means stage k has landed.
-  auto issue = [&](uint32_t k) {
-    uint4* slot = ring + (k % S) * (2 * U * kShiftThreads) + t;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const uint32_t i = tid0 + (k * U + u) * step;
-      const uint16_t* src;
-      uint16_t* dst;
-      bool rot;
-      if (i < total && shift_pair<D>(ptrs, a, i, per_seg, j, src, dst, rot)) {
-        cp_async16(slot + (2 * u) * kShiftThreads, src);
-        cp_async16(slot + (2 * u + 1) * kShiftThreads, src + HALF);
-      }
-    }
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-  };
-  const uint32_t iters = total > tid0 ? (total - tid0 + U * step - 1) / (U * step) : 0;
-#pragma unroll
-  for (int k = 0; k < S - 1; ++k) issue(k);
-  for (uint32_t k = 0; k < iters; ++k) {
-    issue(k + S - 1);
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(S - 1) : "memory");
-    const uint4* slot = ring + (k % S) * (2 * U * kShiftThreads) + t;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const uint32_t i = tid0 + (k * U + u) * step;
-      const uint16_t* src;
-      uint16_t* dst;
-      bool rot;
-      if (!(i < total && shift_pair<D>(ptrs, a, i, per_seg, j, src, dst, rot))) continue;
-      Vec8 lo, hi;
-      *reinterpret_cast<uint4*>(&lo) = slot[(2 * u) * kShiftThreads];
-      *reinterpret_cast<uint4*>(&hi) = slot[(2 * u + 1) * kShiftThreads];
-      if (rot) {
-        Vec8 olo, ohi;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float xl = T::to_f(lo.h[e]);
-          const float xh = T::to_f(hi.h[e]);
-          // d < D/2: rotate_half = -x[d + D/2];  d >= D/2: rotate_half = x[d - D/2].
-          const float4 c = csj[e];
-          olo.h[e] = rope_elem_hw<T>(xl, -xh, c.x, c.y);
-          ohi.h[e] = rope_elem_hw<T>(xh, xl, c.z, c.w);
-        }
-        st_vec8_stream(dst, olo);
-        st_vec8_stream(dst + HALF, ohi);
-      } else {
-        st_vec8_stream(dst, lo);
-        st_vec8_stream(dst + HALF, hi);
-      }
-    }
-  }
-  asm volatile("cp.async.wait_group 0;\n" ::: "memory");  // only empty groups remain; none may outlive the CTA
 }
 
 // ---------------------------------------------------------------------------
@@ -397,48 +382,13 @@ namespace {
 
 bool valid_dtype(int dtype) { return dtype == KVR_DTYPE_BF16 || dtype == KVR_DTYPE_F16; }
 
-// Once per device: lets `kernel` (256 threads) take `smem` bytes of dynamic
-// shared memory, prefers the largest shared-memory carveout, and returns how
-// many of its CTAs are resident on all SMs at once (the grid of a persistent
-// kernel); 0 when the device refused the attribute (its error is recorded).
-template <auto kernel>
-int resident_blocks(int smem) {
-  static int cache[64] = {0};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    set_last_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidDevice);
-    cudaGetLastError();
-    return 0;
-  }
-  int n = __atomic_load_n(&cache[dev], __ATOMIC_ACQUIRE);
-  if (!n) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) {
-      set_last_cuda_error(e);
-      cudaGetLastError();
-      return 0;
-    }
-    prefer_shared_once<kernel>();
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem) != cudaSuccess || per_sm < 1) {
-      cudaGetLastError();
-      per_sm = 1;
-    }
-    n = per_sm * kNumSMs;
-    __atomic_store_n(&cache[dev], n, __ATOMIC_RELEASE);
-  }
-  return n;
-}
+bool aligned32(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 31u) == 0; }
 
-// The shift kernel on as many CTAs as are resident at once, at most `need`.
+// A kernel as a type, so that one generic lambda can launch any of them.
 template <auto kernel>
-int launch_shift(int64_t need, cudaStream_t s, const ShiftPtrs& p, const ShiftArgs& a, const uint16_t* cs) {
-  const int resident = resident_blocks<kernel>(kShiftRingBytes);
-  if (resident <= 0) return KVR_ERR_CUDA;
-  const dim3 grid(static_cast<unsigned>(need < resident ? need : resident));
-  return launch_pdl<kernel>(grid, dim3(kShiftThreads), kShiftRingBytes, s, 1, p, a, cs);
-}
+struct Kernel {
+  static constexpr auto value = kernel;
+};
 
 int blocks_per_segment(int64_t segment_vecs, int segments, int threads) {
   // Enough CTAs in total for ~8 resident per SM, never more than the work.
@@ -509,7 +459,8 @@ int kvr_copy_layers(const void* const* src, void* const* dst, int num_tensors, i
   a.chunks = a.chunks_per_seg * num_tensors * heads;
   if (a.chunks > 0x7fffffffLL) return KVR_ERR_UNSUPPORTED;
   dim3 grid(static_cast<unsigned>(a.chunks));
-  return launch_pdl<copy_layers_kernel>(grid, dim3(kCopyThreads), 0, static_cast<cudaStream_t>(stream), 1, p, a);
+  return launch_pdl_default_carveout<copy_layers_kernel>(grid, dim3(kCopyThreads), 0,
+                                                         static_cast<cudaStream_t>(stream), 1, p, a);
 }
 
 int kvr_rope_shift_layers(const void* const* src, void* const* dst, int num_layers, int heads,
@@ -539,11 +490,15 @@ int kvr_rope_shift_layers(const void* const* src, void* const* dst, int num_laye
   const uint16_t* cs = static_cast<const uint16_t*>(cos_sin);
   int st = KVR_OK;
   if (dtype == KVR_DTYPE_BF16) {
-    if (head_dim == 128) st = launch_pdl<rope_shift_kernel<BF16, 128>>(grid, dim3(256), 0, s, 1, p, a, cs);
-    else st = launch_pdl<rope_shift_kernel<BF16, 64>>(grid, dim3(256), 0, s, 1, p, a, cs);
+    if (head_dim == 128) st = launch_pdl_default_carveout<rope_shift_kernel<BF16, 128>>(
+        grid, dim3(256), 0, s, 1, p, a, cs);
+    else st = launch_pdl_default_carveout<rope_shift_kernel<BF16, 64>>(
+        grid, dim3(256), 0, s, 1, p, a, cs);
   } else {
-    if (head_dim == 128) st = launch_pdl<rope_shift_kernel<F16, 128>>(grid, dim3(256), 0, s, 1, p, a, cs);
-    else st = launch_pdl<rope_shift_kernel<F16, 64>>(grid, dim3(256), 0, s, 1, p, a, cs);
+    if (head_dim == 128) st = launch_pdl_default_carveout<rope_shift_kernel<F16, 128>>(
+        grid, dim3(256), 0, s, 1, p, a, cs);
+    else st = launch_pdl_default_carveout<rope_shift_kernel<F16, 64>>(
+        grid, dim3(256), 0, s, 1, p, a, cs);
   }
   return st;
 }
@@ -577,22 +532,28 @@ int kvr_shift_cache_layers(const void* const* k_old, const void* const* v_old, v
   const int segs = num_layers * heads * 2;
   ShiftArgs a{heads, segs, new_rows, prefix, old_tail_start, new_tail_start,
               old_head_stride, old_row_stride, new_head_stride, new_row_stride, apply_rope};
-  const int64_t pairs = new_rows * (head_dim / 16);
-  // 32-bit pair index: the issue side runs up to kShiftStages stages past the
-  // end of a thread's pairs (grid of at most 4 CTAs per SM).
-  if (pairs * segs + (kShiftStages + 1LL) * kShiftUnroll * 4 * kNumSMs * kShiftThreads > 0xffffffffLL)
-    return KVR_ERR_UNSUPPORTED;
-  // Persistent: as many CTAs of 256 threads as are resident at once (the grid
-  // stride, a multiple of 256, is then a multiple of the pairs per row).
-  const int64_t need = (pairs * segs + kShiftThreads - 1) / kShiftThreads;
+  const bool wide = (old_row_stride | new_row_stride | old_head_stride | new_head_stride) % 16 == 0 &&
+                    std::all_of(p.k_old, p.k_old + num_layers, aligned32) &&
+                    std::all_of(p.v_old, p.v_old + num_layers, aligned32) &&
+                    std::all_of(p.k_new, p.k_new + num_layers, aligned32) &&
+                    std::all_of(p.v_new, p.v_new + num_layers, aligned32);
+  const int64_t pairs = new_rows * (head_dim / (wide ? 32 : 16)) * segs;
+  if (pairs > 0xffffffffLL) return KVR_ERR_UNSUPPORTED;  // 32-bit pair index
+  const dim3 grid(static_cast<unsigned>((pairs + kShiftThreads - 1) / kShiftThreads));
   auto s = static_cast<cudaStream_t>(stream);
   const uint16_t* cs = static_cast<const uint16_t*>(cos_sin);
+  auto go = [&](auto kernel) {
+    return launch_pdl_default_carveout<decltype(kernel)::value>(grid, dim3(kShiftThreads), 0, s, 1, p, a, cs);
+  };
   if (dtype == KVR_DTYPE_BF16) {
-    if (head_dim == 128) return launch_shift<shift_cache_kernel<BF16, 128>>(need, s, p, a, cs);
-    return launch_shift<shift_cache_kernel<BF16, 64>>(need, s, p, a, cs);
+    if (head_dim == 128)
+      return wide ? go(Kernel<shift_cache_kernel<BF16, 128, 32>>{})
+                  : go(Kernel<shift_cache_kernel<BF16, 128, 16>>{});
+    return wide ? go(Kernel<shift_cache_kernel<BF16, 64, 32>>{}) : go(Kernel<shift_cache_kernel<BF16, 64, 16>>{});
   }
-  if (head_dim == 128) return launch_shift<shift_cache_kernel<F16, 128>>(need, s, p, a, cs);
-  return launch_shift<shift_cache_kernel<F16, 64>>(need, s, p, a, cs);
+  if (head_dim == 128)
+    return wide ? go(Kernel<shift_cache_kernel<F16, 128, 32>>{}) : go(Kernel<shift_cache_kernel<F16, 128, 16>>{});
+  return wide ? go(Kernel<shift_cache_kernel<F16, 64, 32>>{}) : go(Kernel<shift_cache_kernel<F16, 64, 16>>{});
 }
 
 int kvr_scatter_rows(const void* k_fresh, const void* v_fresh, void* k_cache, void* v_cache,

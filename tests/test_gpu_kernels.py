@@ -121,23 +121,27 @@ def test_shift_cache_special_values_match_torch_ops(lib, dtype):
         assert bits_equal(v_new[i][0].cpu()[:, new_tail:], v[i, :, old_tail:])
 
 
-@pytest.mark.parametrize("dtype, dim", [(torch.bfloat16, 64), (torch.float16, 64), (torch.bfloat16, 128)])
-def test_shift_cache_gap_rows_strides_and_many_grid_strides(lib, dtype, dim):
+@pytest.mark.parametrize("dtype, dim, row_pad", [(torch.bfloat16, 64, 0), (torch.float16, 64, 0),
+                                                  (torch.bfloat16, 128, 0), (torch.bfloat16, 128, 8),
+                                                  (torch.float16, 64, 8)])
+def test_shift_cache_gap_rows_strides_and_large_caches(lib, dtype, dim, row_pad):
     """Rows in [prefix, new_tail) are left to the caller (never written), head
-    planes padded beyond their rows are read and written through their
-    strides, and a cache large enough that every thread walks many grid
-    strides matches torch's ops bit for bit (cache.py:47-77,103-144)."""
-    torch.manual_seed(12 + dim)
+    planes padded beyond their rows (and, with row_pad, old rows padded beyond
+    head_dim: 16-byte instead of 32-byte accesses) are read and written through
+    their strides, and a cache of tens of thousands of CTAs matches torch's ops
+    bit for bit (cache.py:47-77,103-144)."""
+    torch.manual_seed(12 + dim + row_pad)
     layers, heads, old_rows = 4, 8, 3001
     prefix, old_tail, new_tail = 700, 1037, 709  # 9 rows for the caller, 328 deleted
     new_rows = old_rows - (old_tail - new_tail)
     pad_old, pad_new = 24, 40  # unused rows at the end of every head plane
-    k = torch.randn(layers, heads, old_rows + pad_old, dim).to(dtype)
-    v = torch.randn(layers, heads, old_rows + pad_old, dim).to(dtype)
+    k_rows = torch.randn(layers, heads, old_rows + pad_old, dim + row_pad).to(dtype)
+    v_rows = torch.randn(layers, heads, old_rows + pad_old, dim + row_pad).to(dtype)
+    k, v = k_rows[..., :dim], v_rows[..., :dim]
     cos = (torch.rand(dim) * 2 - 1).to(dtype)
     sin = (torch.rand(dim) * 2 - 1).to(dtype)
     sentinel = -3.0
-    kd, vd = k.to(DEV), v.to(DEV)
+    kd, vd = k_rows.to(DEV)[..., :dim], v_rows.to(DEV)[..., :dim]
     k_out = torch.full((layers, heads, new_rows + pad_new, dim), sentinel, dtype=dtype, device=DEV)
     v_out = torch.full_like(k_out, sentinel)
     L = lib.load()
@@ -145,8 +149,9 @@ def test_shift_cache_gap_rows_strides_and_many_grid_strides(lib, dtype, dim):
                                        lib.ptr_array([vd[i] for i in range(layers)]),
                                        lib.ptr_array([k_out[i] for i in range(layers)]),
                                        lib.ptr_array([v_out[i] for i in range(layers)]), layers, heads, dim,
-                                       new_rows, prefix, old_tail, new_tail, (old_rows + pad_old) * dim, dim,
-                                       (new_rows + pad_new) * dim, dim, _rope_table(cos, sin).data_ptr(), 1,
+                                       new_rows, prefix, old_tail, new_tail, (old_rows + pad_old) * (dim + row_pad),
+                                       dim + row_pad, (new_rows + pad_new) * dim, dim,
+                                       _rope_table(cos, sin).data_ptr(), 1,
                                        lib.dtype_code(dtype), lib.stream_handle()), "shift")
     torch.cuda.synchronize()
     tail = k[:, :, old_tail:old_rows]
