@@ -94,9 +94,9 @@ GRAPH_WARMUP = 6
 # DRAM traffic of one RoPE-fix launch at config 2: dram__bytes_read.sum +
 # dram__bytes_write.sum of one ncu capture (one pass) of the full 32-layer
 # launch of kvr_shift_cache_layers at this geometry (2.080 GB algorithmic).
-ROPE_TRAFFIC = int(1.040e9 + 989.02e6)
+ROPE_TRAFFIC = int(1.040e9 + 984.19e6)
 ROPE_TRAFFIC_NOTE = ("ncu dram__bytes_read.sum (1.040 GB, the algorithmic reads) + dram__bytes_write.sum "
-                     "(0.989 GB) of one full 32-layer launch at this geometry; the ~51 MB of writes not counted "
+                     "(0.984 GB) of one full 32-layer launch at this geometry; the ~56 MB of writes not counted "
                      "were still in L2 when the launch ended")
 
 
