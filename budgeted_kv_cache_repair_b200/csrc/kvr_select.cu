@@ -49,7 +49,15 @@ __device__ __forceinline__ void load8(const void* base, int64_t i, float (&v)[8]
 template <class T>
 struct Raw8 {
   Vec8 x;
-  __device__ __forceinline__ void load(const void* base, int64_t i) { x = ld_vec8(static_cast<const uint16_t*>(base) + i); }
+  // The table is read-only here and a row is read once per pass: no L1
+  // allocation (3 % faster than plain loads on the Qwen3-8B table).
+  __device__ __forceinline__ void load(const void* base, int64_t i) {
+    uint4 u;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                 : "l"(static_cast<const uint16_t*>(base) + i));
+    *reinterpret_cast<uint4*>(&x) = u;
+  }
   __device__ __forceinline__ float get(int e) const { return T::to_f(x.h[e]); }
 };
 template <>
@@ -287,8 +295,9 @@ int launch(const void* embed, int64_t vocab, int hidden, const int64_t* prompt_i
   const int64_t groups = (n + kTokens - 1) / kTokens;
   const int64_t want = (groups + kScoreThreads / 32 - 1) / (kScoreThreads / 32);
   const unsigned blocks = static_cast<unsigned>(want < kNumSMs ? want : kNumSMs);
-  return launch_pdl<relevance_kernel<E>>(dim3(blocks), dim3(kScoreThreads), smem, s, 1, e, vocab, hidden, prompt_ids,
-                                         n, query_ids, nq, static_cast<const float*>(qn), qb, boost, scores, status);
+  return launch_pdl_default_carveout<relevance_kernel<E>>(dim3(blocks), dim3(kScoreThreads), smem, s, 1, e, vocab,
+                                                         hidden, prompt_ids, n, query_ids, nq,
+                                                         static_cast<const float*>(qn), qb, boost, scores, status);
 }
 
 }  // namespace sel
