@@ -701,7 +701,7 @@ def our_arm(args):
     readback = torch.empty(picked.shape, dtype=picked.dtype).pin_memory()
 
     # The output cache's layers are views of one [2L, 1, H, N, D] block
-    # (cache.allocate_layers): one gather takes every refreshed K and V row of
+    # (cache.allocate_arena): one gather takes every refreshed K and V row of
     # every layer; per-layer gathers otherwise.
     picked_block = picked.view(2 * cfg["layers"], 1, cfg["kv_heads"], rows, cfg["head_dim"])
     # The device-to-host copy of step k runs on its own stream under step

@@ -9,6 +9,8 @@ multi-layer kernel each. Inputs are never modified; outputs own new storage.
 
 from __future__ import annotations
 
+import operator
+from itertools import repeat
 from typing import Any
 
 import torch
@@ -78,16 +80,28 @@ def _uniform_strides(tensors, what):
     return strides.pop()
 
 
-def allocate_layers(count: int, heads: int, rows: int, dim: int, dtype, device):
-    """``count`` new ``(K, V)`` pairs of ``[1, heads, rows, dim]``, contiguous.
+def allocate_arena(count: int, heads: int, rows: int, dim: int, dtype, device) -> torch.Tensor:
+    """One contiguous ``[2 * count, 1, heads, rows, dim]`` block for ``count``
+    ``(K, V)`` pairs (K of layer l at index 2l, V at 2l + 1): a request costs
+    one allocator call instead of two per layer."""
+    return torch.empty((count * 2, 1, heads, rows, dim), dtype=dtype, device=device)
 
-    One allocation backs every layer (per-layer tensors are views of it), so a
-    request costs one allocator call instead of two per layer. The block is
-    released once no layer of the cache is referenced any more.
-    """
-    arena = torch.empty((count * 2, 1, heads, rows, dim), dtype=dtype, device=device)
+
+def arena_layers(arena: torch.Tensor):
+    """The ``(K, V)`` pairs of ``[1, heads, rows, dim]`` that an arena holds, as
+    views of it; the block is released once no view is referenced any more."""
     views = arena.unbind(0)
-    return [(views[2 * i], views[2 * i + 1]) for i in range(count)]
+    return [(views[2 * i], views[2 * i + 1]) for i in range(len(views) // 2)]
+
+
+def allocate_layers(count: int, heads: int, rows: int, dim: int, dtype, device):
+    """``count`` new ``(K, V)`` pairs of ``[1, heads, rows, dim]``, contiguous
+    views of one allocation (``allocate_arena``)."""
+    return arena_layers(allocate_arena(count, heads, rows, dim, dtype, device))
+
+
+_dtype_of = operator.attrgetter("dtype")
+_device_of = operator.attrgetter("device")
 
 
 def uniform_layout(pairs, what: str):
@@ -98,8 +112,16 @@ def uniform_layout(pairs, what: str):
     require_cuda_tensors([first], what)
     _check_kv_layout([first], what)
     shape, stride, dtype, device = first.shape, first.stride(), first.dtype, first.device
-    for pair in pairs:
-        for t in pair:
+    tensors = [t for pair in pairs for t in pair]
+    try:  # one pass per property over all tensors; any non-tensor takes the loop below
+        uniform = (set(map(type, tensors)) == {type(first)} and set(map(torch.Tensor.size, tensors)) == {shape}
+                   and set(map(torch.Tensor.stride, tensors)) == {stride}
+                   and set(map(_dtype_of, tensors)) == {dtype} and set(map(_device_of, tensors)) == {device})
+        aligned = uniform and not any(map(operator.mod, map(torch.Tensor.data_ptr, tensors), repeat(16)))
+    except (TypeError, AttributeError):
+        uniform = aligned = False
+    if not aligned:
+        for t in tensors:
             if t.shape != shape or t.stride() != stride or t.dtype != dtype or t.device != device:
                 raise ValueError(f"{what}: every layer must share one shape, stride pair, dtype and device")
             if t.data_ptr() % 16:

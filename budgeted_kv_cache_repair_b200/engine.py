@@ -37,6 +37,8 @@ them from a graph captured on the second such call.
 
 from __future__ import annotations
 
+import ctypes
+import operator
 import threading
 import weakref
 from collections import OrderedDict
@@ -272,16 +274,24 @@ def model_view(base) -> ModelView:
     return view
 
 
+_version_of = operator.attrgetter("_version")
+
+
 def _native_model(view: ModelView):
-    """The kvr_model struct for this view, refreshed when fused weights were rebuilt."""
-    qkv = [w.fused_qkv() for w in view.layers]
-    flat = getattr(view, "_flat", None)
-    if flat is None:
-        flat = view._flat = [view.embed] + [t for w in view.layers
-                                            for t in (w.in_norm, w.o, w.post_norm, w.gate, w.up, w.down)]
-    # Any replaced parameter storage changes a data pointer: rebuild the struct.
-    key = tuple(map(torch.Tensor.data_ptr, qkv)) + tuple(map(torch.Tensor.data_ptr, flat))
+    """The kvr_model struct for this view, rebuilt when a weight's storage moved
+    or q/k/v (whose fused copy the engine owns) changed in place."""
+    watched = getattr(view, "_watched", None)
+    if watched is None:
+        watched = view._watched = [view.embed] + [
+            t for w in view.layers
+            for t in (w.in_norm, w.q, w.k, w.v, w.o, w.post_norm, w.gate, w.up, w.down, w.q_norm, w.k_norm)
+            if t is not None]
+        view._qkv_sources = [t for w in view.layers for t in (w.q, w.k, w.v)]
+    # One pass over every weight's data pointer and over q/k/v's version
+    # counters (the fused copies' keys hold the same facts per layer).
+    key = tuple(map(torch.Tensor.data_ptr, watched)) + tuple(map(_version_of, view._qkv_sources))
     if getattr(view, "_native_key", None) != key:
+        qkv = [w.fused_qkv() for w in view.layers]
         arr = (_lib.LayerWeights * len(view.layers))()
         for i, (w, fused) in enumerate(zip(view.layers, qkv)):
             arr[i] = _lib.LayerWeights(
@@ -337,7 +347,10 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions,
     """Recompute the selected rows through every layer, writing K/V in place.
 
     ``layers``: the owned output cache, ``[(K, V)]`` each ``[1, Hkv, N, D]``
-    with unit D stride and one (head, row) stride pair; ``ids``: ``[N]`` int64
+    with unit D stride and one (head, row) stride pair, or a contiguous
+    ``[2L, 1, Hkv, N, D]`` arena holding them (``cache.allocate_arena``: K of
+    layer l at 2l, V at 2l + 1), whose layer addresses follow from its base
+    address so that no per-layer view is needed; ``ids``: ``[N]`` int64
     on the device, or in pinned host memory (copied once, into the request's
     staged buffer); ``positions``: ``[B]`` sorted, a device int64 tensor or
     host integers validated by the caller (an ``IndexedPlan``'s). One
@@ -349,17 +362,31 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions,
     """
     lib = _lib.load()
     host_positions = not isinstance(positions, torch.Tensor)
-    device = layers[0][0].device
     if ids.device.type == "cpu" and not (ids.dtype == torch.int64 and ids.is_pinned()):
         raise ValueError("host ids must be pinned int64")
     rows = len(positions) if host_positions else positions.numel()
-    strides = {(t.stride(1), t.stride(2)) for pair in layers for t in pair}
-    if len(strides) != 1:
-        raise ValueError("every cache layer must share one (head, row) stride pair")
-    head_stride, row_stride = strides.pop()
+    if isinstance(layers, torch.Tensor):
+        arena = layers
+        if arena.dim() != 5 or arena.shape[0] % 2 or arena.shape[1] != 1 or not arena.is_contiguous():
+            raise ValueError("a cache arena must be a contiguous [2L, 1, heads, rows, head_dim] tensor")
+        device, dtype = arena.device, arena.dtype
+        count, heads, dim = arena.shape[0] // 2, arena.shape[2], arena.shape[4]
+        head_stride, row_stride = arena.stride(2), arena.stride(3)
+        plane = arena.stride(0) * arena.element_size()
+        base = arena.data_ptr()
+        k_ptrs = (ctypes.c_void_p * count)(*range(base, base + 2 * count * plane, 2 * plane))
+        v_ptrs = (ctypes.c_void_p * count)(*range(base + plane, base + 2 * count * plane, 2 * plane))
+    else:
+        first = layers[0][0]
+        device, dtype = first.device, first.dtype
+        count, heads, dim = len(layers), first.shape[1], first.shape[3]
+        strides = {(t.stride(1), t.stride(2)) for pair in layers for t in pair}
+        if len(strides) != 1:
+            raise ValueError("every cache layer must share one (head, row) stride pair")
+        head_stride, row_stride = strides.pop()
+        k_ptrs = _lib.ptr_array([k for k, _ in layers])
+        v_ptrs = _lib.ptr_array([v for _, v in layers])
     model = _native_model(view)
-    k_ptrs = _lib.ptr_array([k for k, _ in layers])
-    v_ptrs = _lib.ptr_array([v for _, v in layers])
     request = _lib.RefreshRequest(
         k_cache=k_ptrs, v_cache=v_ptrs, cache_rows=cache_rows, cache_head_stride=head_stride,
         cache_row_stride=row_stride, ids=None, id_count=ids.numel(),
@@ -368,12 +395,10 @@ def refresh_rows(view: ModelView, layers, ids: torch.Tensor, positions,
     if sources is not None:
         from .cache import uniform_layout
 
-        if len(sources) != len(layers):
+        if len(sources) != count:
             raise ValueError("sources must give one (K, V) pair per cache layer")
-        heads, src_rows, dim, dtype, src_device, src_hs, src_rs = uniform_layout(sources, "clone_cache")
-        first = layers[0][0]
-        if (heads, dim, dtype, src_device) != (first.shape[1], first.shape[3], first.dtype, first.device) \
-                or src_rows < cache_rows:
+        src_heads, src_rows, src_dim, src_dtype, src_device, src_hs, src_rs = uniform_layout(sources, "clone_cache")
+        if (src_heads, src_dim, src_dtype, src_device) != (heads, dim, dtype, device) or src_rows < cache_rows:
             raise ValueError("sources must match the cache's heads, head_dim, dtype and device and hold its rows")
         request.k_src = _lib.ptr_array([k for k, _ in sources])
         request.v_src = _lib.ptr_array([v for _, v in sources])

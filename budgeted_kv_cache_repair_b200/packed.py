@@ -15,7 +15,7 @@ from typing import Any, Sequence
 import torch
 
 from . import _lib
-from .cache import allocate_layers, make_cache
+from .cache import allocate_arena, arena_layers, make_cache
 from .engine import model_view, refresh_rows
 from .plan import IndexedPlan
 from .validate import qualify_model, validate_cache, validate_intervals
@@ -164,6 +164,8 @@ def packed_interval_repair(
         # The ownership copy (kernels/packed_cache.py:287) runs inside the
         # refresh call, each layer's copy overlapping earlier layers' work; the
         # validated host positions reach the device there too.
-        owned = allocate_layers(len(layers), view.kv_heads, length, view.head_dim, layers[0][0].dtype, device)
-        refresh_rows(view, owned, ids, selected, selected[-1], length, sources=layers)
-    return make_cache(owned), receipt
+        # The kernels take the output block's layer addresses; its per-layer
+        # views are made after the launch, while the device works.
+        arena = allocate_arena(len(layers), view.kv_heads, length, view.head_dim, layers[0][0].dtype, device)
+        refresh_rows(view, arena, ids, selected, selected[-1], length, sources=layers)
+    return make_cache(arena_layers(arena)), receipt

@@ -8,8 +8,9 @@ api.py:135-166, kernels/writeback.py:6-15).
 from __future__ import annotations
 
 import weakref
+from itertools import repeat
 from numbers import Integral
-from operator import attrgetter, methodcaller
+from operator import attrgetter, is_not
 from typing import Any, Sequence
 
 import torch
@@ -94,9 +95,11 @@ def validate_intervals(intervals: Sequence[tuple[int, int]], logical_length: int
     for interval in intervals:
         if not isinstance(interval, (tuple, list)) or len(interval) != 2:
             raise ValueError("each interval must contain exactly a start and end")
-        if any(isinstance(v, bool) or not isinstance(v, Integral) for v in interval):
-            raise ValueError("interval bounds must be integers, not booleans")
-        start, end = int(interval[0]), int(interval[1])
+        start, end = interval
+        if type(start) is not int or type(end) is not int:  # plain ints skip the ABC checks
+            if any(isinstance(v, bool) or not isinstance(v, Integral) for v in interval):
+                raise ValueError("interval bounds must be integers, not booleans")
+            start, end = int(start), int(end)
         if not 0 <= start < end <= logical_length:
             raise ValueError("interval bounds must satisfy 0 <= start < end <= token length")
         if start <= previous_end:
@@ -163,11 +166,17 @@ _scans: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
 
 
 _training = attrgetter("training")
-_has_forward = methodcaller("__contains__", "forward")
 
 
-def _has_hook(state: dict) -> bool:
-    return state.get("_hf_hook") is not None
+def _any_hook(states) -> bool:
+    """Some module's attribute dict holds a non-None ``_hf_hook`` (an
+    accelerate dispatch/offload hook); the scan runs at C level."""
+    return any(map(is_not, map(dict.get, states, repeat("_hf_hook")), repeat(None)))
+
+
+def _any_forward(states) -> bool:
+    """Some module's attribute dict holds a per-instance ``forward``."""
+    return any(map(dict.__contains__, states, repeat("forward")))
 
 
 def _check_modules(model, base, device, dtype):
@@ -181,9 +190,9 @@ def _check_modules(model, base, device, dtype):
         _scans[model] = scan
     if any(map(_training, scan.modules)):
         raise ValueError("packed executor requires eval mode on all decoder modules")
-    if any(map(_has_hook, scan.states)):
+    if _any_hook(scan.states):
         raise ValueError("packed executor does not support dispatch/offload hooks")
-    if any(map(_has_forward, scan.base_states)):
+    if _any_forward(scan.base_states):
         raise ValueError("packed executor does not support per-instance decoder forward overrides")
     # Parameter placement only needs re-checking when some parameter moved.
     state = (device, dtype, tuple(map(torch.Tensor.data_ptr, scan.param_list)))

@@ -198,7 +198,7 @@ def test_empty_support_returns_base_and_does_no_work(monkeypatch):
 
     monkeypatch.setattr(packed, "qualify_model", forbidden)
     monkeypatch.setattr(packed, "refresh_rows", forbidden)
-    monkeypatch.setattr(packed, "allocate_layers", forbidden)
+    monkeypatch.setattr(packed, "allocate_arena", forbidden)
     monkeypatch.setattr(IndexedPlan, "to", forbidden)
     base = make_cache([(torch.zeros(1, 2, 0, 8), torch.zeros(1, 2, 0, 8)) for _ in range(2)])
     actual, receipt = packed_interval_repair(object(), base, torch.empty((1, 0), dtype=torch.long), [])
@@ -397,3 +397,34 @@ def test_registration_count_ignores_unwatched_and_unhashable_modules():
     Unhashable()
     torch.nn.Linear(3, 3)
     assert registry.epoch() == before
+
+
+def test_module_checks_see_hooks_forwards_and_modes_set_after_a_cached_scan():
+    """The per-call module checks (kernels/packed_cache.py:123-163) run on a
+    scan cached across calls: a dispatch hook, a per-instance forward or train
+    mode set after the scan was built (no registration, so the scan is reused)
+    is still rejected, and a hook attribute that is None is not a hook."""
+    from budgeted_kv_cache_repair_b200 import validate
+
+    model = _tiny_model().to(torch.bfloat16).eval()
+    base = model.model
+    cpu = torch.device("cpu")
+    validate._check_modules(model, base, cpu, torch.bfloat16)  # builds and caches the scan
+    scan = validate._scans[model]
+    mlp = base.layers[1].mlp
+    mlp._hf_hook = None
+    validate._check_modules(model, base, cpu, torch.bfloat16)
+    mlp._hf_hook = object()
+    with pytest.raises(ValueError, match="hooks"):
+        validate._check_modules(model, base, cpu, torch.bfloat16)
+    del mlp._hf_hook
+    base.layers[0].self_attn.forward = lambda *args, **kwargs: None
+    with pytest.raises(ValueError, match="forward overrides"):
+        validate._check_modules(model, base, cpu, torch.bfloat16)
+    del base.layers[0].self_attn.forward
+    base.norm.train()
+    with pytest.raises(ValueError, match="eval mode"):
+        validate._check_modules(model, base, cpu, torch.bfloat16)
+    base.norm.eval()
+    validate._check_modules(model, base, cpu, torch.bfloat16)
+    assert validate._scans[model] is scan
