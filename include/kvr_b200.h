@@ -113,7 +113,9 @@ KVR_API int kvr_rope_shift_layers(const void* const* src, void* const* dst, int 
  *   n >= new_tail_start  : K rotated (as above; copied when apply_rope == 0)
  *                          and V copied from old row n - new_tail_start + old_tail_start
  * Rows in [prefix, new_tail_start) are left untouched (changed boundary tokens,
- * recomputed afterwards). k_old/v_old/k_new/v_new each hold num_layers pointers.
+ * recomputed afterwards). k_old/v_old/k_new/v_new each hold num_layers pointers;
+ * the new tensors must not overlap the old ones (the old rows are read through
+ * the read-only data path while the new ones are written).
  */
 KVR_API int kvr_shift_cache_layers(const void* const* k_old, const void* const* v_old,
                            void* const* k_new, void* const* v_new, int num_layers,
