@@ -1,12 +1,14 @@
 // HBM-bound cache kernels: ownership copy, delta-RoPE positional correction,
 // fused shift cache, indexed row scatter and embedding gather.
 //
-// All of them move 16-byte vectors (8 bf16/fp16) with consecutive threads on
+// All of them move 16- or 32-byte vectors with consecutive threads on
 // consecutive addresses. A "segment" is one (tensor, head) plane of rows*D
-// elements. The copy runs one short CTA per 16 KB chunk and the shift a
-// persistent grid (the CTAs resident on all SMs), both over work units that
-// span every segment; the others index segments with blockIdx.y and rows with
-// blockIdx.x.
+// elements. The copy runs one short CTA per 16 KB chunk, the shift and the
+// delta-RoPE one short CTA per 256 vector pairs, all over work units that
+// span every segment; the scatter walks its (head, row, vector) items in a
+// grid-stride loop and the embedding gather takes one CTA per row. The
+// streaming kernels keep the driver's L1 / shared-memory split
+// (launch_pdl_default_carveout).
 #include <stdio.h>
 
 #include <algorithm>
@@ -100,58 +102,15 @@ __global__ void __launch_bounds__(kCopyThreads) copy_layers_kernel(LayerPtrs ptr
 }
 
 // ---------------------------------------------------------------------------
-// Delta-RoPE (shifted_suffix_keys, cache.py:47-77). Each thread owns one
-// 8-element vector of the low half of a row and its partner in the high half,
-// so rotate_half needs no data exchange.
+// Delta-RoPE (shifted_suffix_keys, cache.py:47-77): every layer's rows
+// rotated in one launch, in the shift kernel's layout (below).
 // ---------------------------------------------------------------------------
 struct RopeArgs {
   int heads;
+  int segments;  // num_layers * heads
   int64_t rows;
   int64_t src_hs, src_rs, dst_hs, dst_rs;
 };
-
-template <class T, int D>
-__device__ __forceinline__ void rope_pair(const uint16_t* src_row, uint16_t* dst_row, int j,
-                                          const float* cs) {
-  constexpr int H = D / 2;
-  Vec8 lo = ld_vec8_stream(src_row + j * 8);
-  Vec8 hi = ld_vec8_stream(src_row + H + j * 8);
-  Vec8 olo, ohi;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const int d = j * 8 + e;
-    const float xl = T::to_f(lo.h[e]);
-    const float xh = T::to_f(hi.h[e]);
-    // d < D/2: rotate_half = -x[d + D/2];  d >= D/2: rotate_half = x[d - D/2].
-    olo.h[e] = rope_elem<T>(xl, -xh, cs[d], cs[D + d]);
-    ohi.h[e] = rope_elem<T>(xh, xl, cs[H + d], cs[D + H + d]);
-  }
-  st_vec8_stream(dst_row + j * 8, olo);
-  st_vec8_stream(dst_row + H + j * 8, ohi);
-}
-
-template <class T, int D>
-__global__ void __launch_bounds__(256) rope_shift_kernel(LayerPtrs ptrs, RopeArgs a,
-                                                         const uint16_t* __restrict__ cos_sin) {
-  pdl_launch_dependents();  // the next kernel may start its independent prologue
-  pdl_wait();  // every input may come from the previous kernel
-  __shared__ float cs[2 * D];
-  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) cs[i] = T::to_f(cos_sin[i]);
-  __syncthreads();
-  const int seg = blockIdx.y;
-  const int l = seg / a.heads;
-  const int h = seg - l * a.heads;
-  const uint16_t* src = static_cast<const uint16_t*>(ptrs.src[l]) + h * a.src_hs;
-  uint16_t* dst = static_cast<uint16_t*>(ptrs.dst[l]) + h * a.dst_hs;
-  constexpr int PAIRS = D / 16;  // vector pairs per row
-  const int64_t n = a.rows * PAIRS;
-  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += step) {
-    const int64_t r = i / PAIRS;  // PAIRS is a power of two: shift
-    const int j = static_cast<int>(i & (PAIRS - 1));
-    rope_pair<T, D>(src + r * a.src_rs, dst + r * a.dst_rs, j, cs);
-  }
-}
 
 // ---------------------------------------------------------------------------
 // Fused shift cache (build_halo_cache, cache.py:103-144, halo 0): prefix rows
@@ -287,6 +246,85 @@ __global__ void __launch_bounds__(kShiftThreads) shift_cache_kernel(ShiftPtrs pt
   }
 }
 
+// Delta-RoPE with the shift kernel's layout: one short CTA per 256 vector
+// pairs over all (layer, head, row), one pair per thread, 32-byte vectors
+// where pointers and strides allow, launched with the driver's L1 split. The
+// rotation may run in place (src == dst): every element is read and written
+// by the same thread, so the loads take the coherent path (not the read-only
+// one) and skip L1 allocation; read-only loads for out-of-place calls
+// measured the same (164.9 against 167.3 us for 0.9 GB).
+template <int VB>
+__device__ __forceinline__ ShiftVec<VB> ld_rope(const void* p) {
+  ShiftVec<VB> v;
+  if constexpr (VB == 32) {
+    asm volatile("ld.global.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                   "=r"(v.w[6]), "=r"(v.w[7])
+                 : "l"(p)
+                 : "memory");
+  } else {
+    asm volatile("ld.global.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+                 : "l"(p)
+                 : "memory");
+  }
+  return v;
+}
+
+template <class T, int D, int VB>
+__global__ void __launch_bounds__(kShiftThreads) rope_shift_kernel(LayerPtrs ptrs, RopeArgs a,
+                                                                const uint16_t* __restrict__ cos_sin) {
+  pdl_launch_dependents();  // the next kernel may start its independent prologue
+  pdl_wait();  // every input may come from the previous kernel
+  constexpr int EV = VB / 2;           // 16-bit elements per vector
+  constexpr int PAIRS = D / (2 * EV);  // vector pairs per row
+  constexpr int HALF = D / 2;
+  constexpr int PAD = EV + 1;
+  static_assert(kShiftThreads % PAIRS == 0, "a CTA covers whole rows");
+  __shared__ float4 cs4[PAIRS * PAD];  // [pair index][element (+1 pad)] = (cos_lo, sin_lo, cos_hi, sin_hi)
+  for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
+    cs4[(i / EV) * PAD + (i % EV)] = make_float4(T::to_f(cos_sin[i]), T::to_f(cos_sin[D + i]),
+                                                T::to_f(cos_sin[HALF + i]), T::to_f(cos_sin[D + HALF + i]));
+  }
+  __syncthreads();
+  const int j = threadIdx.x % PAIRS;
+  const uint32_t per_seg = static_cast<uint32_t>(a.rows) * PAIRS;
+  const uint32_t i = blockIdx.x * kShiftThreads + threadIdx.x;  // < 2^32 (host-checked)
+  if (i >= per_seg * static_cast<uint32_t>(a.segments)) return;
+  const uint32_t seg = i / per_seg;
+  const int64_t r = (i - seg * per_seg) / PAIRS;
+  const int l = static_cast<int>(seg) / a.heads;
+  const int h = static_cast<int>(seg) - l * a.heads;
+  const uint16_t* src = static_cast<const uint16_t*>(ptrs.src[l]) + h * a.src_hs + r * a.src_rs + j * EV;
+  uint16_t* dst = static_cast<uint16_t*>(ptrs.dst[l]) + h * a.dst_hs + r * a.dst_rs + j * EV;
+  const ShiftVec<VB> lo = ld_rope<VB>(src);
+  const ShiftVec<VB> hi = ld_rope<VB>(src + HALF);
+  const float4* csj = cs4 + j * PAD;
+  const uint16_t* xl = reinterpret_cast<const uint16_t*>(lo.w);
+  const uint16_t* xh = reinterpret_cast<const uint16_t*>(hi.w);
+  ShiftVec<VB> olo, ohi;
+  uint16_t* ol = reinterpret_cast<uint16_t*>(olo.w);
+  uint16_t* oh = reinterpret_cast<uint16_t*>(ohi.w);
+#pragma unroll
+  for (int e = 0; e < EV; ++e) {
+    const float fl = T::to_f(xl[e]);
+    const float fh = T::to_f(xh[e]);
+    // d < D/2: rotate_half = -x[d + D/2];  d >= D/2: rotate_half = x[d - D/2].
+    const float4 c = csj[e];
+    ol[e] = rope_elem_hw<T>(fl, -fh, c.x, c.y);
+    oh[e] = rope_elem_hw<T>(fh, fl, c.z, c.w);
+  }
+  st_shift<VB>(dst, olo);
+  st_shift<VB>(dst + HALF, ohi);
+}
+
+template <class T, int D>
+int launch_rope(bool wide, dim3 grid, cudaStream_t s, const LayerPtrs& p, const RopeArgs& a, const uint16_t* cs) {
+  const dim3 block(kShiftThreads);
+  return wide ? launch_pdl_default_carveout<rope_shift_kernel<T, D, 32>>(grid, block, 0, s, 1, p, a, cs)
+              : launch_pdl_default_carveout<rope_shift_kernel<T, D, 16>>(grid, block, 0, s, 1, p, a, cs);
+}
+
 // ---------------------------------------------------------------------------
 // Bitwise scatter (indexed_kv_scatter_ / index_copy_). One warp-slice of
 // D/8 threads per (head, row); positions read once per row.
@@ -390,17 +428,6 @@ struct Kernel {
   static constexpr auto value = kernel;
 };
 
-int blocks_per_segment(int64_t segment_vecs, int segments, int threads) {
-  // Enough CTAs in total for ~8 resident per SM, never more than the work.
-  int64_t total_target = static_cast<int64_t>(kNumSMs) * 8;
-  int64_t per = (total_target + segments - 1) / segments;
-  int64_t need = (segment_vecs + threads - 1) / threads;
-  if (per > need) per = need;
-  if (per < 1) per = 1;
-  if (per > 65535) per = 65535;
-  return static_cast<int>(per);
-}
-
 }  // namespace
 
 extern "C" {
@@ -482,25 +509,21 @@ int kvr_rope_shift_layers(const void* const* src, void* const* dst, int num_laye
     p.src[l] = src[l];
     p.dst[l] = dst[l];
   }
-  RopeArgs a{heads, rows, src_head_stride, src_row_stride, dst_head_stride, dst_row_stride};
   const int segs = num_layers * heads;
-  const int64_t pairs = rows * (head_dim / 16);
-  dim3 grid(blocks_per_segment(pairs / 2, segs, 256), segs);
+  RopeArgs a{heads, segs, rows, src_head_stride, src_row_stride, dst_head_stride, dst_row_stride};
+  const bool wide = (src_row_stride | dst_row_stride | src_head_stride | dst_head_stride) % 16 == 0 &&
+                    std::all_of(p.src, p.src + num_layers, aligned32) &&
+                    std::all_of(p.dst, p.dst + num_layers, aligned32);
+  const int64_t pairs = rows * (head_dim / (wide ? 32 : 16)) * segs;
+  if (pairs > 0xffffffffLL) return KVR_ERR_UNSUPPORTED;  // 32-bit pair index
+  const dim3 grid(static_cast<unsigned>((pairs + kShiftThreads - 1) / kShiftThreads));
   auto s = static_cast<cudaStream_t>(stream);
   const uint16_t* cs = static_cast<const uint16_t*>(cos_sin);
-  int st = KVR_OK;
-  if (dtype == KVR_DTYPE_BF16) {
-    if (head_dim == 128) st = launch_pdl_default_carveout<rope_shift_kernel<BF16, 128>>(
-        grid, dim3(256), 0, s, 1, p, a, cs);
-    else st = launch_pdl_default_carveout<rope_shift_kernel<BF16, 64>>(
-        grid, dim3(256), 0, s, 1, p, a, cs);
-  } else {
-    if (head_dim == 128) st = launch_pdl_default_carveout<rope_shift_kernel<F16, 128>>(
-        grid, dim3(256), 0, s, 1, p, a, cs);
-    else st = launch_pdl_default_carveout<rope_shift_kernel<F16, 64>>(
-        grid, dim3(256), 0, s, 1, p, a, cs);
-  }
-  return st;
+  if (dtype == KVR_DTYPE_BF16)
+    return head_dim == 128 ? launch_rope<BF16, 128>(wide, grid, s, p, a, cs)
+                           : launch_rope<BF16, 64>(wide, grid, s, p, a, cs);
+  return head_dim == 128 ? launch_rope<F16, 128>(wide, grid, s, p, a, cs)
+                         : launch_rope<F16, 64>(wide, grid, s, p, a, cs);
 }
 
 int kvr_shift_cache_layers(const void* const* k_old, const void* const* v_old, void* const* k_new,

@@ -96,7 +96,8 @@ KVR_API int kvr_copy_layers(const void* const* src, void* const* dst, int num_te
  *   dst[l][h, r, :] = src[l][h, r, :] * cos + rotate_half(src[l][h, r, :]) * sin
  * with cos/sin = cos_sin[0:D], cos_sin[D:2D] (one angle set: every row moves
  * by the same shift), each product and the sum rounded to the element type the
- * way torch's bf16/fp16 elementwise ops round them. src == dst is allowed.
+ * way torch's bf16/fp16 elementwise ops round them. src == dst is allowed;
+ * otherwise a layer's src and dst must not overlap.
  * Replaces shifted_suffix_keys (cache.py:47-77) called per layer by
  * build_halo_cache (cache.py:129-139).
  */

@@ -58,6 +58,41 @@ def test_rope_shift_in_place_multi_layer(lib):
         assert bits_equal(got.cpu(), exp)
 
 
+@pytest.mark.parametrize("dtype, dim, row_pad, in_place", [(torch.bfloat16, 64, 0, False),
+                                                           (torch.float16, 128, 0, True),
+                                                           (torch.bfloat16, 128, 8, False),
+                                                           (torch.float16, 64, 8, True)])
+def test_rope_shift_head_dims_strides_and_in_place(lib, dtype, dim, row_pad, in_place):
+    """Delta-RoPE over many layers equals torch's op sequence bit for bit
+    (cache.py:47-77) for both head dims, rows padded beyond head_dim (16-byte
+    instead of 32-byte accesses), in place and into new tensors; padding is
+    never written."""
+    torch.manual_seed(20 + dim + row_pad)
+    layers, heads, rows = 6, 8, 1537
+    full = torch.randn(layers, 1, heads, rows, dim + row_pad).to(dtype)
+    cos = (torch.rand(dim) * 2 - 1).to(dtype)
+    sin = (torch.rand(dim) * 2 - 1).to(dtype)
+    src_full = full.to(DEV)
+    src = [src_full[i, ..., :dim] for i in range(layers)]
+    if in_place:
+        dst_full, dst = src_full, src
+    else:
+        dst_full = torch.full_like(src_full, -5.0)
+        dst = [dst_full[i, ..., :dim] for i in range(layers)]
+    L = lib.load()
+    stride = dim + row_pad
+    lib.check(L.kvr_rope_shift_layers(lib.ptr_array(src), lib.ptr_array(dst), layers, heads, rows, dim,
+                                      rows * stride, stride, rows * stride, stride, _rope_table(cos, sin).data_ptr(),
+                                      lib.dtype_code(dtype), lib.stream_handle()), "rope")
+    torch.cuda.synchronize()
+    expected = oracle.apply_rope(full[..., :dim], cos, sin)
+    got = dst_full.cpu()
+    assert bits_equal(got[..., :dim], expected)
+    if row_pad:
+        pad = full[..., dim:] if in_place else torch.full_like(full[..., dim:], -5.0)
+        assert bits_equal(got[..., dim:], pad)
+
+
 @pytest.mark.parametrize("name", [n for n in golden_cases() if "fp32" not in n])
 def test_shift_cache_is_bit_exact_with_reference_fixture(lib, name):
     record = load_golden(name)
