@@ -123,9 +123,10 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 
 // Per-device once: prefer the largest shared-memory split of L1 for `kernel`,
-// so that the SM keeps one configuration across the library's kernels (the
+// so that the SM keeps one configuration across the layer loop's kernels (the
 // projection and attention kernels need it) instead of switching between
-// consecutive launches.
+// consecutive launches. The HBM-streaming cache kernels opt out
+// (launch_pdl_default_carveout).
 template <auto kernel>
 inline void prefer_shared_once() {
   static int done[64] = {0};
