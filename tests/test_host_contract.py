@@ -428,3 +428,22 @@ def test_module_checks_see_hooks_forwards_and_modes_set_after_a_cached_scan():
     base.norm.eval()
     validate._check_modules(model, base, cpu, torch.bfloat16)
     assert validate._scans[model] is scan
+
+
+@pytest.mark.parametrize("shape, contiguous", [((3, 1, 2, 4, 8), True), ((4, 2, 2, 4, 8), True),
+                                               ((4, 1, 2, 4, 8), False), ((2, 2, 4, 8), True)])
+def test_refresh_rejects_malformed_output_arenas(shape, contiguous):
+    """An output block passed as one tensor must be a contiguous
+    [2L, 1, heads, rows, head_dim] arena (K of layer l at 2l, V at 2l + 1):
+    anything else raises ValueError before any device work."""
+    from budgeted_kv_cache_repair_b200 import _lib
+    from budgeted_kv_cache_repair_b200.engine import refresh_rows
+
+    arena = torch.empty(shape, dtype=torch.bfloat16)
+    if not contiguous:
+        arena = torch.empty(shape[:-1] + (2 * shape[-1],), dtype=torch.bfloat16)[..., : shape[-1]]
+    ids = torch.empty(6, dtype=torch.int64, device="meta")
+    launches = _lib.load().kvr_kernel_launches()
+    with pytest.raises(ValueError, match="arena"):
+        refresh_rows(None, arena, ids, [1, 2], 2, shape[-2])
+    assert _lib.load().kvr_kernel_launches() == launches
