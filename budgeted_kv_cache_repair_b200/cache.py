@@ -113,14 +113,16 @@ def uniform_layout(pairs, what: str):
     _check_kv_layout([first], what)
     shape, stride, dtype, device = first.shape, first.stride(), first.dtype, first.device
     tensors = [t for pair in pairs for t in pair]
-    try:  # one pass per property over all tensors; any non-tensor takes the loop below
-        uniform = (set(map(type, tensors)) == {type(first)} and set(map(torch.Tensor.size, tensors)) == {shape}
-                   and set(map(torch.Tensor.stride, tensors)) == {stride}
-                   and set(map(_dtype_of, tensors)) == {dtype} and set(map(_device_of, tensors)) == {device})
-        aligned = uniform and not any(map(operator.mod, map(torch.Tensor.data_ptr, tensors), repeat(16)))
+    # One C-level pass per property over all tensors; a mismatch, a
+    # misaligned row or a non-tensor takes the loop below, which names it.
+    try:
+        fast = (set(map(type, tensors)) == {type(first)} and set(map(torch.Tensor.size, tensors)) == {shape}
+                and set(map(torch.Tensor.stride, tensors)) == {stride}
+                and set(map(_dtype_of, tensors)) == {dtype} and set(map(_device_of, tensors)) == {device}
+                and not any(map(operator.mod, map(torch.Tensor.data_ptr, tensors), repeat(16))))
     except (TypeError, AttributeError):
-        uniform = aligned = False
-    if not aligned:
+        fast = False
+    if not fast:
         for t in tensors:
             if t.shape != shape or t.stride() != stride or t.dtype != dtype or t.device != device:
                 raise ValueError(f"{what}: every layer must share one shape, stride pair, dtype and device")

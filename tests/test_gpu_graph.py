@@ -270,3 +270,31 @@ def test_in_place_refresh_of_repair_after_deletion_replays(monkeypatch):
         got_positions, got = call()
         assert got_positions == positions and _same(got, expect)
     assert _counters()[0] - replays0 >= 2
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_weights_changed_in_place_between_replays(name, monkeypatch):
+    """Weights modified in place after a request's graph was captured are
+    used by the next call: q/k/v (whose fused copy the engine owns and
+    rebuilds when their version counters move) and o/MLP weights (read
+    through their own storage). The result equals a direct run with the new
+    weights and differs from the old one."""
+    from budgeted_kv_cache_repair_b200 import packed_interval_repair
+
+    record, shim, base = _setup(name)
+    ids = record["new_ids"].to(DEV)
+    for _ in range(3):  # direct, captured, replayed
+        out, _ = packed_interval_repair(shim, base, ids, record["intervals"])
+        before = layers_cpu(out)
+        del out
+    first, last = shim.generator.model.layers[0], shim.generator.model.layers[-1]
+    with torch.no_grad():  # o and down of layer 0 reach every later layer's K/V
+        last.self_attn.k_proj.weight.mul_(1.5)
+        first.self_attn.o_proj.weight.mul_(0.5)
+        first.mlp.down_proj.weight.mul_(2.0)
+    out, _ = packed_interval_repair(shim, base, ids, record["intervals"])
+    after = layers_cpu(out)
+    del out
+    expect = _direct(monkeypatch, shim, base, ids, record["intervals"])
+    assert _same(after, expect)
+    assert not _same(after, before)
