@@ -6,6 +6,7 @@ import os
 import re
 from dataclasses import FrozenInstanceError
 
+import numpy as np
 import pytest
 import torch
 
@@ -447,3 +448,31 @@ def test_refresh_rejects_malformed_output_arenas(shape, contiguous):
     with pytest.raises(ValueError, match="arena"):
         refresh_rows(None, arena, ids, [1, 2], 2, shape[-2])
     assert _lib.load().kvr_kernel_launches() == launches
+
+
+@pytest.mark.parametrize("intervals, ok", [
+    ([(1, 3), (5, 9)], True),
+    ([[1, 3], [5, 9]], True),
+    ([(np.int64(1), np.int64(3)), (5, np.int32(9))], True),
+    ([(True, 3)], False),
+    ([(1, False)], False),
+    ([(1.0, 3)], False),
+    ([(1, 3), (3, 5)], False),
+    ([(2, 2)], False),
+])
+def test_interval_bound_types_follow_the_reference(intervals, ok):
+    """Plain-int bounds take a fast path; NumPy integers, booleans and floats
+    take the general one. Either way the verdict, the returned bounds and their
+    Python int type are the reference's (kernels/executor.py:50-70)."""
+    from budgeted_kv_cache_repair_b200.validate import validate_intervals
+    from oracle import packed_oracle as oracle
+
+    if ok:
+        ours = validate_intervals(intervals, 16)
+        assert [list(x) for x in ours] == [list(x) for x in oracle.validate_intervals(intervals, 16)]
+        assert all(type(v) is int for pair in ours for v in pair)
+    else:
+        with pytest.raises(ValueError):
+            oracle.validate_intervals(intervals, 16)
+        with pytest.raises(ValueError):
+            validate_intervals(intervals, 16)
