@@ -476,3 +476,31 @@ def test_interval_bound_types_follow_the_reference(intervals, ok):
             oracle.validate_intervals(intervals, 16)
         with pytest.raises(ValueError):
             validate_intervals(intervals, 16)
+
+
+def test_native_weight_struct_follows_storage_and_qkv_versions():
+    """The weight struct handed to the native refresh is rebuilt exactly when
+    a weight's storage moved (`.data` reassigned, the same parameter object)
+    or q/k/v changed in place (their stacked copy is the engine's); other
+    in-place changes keep it, since the kernels read those weights through
+    their own storage."""
+    from budgeted_kv_cache_repair_b200.engine import _native_model, model_view
+
+    model = _view_model()
+    view = model_view(model.model)
+    first = _native_model(view)
+    assert _native_model(view) is first
+    layer = model.model.layers[1]
+    with torch.no_grad():
+        layer.mlp.up_proj.weight.mul_(2.0)  # in place, not q/k/v: same struct
+    assert _native_model(view) is first
+    with torch.no_grad():
+        layer.self_attn.v_proj.weight.add_(1.0)  # q/k/v in place: a new stacked copy
+    second = _native_model(view)
+    assert second is not first
+    stacked = view.layers[1].qkv
+    assert torch.equal(stacked[-layer.self_attn.v_proj.weight.shape[0]:], layer.self_attn.v_proj.weight)
+    layer.mlp.gate_proj.weight.data = layer.mlp.gate_proj.weight.data.clone()  # storage moved, no registration
+    third = _native_model(view)
+    assert third is not second
+    assert third.layers[1].gate == layer.mlp.gate_proj.weight.data_ptr()
