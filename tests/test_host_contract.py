@@ -504,3 +504,21 @@ def test_native_weight_struct_follows_storage_and_qkv_versions():
     third = _native_model(view)
     assert third is not second
     assert third.layers[1].gate == layer.mlp.gate_proj.weight.data_ptr()
+
+
+def test_arena_layers_are_views_in_layer_order():
+    """allocate_arena's block holds K of layer l at 2l and V at 2l + 1; the
+    pairs arena_layers returns are [1, heads, rows, dim] views of it, each
+    contiguous, sharing the block's storage."""
+    from budgeted_kv_cache_repair_b200.cache import allocate_arena, arena_layers
+
+    arena = allocate_arena(3, 2, 5, 8, torch.bfloat16, torch.device("cpu"))
+    assert arena.shape == (6, 1, 2, 5, 8) and arena.is_contiguous()
+    pairs = arena_layers(arena)
+    assert len(pairs) == 3
+    plane = 2 * 5 * 8 * arena.element_size()
+    for l, (k, v) in enumerate(pairs):
+        assert k.shape == v.shape == (1, 2, 5, 8) and k.is_contiguous() and v.is_contiguous()
+        assert k.data_ptr() == arena.data_ptr() + 2 * l * plane
+        assert v.data_ptr() == arena.data_ptr() + (2 * l + 1) * plane
+        assert k.untyped_storage().data_ptr() == arena.untyped_storage().data_ptr()
